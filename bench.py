@@ -1,0 +1,387 @@
+"""Benchmark of the particle hot path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload sharded16m|dambreak1m|blobs4m|ref65k]
+
+A step is one manifest SPH step of the workload (grid rebuild: cell hash +
+stable radix sort + cell table; density; pressure+viscosity; gravity,
+integrate, box) on synthetic seeded inputs resident in HBM. The default
+workload is cfg3 (16,384,000 particles, 160^3 cells), the config the metric
+quotes at 1/2/4/8 GPUs; at N=1 the line also carries the 1M dam-break step
+rate and the 2^28-pair radix sort rate under "extra".
+
+--impl reference times the reference algorithm's CPU implementation (the
+oracle port; the Rust reference cannot be built here) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "forge-gpu_b200"))
+
+import numpy as np  # noqa: E402
+
+import workloads  # noqa: E402
+
+# DRAM bytes (read + write) per force+epilogue launch per particle, from the
+# ncu capture summarised in profiles/ (None until captured).
+FORCE_TRAFFIC_B_PER_PARTICLE = None
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+# Algorithmic HBM bytes per particle per phase (compulsory traffic; perfect
+# neighbour reuse). P = radix passes, C/N = cells per particle.
+def alg_bytes(cfg):
+    P = (cfg.key_bits + 7) // 8
+    cn = (cfg.cells + 1) / cfg.n
+    return {
+        # hash+histogram: read pos, write key; pass 0: read key, write key+idx;
+        # passes 1..P-1: read and write key+idx
+        "sort": 12 + 4 + 4 + 8 + 16 * (P - 1),
+        # read sorted key + idx, gather pos + vel, write pos4 + vel4 + cell_start
+        "cells_gather": 4 + 4 + 12 + 12 + 32 + 4 * cn,
+        "density": 16 + 4 + 4 + 4,  # pos4 read, idx read, rho to vel4.w + density_out
+        "force": 16 + 16 + 4 + 24,  # pos4, vel4, idx read; pos, vel write
+    }
+
+
+class Clocks:
+    """Samples nvidia-smi clocks / throttle reasons during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), "--query-gpu=" + self.Q,
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 8:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for nm, val in zip(names, f[4:8]):
+                if val.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+PHASES = ("sort", "cells_gather", "density", "force")
+
+
+def kernels_per_step(cfg):
+    return 1 + (cfg.key_bits + 7) // 8 + 3  # histogram, passes, cell table, density, force
+
+
+def sph_params(forge_sph, cfg):
+    return forge_sph.SphParams(cfg.h, cfg.mass, cfg.gas_constant, cfg.rest_density, cfg.viscosity)
+
+
+def step_params(forge_sph, cfg):
+    sp = forge_sph.StepParams()
+    sp.dt = cfg.dt
+    sp.gravity[:] = list(cfg.gravity)
+    sp.box_min[:] = list(cfg.box_min)
+    sp.box_max[:] = list(cfg.box_max)
+    sp.restitution = cfg.restitution
+    sp.flags = 7
+    return sp
+
+
+class SphRun:
+    """Device-resident state + the step call (forge_sph_step through the C ABI)."""
+
+    def __init__(self, torch, forge_sph, cfg, pos, vel):
+        self.t, self.f, self.cfg = torch, forge_sph, cfg
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self.p = [torch.from_numpy(x).to(dev) for x in pos]
+        self.v = [torch.from_numpy(x).to(dev) for x in vel]
+        self.rho = torch.empty(cfg.n, dtype=torch.float32, device=dev)
+        self.grid = forge_sph.HashGrid(cfg.cell_size, cfg.dims, (0, 0, 0), cfg.n, dev.index)
+        self.sp = sph_params(forge_sph, cfg)
+        self.stp = step_params(forge_sph, cfg)
+        self.args = [x.data_ptr() for x in self.p] + [x.data_ptr() for x in self.v] + [self.rho.data_ptr()]
+        self.L = forge_sph.lib()
+
+    def step(self):
+        st = self.t.cuda.current_stream().cuda_stream
+        rc = self.L.forge_sph_step(self.grid.handle, ctypes.byref(self.sp), ctypes.byref(self.stp), *self.args,
+                                   self.cfg.n, st)
+        self.f.check(rc)
+
+
+def time_steps(torch, fn, steps):
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    s.record()
+    for _ in range(steps):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e)
+
+
+def max_over_ranks(torch, dist, v):
+    if dist is None:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def run_sph_single(torch, forge_sph, cfg, steps, warmup, rank_dev, clocks=True):
+    pos, vel = workloads.particles(cfg)
+    run = SphRun(torch, forge_sph, cfg, pos, vel)
+    for _ in range(warmup):
+        run.step()
+    run.grid.check()
+    L = forge_sph.lib()
+    forge_sph.check(L.forge_grid_profile_enable(run.grid.handle, steps))
+    ck = Clocks(rank_dev)
+    if clocks:
+        ck.start()
+        time.sleep(0.3)
+    ms = time_steps(torch, run.step, steps)
+    clk = ck.stop() if clocks else None
+    run.grid.check()
+    buf = (ctypes.c_float * (4 * steps))()
+    got = ctypes.c_uint32(0)
+    forge_sph.check(L.forge_grid_profile_read(run.grid.handle, buf, steps, ctypes.byref(got)))
+    ph = np.array(buf[:4 * got.value], np.float64).reshape(-1, 4)
+    forge_sph.check(L.forge_grid_profile_enable(run.grid.handle, 0))
+    phase_ms = {k: float(ph[:, i].mean()) for i, k in enumerate(PHASES)}
+    return run, ms, phase_ms, clk, pos, vel
+
+
+def e2e_sph(torch, forge_sph, cfg, pos, vel, steps, warmup):
+    """Same step through the public API with HOST buffers: every step copies the
+    particle state from pinned host memory to the device, steps, and reads the
+    new state back (pos, vel: 24 B/particle each way)."""
+    run = SphRun(torch, forge_sph, cfg, pos, vel)
+    hp = [torch.from_numpy(x.copy()).pin_memory() for x in pos + vel]
+    dv = run.p + run.v
+
+    def one():
+        for d, h in zip(dv, hp):
+            d.copy_(h, non_blocking=True)
+        run.step()
+        for d, h in zip(dv, hp):
+            h.copy_(d, non_blocking=True)
+
+    for _ in range(warmup):
+        one()
+    ms = time_steps(torch, one, steps)
+    nbytes = sum(x.numel() * 4 for x in hp)
+    return ms / steps, nbytes
+
+
+def sort_rate(torch, forge_sph, kind, n, steps=5, warmup=3):
+    keys_np = workloads.sort_keys(kind, n)
+    k0 = torch.from_numpy(keys_np.view(np.int32)).cuda()
+    keys, vals = k0.clone(), torch.arange(n, dtype=torch.int32, device="cuda")
+    s = forge_sph.RadixSorter(n, torch.cuda.current_device())
+    bits = 32 if kind == "uniform" else 30
+
+    def one():
+        s.sort_pairs(keys, vals, n, 0, bits)
+
+    for _ in range(warmup):
+        keys.copy_(k0)
+        one()
+    s.check()
+    total = 0.0
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    for _ in range(steps):
+        keys.copy_(k0)  # 1 GiB rewrite between sorts also evicts L2
+        ev[0].record()
+        one()
+        ev[1].record()
+        torch.cuda.synchronize()
+        total += ev[0].elapsed_time(ev[1])
+    s.check()
+    t = total / steps / 1e3
+    passes = (bits + 7) // 8
+    gbs = (4 + 16 * passes) * n / t / 1e9  # histogram reads keys; each pass reads+writes key+value
+    return {"gkeys_per_s": n / t / 1e9, "ms": t * 1e3, "passes": passes, "achieved_gbs": gbs}
+
+
+def cpu_sample(cfg, max_particles):
+    """Bounded CPU sample of a workload: the first max_particles particles in
+    original order (for the lattice configs a bottom slab of the same domain)."""
+    pos, vel = workloads.particles(cfg)
+    m = min(cfg.n, max_particles)
+    return [np.ascontiguousarray(x[:m]) for x in pos], [np.ascontiguousarray(x[:m]) for x in vel], m
+
+
+def cpu_steps(cfg, pos, vel, steps, threads):
+    """Reference algorithm on the host: the oracle port of the manifest step."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    p = oracle.SphParams(cfg.h, cfg.mass, cfg.gas_constant, cfg.rest_density, cfg.viscosity)
+    sp = oracle.StepParams(cfg.dt, cfg.gravity, cfg.box_min, cfg.box_max, cfg.restitution, 7)
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        oracle.step(p, sp, pos, vel, cfg.cell_size, cfg.dims, threads=threads)
+        times.append(time.perf_counter() - t0)
+    return times
+
+
+def cpu_threads():
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    return oracle.max_threads()
+
+
+CPU_SAMPLE = {"sharded16m": 1_024_000, "dambreak1m": 131_072, "blobs4m": 262_144, "ref65k": 65_536}
+
+
+def reference_arm(args, rank, world):
+    if rank != 0:
+        return
+    cfg = workloads.config(args.workload)
+    m = CPU_SAMPLE.get(args.workload, 262_144)
+    pos, vel, m = cpu_sample(cfg, m)
+    th = cpu_threads()
+    cpu_steps(cfg, pos, vel, args.warmup, th)
+    times = cpu_steps(cfg, pos, vel, args.steps, th)
+    t = sum(times) / len(times)
+    val = m / t
+    sample = f"first {m} of {cfg.n} particles ({cfg.name}), oracle port of the manifest step, {th} OpenMP threads"
+    line = {"metric": "SPH particle-steps/s", "value": val, "unit": "particle-steps/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": cfg.name, "particles": cfg.n, "cells": cfg.cells, "h": cfg.h},
+            "cpu_baseline": {"value": val, "unit": "particle-steps/s", "cores": th, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": val, "unit": "particle-steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="sharded16m",
+                    choices=["sharded16m", "dambreak1m", "dambreak65k", "blobs4m", "ref65k"])
+    ap.add_argument("--no-extra", action="store_true", help="skip the 1M dam-break and 2^28 sort extras")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        reference_arm(args, rank, world)
+        return
+
+    import torch
+    import forge_sph
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+        import slab_bench
+        slab_bench.run(args, torch, dist, rank, world, local)
+        dist.destroy_process_group()
+        return
+
+    cfg = workloads.config(args.workload)
+    hbm, peak_kind = peaks()
+    run, ms, phase_ms, clk, pos, vel = run_sph_single(torch, forge_sph, cfg, args.steps, args.warmup, local)
+    ms_step = ms / args.steps
+    value = cfg.n / (ms_step / 1e3)
+    ab = alg_bytes(cfg)
+    dom = max(PHASES, key=lambda k: phase_ms[k])
+    achieved = ab[dom] * cfg.n / (phase_ms[dom] / 1e3) / 1e9
+    traffic = None
+    if dom == "force" and FORCE_TRAFFIC_B_PER_PARTICLE is not None:
+        traffic = FORCE_TRAFFIC_B_PER_PARTICLE * cfg.n
+    phases = {k: {"ms": phase_ms[k], "alg_bytes_per_particle": ab[k],
+                  "achieved_gbs": ab[k] * cfg.n / (phase_ms[k] / 1e3) / 1e9,
+                  "frac_of_hbm": ab[k] * cfg.n / (phase_ms[k] / 1e3) / 1e9 / hbm} for k in PHASES}
+    del run
+    torch.cuda.empty_cache()
+    e2e_ms, e2e_bytes = e2e_sph(torch, forge_sph, cfg, pos, vel, max(3, args.steps // 2), 3)
+
+    line = {"metric": "SPH particle-steps/s", "value": value, "unit": "particle-steps/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": cfg.name, "particles": cfg.n, "cells": cfg.cells, "h": cfg.h,
+                       "key_bits": cfg.key_bits, "inputs_exceed_l2": cfg.n * 24 > 126e6,
+                       "parallelism": "single GPU"},
+            "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                         "frac": achieved / hbm, "traffic": traffic, "peak_kind": peak_kind},
+            "phases": phases,
+            "e2e": {"value": cfg.n / (e2e_ms / 1e3), "unit": "particle-steps/s",
+                    "h2d_bytes_per_step": e2e_bytes, "d2h_bytes_per_step": e2e_bytes},
+            "gpu_launches": kernels_per_step(cfg) * args.steps,
+            "clocks": clk}
+    if not args.no_cpu:
+        m = CPU_SAMPLE.get(cfg.name, 262_144)
+        cp, cv, m = cpu_sample(cfg, m)
+        th = cpu_threads()
+        times = cpu_steps(cfg, cp, cv, 2, th)
+        t = min(times)
+        line["cpu_baseline"] = {"value": m / t, "unit": "particle-steps/s", "cores": th, "kind": "port",
+                                "sample": f"first {m} of {cfg.n} particles, 2 oracle steps, best of 2"}
+    if not args.no_extra and cfg.name != "dambreak1m":
+        extra = {}
+        c1 = workloads.config("dambreak1m")
+        r1, ms1, ph1, _, _, _ = run_sph_single(torch, forge_sph, c1, 50, 5, local, clocks=False)
+        del r1
+        extra["dambreak1m"] = {"value": c1.n / (ms1 / 50 / 1e3), "unit": "particle-steps/s",
+                               "ms_per_step": ms1 / 50, "phases_ms": ph1}
+        torch.cuda.empty_cache()
+        for kind in ("uniform", "morton"):
+            extra["radix_sort_2^28_" + kind] = sort_rate(torch, forge_sph, kind, 1 << 28)
+            extra["radix_sort_2^28_" + kind]["frac_of_hbm"] = extra["radix_sort_2^28_" + kind]["achieved_gbs"] / hbm
+            torch.cuda.empty_cache()
+        line["extra"] = extra
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,662 @@
+// C ABI of the particle hot path: handles, launch plumbing and error
+// reporting around the sm_100a kernels in radix_sort.cuh, grid.cuh, sph.cuh.
+// Single translation unit -> libforge_sph.so.
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "forge_sph.h"
+#include "common.cuh"
+#include "grid.cuh"
+#include "radix_sort.cuh"
+#include "sph.cuh"
+
+using namespace forge;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int set_error(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+#define FORGE_CUDA(call)                                                                              \
+    do {                                                                                              \
+        cudaError_t e_ = (call);                                                                      \
+        if (e_ != cudaSuccess)                                                                        \
+            return set_error(FORGE_ERR_CUDA, "%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_), \
+                             __FILE__, __LINE__);                                                     \
+    } while (0)
+
+#define FORGE_LAUNCHED()                                                                              \
+    do {                                                                                              \
+        cudaError_t e_ = cudaGetLastError();                                                          \
+        if (e_ != cudaSuccess)                                                                        \
+            return set_error(FORGE_ERR_CUDA, "kernel launch failed: %s (%s:%d)", cudaGetErrorString(e_), \
+                             __FILE__, __LINE__);                                                     \
+    } while (0)
+
+// Makes `dev` current for the scope of one API call and restores the caller's.
+struct DeviceScope {
+    int prev = -1;
+    int dev;
+    cudaError_t status = cudaSuccess;
+    explicit DeviceScope(int d) : dev(d) {
+        status = cudaGetDevice(&prev);
+        if (status == cudaSuccess && prev != dev) status = cudaSetDevice(dev);
+    }
+    ~DeviceScope() {
+        if (prev >= 0 && prev != dev) cudaSetDevice(prev);
+    }
+};
+
+#define FORGE_DEVICE_SCOPE(d)                                                                         \
+    DeviceScope scope_(d);                                                                            \
+    if (scope_.status != cudaSuccess)                                                                 \
+        return set_error(FORGE_ERR_CUDA, "cannot select device %d: %s", (d), cudaGetErrorString(scope_.status))
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+template <class T>
+cudaError_t dalloc(T** p, size_t count) {
+    return cudaMalloc(reinterpret_cast<void**>(p), count * sizeof(T) + 16);
+}
+
+uint32_t grid_blocks(uint64_t work, uint32_t threads) { return (uint32_t)((work + threads - 1) / threads); }
+
+int num_sms(int device) {
+    int v = 148;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device);
+    return v;
+}
+
+// Radix-sort scratch shared by the standalone sorter and the grid build:
+// meta = [kMaxPasses x 256 digit histograms][kMaxPasses tile counters][status word].
+constexpr size_t kMetaHist = radix::kMaxPasses * radix::kRadix;
+constexpr size_t kMetaCounters = kMetaHist;
+constexpr size_t kMetaErr = kMetaHist + radix::kMaxPasses;
+constexpr size_t kMetaWords = kMetaErr + 1;
+
+struct SortScratch {
+    uint32_t* meta = nullptr;    // kMetaWords
+    uint32_t* status = nullptr;  // tiles * 256 (+pad to uint4)
+    uint32_t max_tiles = 0;
+    int sms = 148;
+};
+
+int scratch_alloc(SortScratch& s, uint64_t max_n, int device) {
+    s.max_tiles = radix::num_tiles(max_n > 0 ? max_n : 1);
+    FORGE_CUDA(dalloc(&s.meta, kMetaWords));
+    FORGE_CUDA(cudaMemset(s.meta, 0, kMetaWords * sizeof(uint32_t)));
+    FORGE_CUDA(dalloc(&s.status, (size_t)s.max_tiles * radix::kRadix));
+    s.sms = num_sms(device);
+    return FORGE_OK;
+}
+
+void scratch_free(SortScratch& s) {
+    cudaFree(s.meta);
+    cudaFree(s.status);
+    s.meta = nullptr;
+    s.status = nullptr;
+}
+
+// Runs histogram + passes. The histogram kernel reads keys through `src`.
+// Pass 0 reads keys0 (vals0, or iota if vals0 == nullptr) and writes
+// (ka, va); later passes ping-pong between (ka, va) and (kb, vb).
+// Returns 0 if the result is in (ka, va), 1 if in (kb, vb).
+template <class Src>
+int run_onesweep(const SortScratch& s, Src src, const uint32_t* keys0, const uint32_t* vals0, uint32_t* ka,
+                 uint32_t* va, uint32_t* kb, uint32_t* vb, uint32_t n, uint32_t begin_bit, uint32_t end_bit,
+                 cudaStream_t st, int* where) {
+    const uint32_t passes = (end_bit - begin_bit + radix::kRadixBits - 1) / radix::kRadixBits;
+    const uint32_t tiles = radix::num_tiles(n);
+    FORGE_CUDA(cudaMemsetAsync(s.meta, 0, kMetaErr * sizeof(uint32_t), st));
+    const uint32_t status_vec4 = (uint32_t)(((size_t)tiles * radix::kRadix + 3) / 4);
+    const uint32_t hblocks =
+        std::max(1u, std::min(grid_blocks(n, radix::kHistThreads), (uint32_t)s.sms * 8u));
+    radix::digit_histogram_kernel<Src><<<hblocks, radix::kHistThreads, 0, st>>>(
+        src, n, begin_bit, end_bit, passes, s.meta, reinterpret_cast<uint4*>(s.status), status_vec4);
+    FORGE_LAUNCHED();
+    const uint32_t* kin = keys0;
+    const uint32_t* vin = vals0;
+    int cur = -1;
+    for (uint32_t p = 0; p < passes; ++p) {
+        uint32_t* kout = (p % 2 == 0) ? ka : kb;
+        uint32_t* vout = (p % 2 == 0) ? va : vb;
+        const uint32_t shift = begin_bit + p * radix::kRadixBits;
+        const uint32_t bits = std::min((uint32_t)radix::kRadixBits, end_bit - shift);
+        if (p == 0 && vin == nullptr) {
+            radix::onesweep_pass_kernel<true><<<tiles, radix::kThreads, 0, st>>>(
+                kin, nullptr, kout, vout, n, shift, bits, s.meta + p * radix::kRadix, s.status,
+                s.meta + kMetaCounters + p, p & 1u, s.meta + kMetaErr);
+        } else {
+            radix::onesweep_pass_kernel<false><<<tiles, radix::kThreads, 0, st>>>(
+                kin, vin, kout, vout, n, shift, bits, s.meta + p * radix::kRadix, s.status,
+                s.meta + kMetaCounters + p, p & 1u, s.meta + kMetaErr);
+        }
+        FORGE_LAUNCHED();
+        kin = kout;
+        vin = vout;
+        cur = (int)(p % 2);
+    }
+    *where = cur;
+    return FORGE_OK;
+}
+
+int check_status_word(uint32_t* word, cudaStream_t st, const char* what) {
+    FORGE_CUDA(cudaStreamSynchronize(st));
+    uint32_t v = 0;
+    FORGE_CUDA(cudaMemcpy(&v, word, sizeof v, cudaMemcpyDeviceToHost));
+    if (v == 0) return FORGE_OK;
+    FORGE_CUDA(cudaMemset(word, 0, sizeof v));
+    if (v & kDevTimeout) return set_error(FORGE_ERR_TIMEOUT, "%s: a look-back wait on the device gave up", what);
+    if (v & kDevCapacity) return set_error(FORGE_ERR_CAPACITY, "%s: output capacity exceeded on the device", what);
+    if (v & kDevKeyRange) return set_error(FORGE_ERR_DEVICE, "%s: device-side range check failed", what);
+    return set_error(FORGE_ERR_DEVICE, "%s: device status 0x%x", what, v);
+}
+
+}  // namespace
+
+// ===========================================================================
+// Errors / version
+// ===========================================================================
+extern "C" uint64_t forge_last_error(char* buf, uint64_t len) {
+    const std::string& m = g_last_error;
+    if (buf && len) {
+        const size_t c = std::min<size_t>(m.size(), len - 1);
+        memcpy(buf, m.data(), c);
+        buf[c] = 0;
+    }
+    return m.size();
+}
+
+extern "C" int forge_abi_version(void) { return FORGE_SPH_ABI_VERSION; }
+
+// ===========================================================================
+// Standalone sorter
+// ===========================================================================
+struct forge_sorter {
+    int device = 0;
+    uint64_t max_n = 0;
+    uint32_t* keys_alt = nullptr;
+    uint32_t* vals_alt = nullptr;
+    SortScratch scratch;
+};
+
+extern "C" int forge_sorter_create(uint64_t max_n, int device, forge_sorter** out) {
+    if (!out) return set_error(FORGE_ERR_INVALID_ARG, "forge_sorter_create: out is NULL");
+    *out = nullptr;
+    if (max_n > radix::kMaxN)
+        return set_error(FORGE_ERR_INVALID_ARG, "forge_sorter_create: max_n=%llu exceeds %llu",
+                         (unsigned long long)max_n, (unsigned long long)radix::kMaxN);
+    FORGE_DEVICE_SCOPE(device);
+    forge_sorter* s = new forge_sorter;
+    s->device = device;
+    s->max_n = max_n;
+    int rc = FORGE_OK;
+    if (cudaMalloc(&s->keys_alt, (max_n ? max_n : 1) * 4) != cudaSuccess ||
+        cudaMalloc(&s->vals_alt, (max_n ? max_n : 1) * 4) != cudaSuccess) {
+        rc = set_error(FORGE_ERR_CUDA, "forge_sorter_create: cudaMalloc of %llu pairs failed",
+                       (unsigned long long)max_n);
+    } else {
+        rc = scratch_alloc(s->scratch, max_n, device);
+    }
+    if (rc != FORGE_OK) {
+        cudaFree(s->keys_alt);
+        cudaFree(s->vals_alt);
+        scratch_free(s->scratch);
+        delete s;
+        return rc;
+    }
+    *out = s;
+    return FORGE_OK;
+}
+
+extern "C" int forge_sorter_sort_pairs(forge_sorter* s, uint32_t* keys, uint32_t* vals, uint32_t* keys_alt,
+                                       uint32_t* vals_alt, uint64_t n, uint32_t begin_bit, uint32_t end_bit,
+                                       int* result_in_alt, void* stream) {
+    if (result_in_alt) *result_in_alt = 0;
+    if (!s) return set_error(FORGE_ERR_INVALID_ARG, "forge_sorter_sort_pairs: sorter is NULL");
+    if (n > s->max_n)
+        return set_error(FORGE_ERR_CAPACITY, "forge_sorter_sort_pairs: n=%llu exceeds max_n=%llu",
+                         (unsigned long long)n, (unsigned long long)s->max_n);
+    if (begin_bit >= end_bit || end_bit > 32 || end_bit - begin_bit > 8 * radix::kMaxPasses)
+        return set_error(FORGE_ERR_INVALID_ARG, "forge_sorter_sort_pairs: bad bit range [%u, %u)", begin_bit,
+                         end_bit);
+    if ((keys_alt == nullptr) != (vals_alt == nullptr))
+        return set_error(FORGE_ERR_INVALID_ARG, "forge_sorter_sort_pairs: pass both alt buffers or neither");
+    if (n == 0) return FORGE_OK;
+    if (!keys || !vals) return set_error(FORGE_ERR_INVALID_ARG, "forge_sorter_sort_pairs: keys/vals NULL");
+    FORGE_DEVICE_SCOPE(s->device);
+    cudaStream_t st = as_stream(stream);
+    const bool own_alt = keys_alt == nullptr;
+    uint32_t* ka = own_alt ? s->keys_alt : keys_alt;
+    uint32_t* va = own_alt ? s->vals_alt : vals_alt;
+    int where = 0;
+    radix::KeysFromArray src{keys};
+    int rc = run_onesweep(s->scratch, src, keys, vals, ka, va, keys, vals, (uint32_t)n, begin_bit, end_bit, st,
+                          &where);
+    if (rc != FORGE_OK) return rc;
+    if (where == 0) {  // result in (ka, va)
+        if (own_alt) {
+            FORGE_CUDA(cudaMemcpyAsync(keys, ka, n * 4, cudaMemcpyDeviceToDevice, st));
+            FORGE_CUDA(cudaMemcpyAsync(vals, va, n * 4, cudaMemcpyDeviceToDevice, st));
+        } else if (result_in_alt) {
+            *result_in_alt = 1;
+        }
+    }
+    return FORGE_OK;
+}
+
+extern "C" int forge_sorter_check(forge_sorter* s, void* stream) {
+    if (!s) return set_error(FORGE_ERR_INVALID_ARG, "forge_sorter_check: sorter is NULL");
+    FORGE_DEVICE_SCOPE(s->device);
+    return check_status_word(s->scratch.meta + kMetaErr, as_stream(stream), "radix sort");
+}
+
+extern "C" void forge_sorter_destroy(forge_sorter* s) {
+    if (!s) return;
+    DeviceScope scope(s->device);
+    cudaFree(s->keys_alt);
+    cudaFree(s->vals_alt);
+    scratch_free(s->scratch);
+    delete s;
+}
+
+extern "C" int forge_cell_bounds(const uint32_t* sorted_ids, uint32_t* start, uint32_t* end, uint64_t n,
+                                 uint64_t num_cells, void* stream) {
+    if (num_cells == 0) return FORGE_OK;
+    if (!start || !end || (n && !sorted_ids))
+        return set_error(FORGE_ERR_INVALID_ARG, "forge_cell_bounds: NULL pointer");
+    if (n >= 0xffffffffull || num_cells >= 0xffffffffull)
+        return set_error(FORGE_ERR_INVALID_ARG, "forge_cell_bounds: sizes must be < 2^32-1");
+    cudaStream_t st = as_stream(stream);
+    grid::cell_bounds_kernel<<<grid_blocks(n + 1, 256), 256, 0, st>>>(sorted_ids, (uint32_t)n, (uint32_t)num_cells,
+                                                                       start, end, nullptr);
+    FORGE_LAUNCHED();
+    return FORGE_OK;
+}
+
+// ===========================================================================
+// Grid
+// ===========================================================================
+struct forge_grid {
+    int device = 0;
+    uint64_t max_n = 0;
+    grid::GridGeom geom{};
+    uint32_t C = 0;
+    uint32_t key_bits = 1;
+    uint32_t* cell_idx = nullptr;  // hash output, original order
+    uint32_t* kb = nullptr;
+    uint32_t* vb = nullptr;
+    uint32_t* kc = nullptr;
+    uint32_t* vc = nullptr;
+    uint32_t* cell_start = nullptr;  // C + 1
+    float4* pos4 = nullptr;          // cell-ordered (x, y, z, key)
+    float4* vel4 = nullptr;          // cell-ordered (vx, vy, vz, rho)
+    uint32_t* scan_sums = nullptr;   // query scan tile sums
+    uint32_t* q_offsets = nullptr;   // max_n + 1
+    SortScratch scratch;
+    // State of the last build.
+    uint32_t* sorted_keys = nullptr;
+    uint32_t* sorted_idx = nullptr;
+    uint64_t n = 0;
+    bool built = false;
+    // Phase-event ring for forge_grid_profile_* (5 events per step).
+    std::vector<cudaEvent_t> prof_events;
+    uint32_t prof_cap = 0, prof_next = 0, prof_count = 0;
+};
+
+namespace {
+void prof_mark(forge_grid* g, int k, cudaStream_t st) {
+    if (g->prof_cap) cudaEventRecord(g->prof_events[(size_t)g->prof_next * 5 + k], st);
+}
+void prof_step_done(forge_grid* g) {
+    if (!g->prof_cap) return;
+    g->prof_next = (g->prof_next + 1) % g->prof_cap;
+    if (g->prof_count < g->prof_cap) ++g->prof_count;
+}
+void prof_free(forge_grid* g) {
+    for (cudaEvent_t e : g->prof_events) cudaEventDestroy(e);
+    g->prof_events.clear();
+    g->prof_cap = g->prof_next = g->prof_count = 0;
+}
+}  // namespace
+
+extern "C" int forge_grid_create(float cell_size, uint32_t nx, uint32_t ny, uint32_t nz, const float* origin,
+                                 uint64_t max_n, int device, forge_grid** out) {
+    if (!out) return set_error(FORGE_ERR_INVALID_ARG, "forge_grid_create: out is NULL");
+    *out = nullptr;
+    if (!(cell_size > 0.f)) return set_error(FORGE_ERR_INVALID_ARG, "forge_grid_create: cell_size must be > 0");
+    const uint64_t C = (uint64_t)nx * ny * nz;
+    if (nx == 0 || ny == 0 || nz == 0 || C >= (1ull << 31))
+        return set_error(FORGE_ERR_INVALID_ARG, "forge_grid_create: grid %ux%ux%u must be non-empty and < 2^31 cells",
+                         nx, ny, nz);
+    if (max_n > radix::kMaxN)
+        return set_error(FORGE_ERR_INVALID_ARG, "forge_grid_create: max_n exceeds %llu",
+                         (unsigned long long)radix::kMaxN);
+    FORGE_DEVICE_SCOPE(device);
+    forge_grid* g = new forge_grid;
+    g->device = device;
+    g->max_n = max_n;
+    g->geom.ox = origin ? origin[0] : 0.f;
+    g->geom.oy = origin ? origin[1] : 0.f;
+    g->geom.oz = origin ? origin[2] : 0.f;
+    g->geom.cs = cell_size;
+    g->geom.nx = (int)nx;
+    g->geom.ny = (int)ny;
+    g->geom.nz = (int)nz;
+    g->C = (uint32_t)C;
+    uint32_t kb = 1;
+    while (kb < 32 && (1ull << kb) < C) ++kb;
+    g->key_bits = kb;
+    const size_t m = max_n ? max_n : 1;
+    int rc = FORGE_OK;
+    bool ok = dalloc(&g->cell_idx, m) == cudaSuccess && dalloc(&g->kb, m) == cudaSuccess &&
+              dalloc(&g->vb, m) == cudaSuccess && dalloc(&g->kc, m) == cudaSuccess &&
+              dalloc(&g->vc, m) == cudaSuccess && dalloc(&g->cell_start, C + 1) == cudaSuccess &&
+              dalloc(&g->pos4, m) == cudaSuccess && dalloc(&g->vel4, m) == cudaSuccess &&
+              dalloc(&g->scan_sums, m / grid::kScanTile + 1) == cudaSuccess &&
+              dalloc(&g->q_offsets, m + 1) == cudaSuccess;
+    if (!ok) rc = set_error(FORGE_ERR_CUDA, "forge_grid_create: cudaMalloc failed (max_n=%llu, cells=%llu)",
+                            (unsigned long long)max_n, (unsigned long long)C);
+    if (rc == FORGE_OK) rc = scratch_alloc(g->scratch, max_n, device);
+    if (rc != FORGE_OK) {
+        forge_grid_destroy(g);
+        return rc;
+    }
+    *out = g;
+    return FORGE_OK;
+}
+
+extern "C" void forge_grid_destroy(forge_grid* g) {
+    if (!g) return;
+    DeviceScope scope(g->device);
+    cudaFree(g->cell_idx);
+    cudaFree(g->kb);
+    cudaFree(g->vb);
+    cudaFree(g->kc);
+    cudaFree(g->vc);
+    cudaFree(g->cell_start);
+    cudaFree(g->pos4);
+    cudaFree(g->vel4);
+    cudaFree(g->scan_sums);
+    cudaFree(g->q_offsets);
+    scratch_free(g->scratch);
+    prof_free(g);
+    delete g;
+}
+
+namespace {
+
+// Hash + sort + cell-start table (+ optional cell-ordered gather).
+int grid_build_impl(forge_grid* g, const float* px, const float* py, const float* pz, uint32_t stride, uint64_t n,
+                    uint32_t* cell_idx_out, bool gather_pos, const float* vx, const float* vy, const float* vz,
+                    cudaStream_t st) {
+    if (n > g->max_n)
+        return set_error(FORGE_ERR_CAPACITY, "grid build: n=%llu exceeds max_n=%llu", (unsigned long long)n,
+                         (unsigned long long)g->max_n);
+    if (n && (!px || !py || !pz)) return set_error(FORGE_ERR_INVALID_ARG, "grid build: NULL positions");
+    uint32_t* keys = cell_idx_out ? cell_idx_out : g->cell_idx;
+    const uint32_t nn = (uint32_t)n;
+    if (n > 0) {
+        grid::HashKeys src{px, py, pz, stride, g->geom, keys};
+        int where = 0;
+        int rc = run_onesweep(g->scratch, src, keys, nullptr, g->kb, g->vb, g->kc, g->vc, nn, 0, g->key_bits, st,
+                              &where);
+        if (rc != FORGE_OK) return rc;
+        g->sorted_keys = where == 0 ? g->kb : g->kc;
+        g->sorted_idx = where == 0 ? g->vb : g->vc;
+    } else {
+        g->sorted_keys = g->kb;
+        g->sorted_idx = g->vb;
+    }
+    prof_mark(g, 1, st);
+    grid::GatherSrc gs{px, py, pz, stride, vx, vy, vz};
+    grid::cell_start_gather_kernel<<<grid_blocks(n + 1, 256), 256, 0, st>>>(
+        g->sorted_keys, g->sorted_idx, nn, g->C, g->cell_start, gs, gather_pos ? g->pos4 : nullptr,
+        (gather_pos && vx) ? g->vel4 : nullptr);
+    FORGE_LAUNCHED();
+    prof_mark(g, 2, st);
+    g->n = n;
+    g->built = true;
+    return FORGE_OK;
+}
+
+int grid_export(forge_grid* g, uint32_t* sorted_idx, uint32_t* cell_start, cudaStream_t st) {
+    if (sorted_idx && g->n)
+        FORGE_CUDA(cudaMemcpyAsync(sorted_idx, g->sorted_idx, g->n * 4, cudaMemcpyDeviceToDevice, st));
+    if (cell_start)
+        FORGE_CUDA(cudaMemcpyAsync(cell_start, g->cell_start, ((size_t)g->C + 1) * 4, cudaMemcpyDeviceToDevice, st));
+    return FORGE_OK;
+}
+
+sph::SphConsts make_consts(const forge_sph_params* p) {
+    // Same float expressions as the reference kernels (sph_density.rs:413-416,
+    // sph_fused.rs:552-555); products/quotients only, so host == device bits.
+    sph::SphConsts c;
+    const float h = p->h;
+    const float h2 = h * h;
+    const float h9 = h2 * h2 * h2 * h2 * h;
+    const float poly6 = 315.0f / (64.0f * 3.14159265f * h9);
+    const float h6 = h2 * h2 * h2;
+    c.h = h;
+    c.h2 = h2;
+    c.mass_poly6 = p->mass * poly6;
+    c.mass = p->mass;
+    c.k = p->gas_constant;
+    c.rho0 = p->rest_density;
+    c.mu = p->viscosity;
+    c.spiky = -45.0f / (3.14159265f * h6);
+    c.visc_lap = 45.0f / (3.14159265f * h6);
+    return c;
+}
+
+sph::Dims dims_of(const forge_grid* g) { return sph::Dims{g->geom.nx, g->geom.ny, g->geom.nz}; }
+
+constexpr uint32_t kSphThreads = 128;
+
+int launch_density(forge_grid* g, const forge_sph_params* p, float* density, cudaStream_t st) {
+    if (g->n == 0) return FORGE_OK;
+    sph::density_kernel<<<grid_blocks(g->n, kSphThreads), kSphThreads, 0, st>>>(
+        g->pos4, g->cell_start, g->sorted_idx, (uint32_t)g->n, dims_of(g), make_consts(p), g->vel4, density);
+    FORGE_LAUNCHED();
+    return FORGE_OK;
+}
+
+template <int TERMS, int EPI>
+void launch_force_t(forge_grid* g, const sph::SphConsts& c, const sph::StepEpi& ep, const sph::ForceOut& o,
+                    cudaStream_t st) {
+    sph::force_kernel<TERMS, EPI><<<grid_blocks(g->n, kSphThreads), kSphThreads, 0, st>>>(
+        g->pos4, g->vel4, g->cell_start, g->sorted_idx, (uint32_t)g->n, dims_of(g), c, ep, o);
+}
+
+}  // namespace
+
+extern "C" int forge_grid_build(forge_grid* g, const float* px, const float* py, const float* pz, uint64_t n,
+                                uint32_t* cell_idx, uint32_t* sorted_idx, uint32_t* cell_start, void* stream) {
+    if (!g) return set_error(FORGE_ERR_INVALID_ARG, "forge_grid_build: grid is NULL");
+    FORGE_DEVICE_SCOPE(g->device);
+    cudaStream_t st = as_stream(stream);
+    int rc = grid_build_impl(g, px, py, pz, 1, n, cell_idx, true, nullptr, nullptr, nullptr, st);
+    if (rc != FORGE_OK) return rc;
+    return grid_export(g, sorted_idx, cell_start, st);
+}
+
+extern "C" int forge_grid_build_aos(forge_grid* g, const float* xyz, uint64_t n, uint32_t* cell_idx,
+                                    uint32_t* sorted_idx, uint32_t* cell_start, void* stream) {
+    if (!g) return set_error(FORGE_ERR_INVALID_ARG, "forge_grid_build_aos: grid is NULL");
+    if (n && !xyz) return set_error(FORGE_ERR_INVALID_ARG, "forge_grid_build_aos: xyz is NULL");
+    FORGE_DEVICE_SCOPE(g->device);
+    cudaStream_t st = as_stream(stream);
+    int rc = grid_build_impl(g, xyz, xyz ? xyz + 1 : nullptr, xyz ? xyz + 2 : nullptr, 3, n, cell_idx, true, nullptr,
+                             nullptr, nullptr, st);
+    if (rc != FORGE_OK) return rc;
+    return grid_export(g, sorted_idx, cell_start, st);
+}
+
+extern "C" int forge_grid_query(forge_grid* g, const float* px, const float* py, const float* pz, const float* qx,
+                                const float* qy, const float* qz, uint64_t nq, float radius, uint32_t* counts,
+                                uint32_t* offsets, uint32_t* hits, uint64_t max_hits, void* stream) {
+    if (!g) return set_error(FORGE_ERR_INVALID_ARG, "forge_grid_query: grid is NULL");
+    if (!g->built) return set_error(FORGE_ERR_INVALID_ARG, "forge_grid_query: grid has not been built");
+    if (nq > g->max_n)
+        return set_error(FORGE_ERR_CAPACITY, "forge_grid_query: nq=%llu exceeds max_n=%llu",
+                         (unsigned long long)nq, (unsigned long long)g->max_n);
+    if (!counts) return set_error(FORGE_ERR_INVALID_ARG, "forge_grid_query: counts is NULL");
+    if (nq && (!qx || !qy || !qz)) return set_error(FORGE_ERR_INVALID_ARG, "forge_grid_query: NULL queries");
+    if (g->n && (!px || !py || !pz)) return set_error(FORGE_ERR_INVALID_ARG, "forge_grid_query: NULL positions");
+    FORGE_DEVICE_SCOPE(g->device);
+    cudaStream_t st = as_stream(stream);
+    uint32_t* offs = offsets ? offsets : g->q_offsets;
+    if (nq == 0) {
+        FORGE_CUDA(cudaMemsetAsync(offs, 0, 4, st));
+        return FORGE_OK;
+    }
+    const float r2 = radius * radius;
+    uint32_t* err = g->scratch.meta + kMetaErr;
+    const uint32_t nb = grid_blocks(nq, 128);
+    grid::query_kernel<false><<<nb, 128, 0, st>>>(px, py, pz, qx, qy, qz, (uint32_t)nq, r2, g->geom, g->cell_start,
+                                                  g->sorted_idx, counts, nullptr, nullptr, 0, err);
+    FORGE_LAUNCHED();
+    if (!offsets && !hits) return FORGE_OK;
+    const uint32_t tiles = grid_blocks(nq, grid::kScanTile);
+    grid::scan_tile_sums_kernel<<<tiles, grid::kScanThreads, 0, st>>>(counts, (uint32_t)nq, g->scan_sums);
+    grid::scan_sums_kernel<<<1, 1024, 0, st>>>(g->scan_sums, tiles);
+    grid::scan_apply_kernel<<<tiles, grid::kScanThreads, 0, st>>>(counts, (uint32_t)nq, g->scan_sums, offs);
+    FORGE_LAUNCHED();
+    if (hits) {
+        grid::query_kernel<true><<<nb, 128, 0, st>>>(px, py, pz, qx, qy, qz, (uint32_t)nq, r2, g->geom,
+                                                     g->cell_start, g->sorted_idx, counts, offs, hits, max_hits, err);
+        FORGE_LAUNCHED();
+    }
+    return FORGE_OK;
+}
+
+extern "C" int forge_grid_check(forge_grid* g, void* stream) {
+    if (!g) return set_error(FORGE_ERR_INVALID_ARG, "forge_grid_check: grid is NULL");
+    FORGE_DEVICE_SCOPE(g->device);
+    return check_status_word(g->scratch.meta + kMetaErr, as_stream(stream), "grid");
+}
+
+// ===========================================================================
+// SPH
+// ===========================================================================
+extern "C" int forge_sph_density(forge_grid* g, const forge_sph_params* p, const float* px, const float* py,
+                                 const float* pz, uint64_t n, float* density, void* stream) {
+    if (!g || !p) return set_error(FORGE_ERR_INVALID_ARG, "forge_sph_density: NULL grid or params");
+    if (n && !density) return set_error(FORGE_ERR_INVALID_ARG, "forge_sph_density: density is NULL");
+    FORGE_DEVICE_SCOPE(g->device);
+    cudaStream_t st = as_stream(stream);
+    int rc = grid_build_impl(g, px, py, pz, 1, n, nullptr, true, nullptr, nullptr, nullptr, st);
+    if (rc != FORGE_OK) return rc;
+    return launch_density(g, p, density, st);
+}
+
+extern "C" int forge_sph_force(forge_grid* g, const forge_sph_params* p, uint32_t terms, const float* px,
+                               const float* py, const float* pz, const float* vx_in, const float* vy_in,
+                               const float* vz_in, const float* density, uint64_t n, float dt, float* vx_out,
+                               float* vy_out, float* vz_out, float* ax_out, float* ay_out, float* az_out,
+                               void* stream) {
+    (void)px;
+    (void)py;
+    (void)pz;
+    if (!g || !p) return set_error(FORGE_ERR_INVALID_ARG, "forge_sph_force: NULL grid or params");
+    if (terms == 0 || terms > 3) return set_error(FORGE_ERR_INVALID_ARG, "forge_sph_force: terms must be 1, 2 or 3");
+    if (!g->built || g->n != n)
+        return set_error(FORGE_ERR_INVALID_ARG,
+                         "forge_sph_force: the grid was not built for these %llu particles (last build: %llu)",
+                         (unsigned long long)n, (unsigned long long)g->n);
+    if (n == 0) return FORGE_OK;
+    if (!vx_in || !vy_in || !vz_in || !density || !vx_out || !vy_out || !vz_out)
+        return set_error(FORGE_ERR_INVALID_ARG, "forge_sph_force: NULL velocity/density pointer");
+    if ((ax_out == nullptr) != (ay_out == nullptr) || (ax_out == nullptr) != (az_out == nullptr))
+        return set_error(FORGE_ERR_INVALID_ARG, "forge_sph_force: pass all three accel arrays or none");
+    FORGE_DEVICE_SCOPE(g->device);
+    cudaStream_t st = as_stream(stream);
+    grid::gather_vel_rho_kernel<<<grid_blocks(n, 256), 256, 0, st>>>(g->sorted_idx, (uint32_t)n, vx_in, vy_in,
+                                                                     vz_in, density, g->vel4);
+    FORGE_LAUNCHED();
+    const sph::SphConsts c = make_consts(p);
+    sph::StepEpi ep{};
+    ep.dt = dt;
+    sph::ForceOut o{vx_out, vy_out, vz_out, ax_out, ay_out, az_out, nullptr, nullptr, nullptr};
+    if (terms == 3) launch_force_t<3, 0>(g, c, ep, o, st);
+    else if (terms == 1) launch_force_t<1, 0>(g, c, ep, o, st);
+    else launch_force_t<2, 0>(g, c, ep, o, st);
+    FORGE_LAUNCHED();
+    return FORGE_OK;
+}
+
+extern "C" int forge_sph_step(forge_grid* g, const forge_sph_params* p, const forge_step_params* sp, float* px,
+                              float* py, float* pz, float* vx, float* vy, float* vz, float* density, uint64_t n,
+                              void* stream) {
+    if (!g || !p || !sp) return set_error(FORGE_ERR_INVALID_ARG, "forge_sph_step: NULL grid or params");
+    if (n && (!px || !py || !pz || !vx || !vy || !vz))
+        return set_error(FORGE_ERR_INVALID_ARG, "forge_sph_step: NULL position/velocity pointer");
+    FORGE_DEVICE_SCOPE(g->device);
+    cudaStream_t st = as_stream(stream);
+    prof_mark(g, 0, st);
+    int rc = grid_build_impl(g, px, py, pz, 1, n, nullptr, true, vx, vy, vz, st);
+    if (rc != FORGE_OK) return rc;
+    if (n == 0) return FORGE_OK;
+    rc = launch_density(g, p, density, st);
+    if (rc != FORGE_OK) return rc;
+    prof_mark(g, 3, st);
+    sph::StepEpi ep{};
+    ep.dt = sp->dt;
+    ep.gx = sp->gravity[0];
+    ep.gy = sp->gravity[1];
+    ep.gz = sp->gravity[2];
+    for (int a = 0; a < 3; ++a) {
+        ep.bmin[a] = sp->box_min[a];
+        ep.bmax[a] = sp->box_max[a];
+    }
+    ep.restitution = sp->restitution;
+    ep.flags = sp->flags;
+    sph::ForceOut o{vx, vy, vz, nullptr, nullptr, nullptr, px, py, pz};
+    launch_force_t<3, 1>(g, make_consts(p), ep, o, st);
+    FORGE_LAUNCHED();
+    prof_mark(g, 4, st);
+    prof_step_done(g);
+    return FORGE_OK;
+}
+
+extern "C" int forge_grid_profile_enable(forge_grid* g, uint32_t max_steps) {
+    if (!g) return set_error(FORGE_ERR_INVALID_ARG, "forge_grid_profile_enable: grid is NULL");
+    FORGE_DEVICE_SCOPE(g->device);
+    prof_free(g);
+    if (max_steps == 0) return FORGE_OK;
+    g->prof_events.resize((size_t)max_steps * 5);
+    for (auto& e : g->prof_events) FORGE_CUDA(cudaEventCreate(&e));
+    g->prof_cap = max_steps;
+    return FORGE_OK;
+}
+
+extern "C" int forge_grid_profile_read(forge_grid* g, float* out, uint32_t cap_steps, uint32_t* steps) {
+    if (!g || !steps) return set_error(FORGE_ERR_INVALID_ARG, "forge_grid_profile_read: NULL argument");
+    *steps = 0;
+    if (!g->prof_cap) return FORGE_OK;
+    FORGE_DEVICE_SCOPE(g->device);
+    const uint32_t cnt = std::min(g->prof_count, cap_steps);
+    const uint32_t first = (g->prof_next + g->prof_cap - g->prof_count) % g->prof_cap;
+    for (uint32_t i = 0; i < cnt; ++i) {
+        const size_t b = (size_t)((first + i) % g->prof_cap) * 5;
+        FORGE_CUDA(cudaEventSynchronize(g->prof_events[b + 4]));
+        for (int k = 0; k < 4; ++k)
+            FORGE_CUDA(cudaEventElapsedTime(&out[i * 4 + k], g->prof_events[b + k], g->prof_events[b + k + 1]));
+    }
+    *steps = cnt;
+    g->prof_count = 0;
+    return FORGE_OK;
+}

@@ -1,0 +1,253 @@
+// Uniform hash grid kernels (sm_100a): cell hashing, the cell-start table,
+// the cell-ordered particle gather, find_cell_boundaries and the batched
+// neighbour query.
+#pragma once
+
+#include "common.cuh"
+
+namespace forge {
+namespace grid {
+
+struct GridGeom {
+    float ox, oy, oz;  // origin (0 for the SPH modules)
+    float cs;          // cell size
+    int nx, ny, nz;
+};
+
+// Saturating float -> int as Rust's `as i32` and CUDA's cvt.rzi.s32 do
+// (NaN -> 0). floorf() already rounded, so this is the truncating convert.
+__device__ __forceinline__ int floor_to_int(float v) { return (int)floorf(v); }
+
+// Cell of a position: hashgrid.rs:128-139 (origin subtracted, floor, clamp,
+// x-fastest linear index); with origin 0 this is sph_fused.rs:91-99 exactly,
+// since (x - 0.0f) == x. The divide is IEEE (no fast-math), which keeps the
+// cell index bit-exact with the CPU.
+__device__ __forceinline__ uint32_t cell_of(float x, float y, float z, const GridGeom& g) {
+    int cx = floor_to_int((x - g.ox) / g.cs);
+    int cy = floor_to_int((y - g.oy) / g.cs);
+    int cz = floor_to_int((z - g.oz) / g.cs);
+    cx = cx < 0 ? 0 : (cx >= g.nx ? g.nx - 1 : cx);
+    cy = cy < 0 ? 0 : (cy >= g.ny ? g.ny - 1 : cy);
+    cz = cz < 0 ? 0 : (cz >= g.nz ? g.nz - 1 : cz);
+    return (uint32_t)cx + (uint32_t)cy * (uint32_t)g.nx + (uint32_t)cz * (uint32_t)g.nx * (uint32_t)g.ny;
+}
+
+// Histogram key source that hashes positions and stores the cell index.
+// stride 1: SoA (px, py, pz separate); stride 3: Vec3f AoS (px = xyz).
+struct HashKeys {
+    const float* __restrict__ px;
+    const float* __restrict__ py;
+    const float* __restrict__ pz;
+    uint32_t stride;
+    GridGeom g;
+    uint32_t* __restrict__ keys_out;
+    __device__ __forceinline__ uint32_t operator()(uint32_t i) const {
+        const size_t o = (size_t)i * stride;
+        const uint32_t c = cell_of(px[o], py[o], pz[o], g);
+        keys_out[i] = c;
+        return c;
+    }
+};
+
+// Fill value `v` into table[a..b] (inclusive, empty if a > b) with the whole
+// warp helping on long runs. Every lane of the warp must call this.
+__device__ __forceinline__ void warp_fill_runs(uint32_t* __restrict__ table, int64_t a, int64_t b,
+                                               uint32_t v) {
+    const int lane = threadIdx.x & 31;
+    const int64_t len = b - a + 1;
+    const bool longrun = len > 8;
+    if (!longrun) {
+        for (int64_t c = a; c <= b; ++c) table[c] = v;
+    }
+    uint32_t todo = __ballot_sync(0xffffffffu, longrun);
+    while (todo) {
+        const int src = __ffs(todo) - 1;
+        todo &= todo - 1;
+        const int64_t la = __shfl_sync(0xffffffffu, a, src);
+        const int64_t lb = __shfl_sync(0xffffffffu, b, src);
+        const uint32_t lv = __shfl_sync(0xffffffffu, v, src);
+        for (int64_t c = la + lane; c <= lb; c += 32) table[c] = lv;
+    }
+}
+
+// cell_start[c] = first sorted position whose key >= c, for c in [0, C],
+// so cell_start[C] == n (sph_fused.rs:280-390 without the scan or memsets).
+// Thread s in [0, n] owns the cells (key[s-1], key[s]]: each entry is
+// written exactly once, so the table needs no clearing.
+// Optionally gathers positions (and velocities) into cell order:
+//   pos4[s] = (x, y, z, bits(key)), vel4[s] = (vx, vy, vz, 0).
+struct GatherSrc {
+    const float* __restrict__ px;
+    const float* __restrict__ py;
+    const float* __restrict__ pz;
+    uint32_t stride;
+    const float* __restrict__ vx;  // nullable
+    const float* __restrict__ vy;
+    const float* __restrict__ vz;
+};
+
+__global__ void __launch_bounds__(256)
+    cell_start_gather_kernel(const uint32_t* __restrict__ skeys, const uint32_t* __restrict__ svals,
+                             uint32_t n, uint32_t C, uint32_t* __restrict__ cell_start, GatherSrc src,
+                             float4* __restrict__ pos4, float4* __restrict__ vel4) {
+    const uint32_t s = blockIdx.x * blockDim.x + threadIdx.x;
+    int64_t a = 1, b = 0;  // empty
+    uint32_t key = 0;
+    if (s <= n) {
+        if (s < n) key = skeys[s];
+        a = (s == 0) ? 0 : (int64_t)skeys[s - 1] + 1;
+        b = (s == n) ? (int64_t)C : (int64_t)key;
+    }
+    warp_fill_runs(cell_start, a, b, s);
+    if (s < n && pos4 != nullptr) {
+        const uint32_t i = svals[s];
+        const size_t o = (size_t)i * src.stride;
+        pos4[s] = make_float4(src.px[o], src.py[o], src.pz[o], __uint_as_float(key));
+        if (vel4 != nullptr) vel4[s] = make_float4(src.vx[i], src.vy[i], src.vz[i], 0.f);
+    }
+}
+
+// vel4[s] = (vx[i], vy[i], vz[i], rho[i]) with i = svals[s].
+__global__ void __launch_bounds__(256)
+    gather_vel_rho_kernel(const uint32_t* __restrict__ svals, uint32_t n, const float* __restrict__ vx,
+                          const float* __restrict__ vy, const float* __restrict__ vz,
+                          const float* __restrict__ rho, float4* __restrict__ vel4) {
+    const uint32_t s = blockIdx.x * blockDim.x + threadIdx.x;
+    if (s >= n) return;
+    const uint32_t i = svals[s];
+    vel4[s] = make_float4(vx[i], vy[i], vz[i], rho[i]);
+}
+
+// find_cell_boundaries (radix_sort.rs:444-466 plus the two fills :259-293)
+// in one pass: thread s in [0, n] handles the boundary between sorted
+// positions s-1 and s, and the empty cells strictly between their ids.
+__global__ void __launch_bounds__(256)
+    cell_bounds_kernel(const uint32_t* __restrict__ ids, uint32_t n, uint32_t C,
+                       uint32_t* __restrict__ start, uint32_t* __restrict__ end, uint32_t* err) {
+    const uint32_t s = blockIdx.x * blockDim.x + threadIdx.x;
+    int64_t a = 1, b = 0;
+    if (s <= n) {
+        int64_t prev = -1, cur = C;
+        if (s > 0) prev = min((int64_t)ids[s - 1], (int64_t)C);
+        if (s < n) {
+            const uint32_t id = ids[s];
+            if (id >= C) atomicOr(err, kDevKeyRange);
+            cur = min((int64_t)id, (int64_t)C);
+        }
+        if (prev != cur) {
+            if (prev >= 0 && prev < C) end[prev] = s;
+            if (cur < C) start[cur] = s;
+        }
+        a = prev + 1;
+        b = min(cur, (int64_t)C) - 1;
+    }
+    warp_fill_runs(start, a, b, 0xffffffffu);
+    warp_fill_runs(end, a, b, 0u);
+}
+
+// ---------------------------------------------------------------------------
+// Batched neighbour query, hashgrid.rs:145-193: cell of the query WITHOUT
+// clamping, 3x3x3 walk dz, dy, dx, hits where dist^2 <= r^2 with
+// diff = p - q. Pass 1 counts, pass 2 (after a scan) writes hits.
+// ---------------------------------------------------------------------------
+template <bool WRITE>
+__global__ void __launch_bounds__(128)
+    query_kernel(const float* __restrict__ px, const float* __restrict__ py, const float* __restrict__ pz,
+                 const float* __restrict__ qx, const float* __restrict__ qy, const float* __restrict__ qz,
+                 uint32_t nq, float r2, GridGeom g, const uint32_t* __restrict__ cell_start,
+                 const uint32_t* __restrict__ sorted_idx, uint32_t* __restrict__ counts,
+                 const uint32_t* __restrict__ offsets, uint32_t* __restrict__ hits, uint64_t max_hits,
+                 uint32_t* err) {
+    const uint32_t q = blockIdx.x * blockDim.x + threadIdx.x;
+    if (q >= nq) return;
+    const float x = qx[q], y = qy[q], z = qz[q];
+    const int cx = floor_to_int((x - g.ox) / g.cs);
+    const int cy = floor_to_int((y - g.oy) / g.cs);
+    const int cz = floor_to_int((z - g.oz) / g.cs);
+    uint64_t out = 0;
+    if (WRITE) {
+        out = offsets[q];
+        if (out + counts[q] > max_hits) {
+            atomicOr(err, kDevCapacity);
+            return;
+        }
+    }
+    uint32_t cnt = 0;
+    for (int dz = -1; dz <= 1; ++dz) {
+        for (int dy = -1; dy <= 1; ++dy) {
+            for (int dx = -1; dx <= 1; ++dx) {
+                // (int64 to avoid overflow for far-away queries)
+                const int64_t nxx = (int64_t)cx + dx, nyy = (int64_t)cy + dy, nzz = (int64_t)cz + dz;
+                if (nxx < 0 || nyy < 0 || nzz < 0) continue;
+                if (nxx >= g.nx || nyy >= g.ny || nzz >= g.nz) continue;
+                const uint32_t cell = (uint32_t)nxx + (uint32_t)nyy * (uint32_t)g.nx +
+                                      (uint32_t)nzz * (uint32_t)g.nx * (uint32_t)g.ny;
+                const uint32_t b = cell_start[cell], e = cell_start[cell + 1];
+                for (uint32_t s = b; s < e; ++s) {
+                    const uint32_t j = sorted_idx[s];
+                    const float ddx = px[j] - x, ddy = py[j] - y, ddz = pz[j] - z;
+                    const float d2 = ddx * ddx + ddy * ddy + ddz * ddz;
+                    if (d2 <= r2) {
+                        if (WRITE) hits[out + cnt] = j;
+                        ++cnt;
+                    }
+                }
+            }
+        }
+    }
+    if (!WRITE) counts[q] = cnt;
+}
+
+// Three-phase exclusive scan of u32 counts (tile sums, scan of the sums in
+// one block, rescan of each tile); out[n] receives the total.
+constexpr int kScanThreads = 256;
+constexpr int kScanItems = 16;
+constexpr int kScanTile = kScanThreads * kScanItems;
+
+__global__ void __launch_bounds__(kScanThreads)
+    scan_tile_sums_kernel(const uint32_t* __restrict__ in, uint32_t n, uint32_t* __restrict__ sums) {
+    __shared__ uint32_t s_scan[kScanThreads / 32 + 1];
+    const uint32_t base = blockIdx.x * kScanTile + threadIdx.x * kScanItems;
+    uint32_t acc = 0;
+    for (int k = 0; k < kScanItems; ++k)
+        if (base + k < n) acc += in[base + k];
+    uint32_t total;
+    block_exclusive_scan<kScanThreads>(acc, s_scan, &total);
+    if (threadIdx.x == 0) sums[blockIdx.x] = total;
+}
+
+__global__ void __launch_bounds__(1024) scan_sums_kernel(uint32_t* __restrict__ sums, uint32_t m) {
+    __shared__ uint32_t s_scan[1024 / 32 + 1];
+    uint32_t carry = 0;
+    for (uint32_t base = 0; base < m; base += 1024) {
+        const uint32_t i = base + threadIdx.x;
+        const uint32_t v = i < m ? sums[i] : 0u;
+        uint32_t total;
+        const uint32_t ex = block_exclusive_scan<1024>(v, s_scan, &total);
+        if (i < m) sums[i] = carry + ex;
+        carry += total;
+    }
+}
+
+__global__ void __launch_bounds__(kScanThreads)
+    scan_apply_kernel(const uint32_t* __restrict__ in, uint32_t n, const uint32_t* __restrict__ sums,
+                      uint32_t* __restrict__ out) {
+    __shared__ uint32_t s_scan[kScanThreads / 32 + 1];
+    const uint32_t base = blockIdx.x * kScanTile + threadIdx.x * kScanItems;
+    uint32_t v[kScanItems];
+    uint32_t acc = 0;
+    for (int k = 0; k < kScanItems; ++k) {
+        v[k] = (base + k < n) ? in[base + k] : 0u;
+        acc += v[k];
+    }
+    uint32_t total;
+    uint32_t run = sums[blockIdx.x] + block_exclusive_scan<kScanThreads>(acc, s_scan, &total);
+    for (int k = 0; k < kScanItems; ++k) {
+        if (base + k < n) out[base + k] = run;
+        run += v[k];
+    }
+    if (base < n && base + kScanItems >= n) out[n] = run;
+}
+
+}  // namespace grid
+}  // namespace forge

@@ -1,0 +1,245 @@
+// Onesweep-style stable LSD radix sort of (u32 key, u32 value) pairs, sm_100a.
+//
+// Replaces the reference's 4-bit LSD sorter (forge-runtime/src/radix_sort.rs:79-220,
+// kernels radix_histogram :323-351, radix_prefix_sum :356-389, radix_scatter
+// :394-440). Same result (a stable sort by the low key bits), different machine:
+//
+//  * 8-bit digits, ceil(bits/8) passes instead of bits/4.
+//  * One up-front kernel builds the digit histograms of every pass at once
+//    (one read of the keys), so each pass is a single kernel.
+//  * Each pass kernel takes a tile of kTile keys, ranks them inside the tile
+//    with warp-level __match_any_sync (stable: item-major, lane-minor order is
+//    the input order), finds the tile's global offset per digit with a
+//    decoupled look-back over earlier tiles (bounded waits), stages the
+//    digit-sorted tile in shared memory and writes it out coalesced.
+//  * Tile ids come from an atomic counter, so every tile a CTA waits on
+//    belongs to a CTA that is already running (forward progress without
+//    co-residency assumptions).
+#pragma once
+
+#include "common.cuh"
+
+namespace forge {
+namespace radix {
+
+constexpr int kRadixBits = 8;
+constexpr int kRadix = 1 << kRadixBits;
+constexpr int kThreads = 256;  // == kRadix: one digit per thread in the look-back
+constexpr int kWarps = kThreads / 32;
+constexpr int kItems = 16;
+constexpr int kTile = kThreads * kItems;  // 4096 keys per tile
+constexpr int kMaxPasses = 4;
+
+// Look-back status word: [31] pass parity | [30:29] flag | [28:0] count.
+constexpr uint32_t kFlagAgg = 1u << 29;
+constexpr uint32_t kFlagPre = 2u << 29;
+constexpr uint32_t kFlagMask = 3u << 29;
+constexpr uint32_t kParityBit = 1u << 31;
+constexpr uint32_t kCountMask = (1u << 29) - 1;
+constexpr uint64_t kMaxN = (1ull << 29) - 1;
+
+constexpr int kHistThreads = 256;
+
+__host__ __device__ constexpr uint32_t num_tiles(uint64_t n) {
+    return (uint32_t)((n + kTile - 1) / kTile);
+}
+
+// Digit of `key` for a pass starting at `shift` with `bits` bits.
+__device__ __forceinline__ uint32_t digit_of(uint32_t key, uint32_t shift, uint32_t mask) {
+    return (key >> shift) & mask;
+}
+
+// ---------------------------------------------------------------------------
+// Key sources for the up-front histogram kernel.
+// ---------------------------------------------------------------------------
+struct KeysFromArray {
+    const uint32_t* __restrict__ keys;
+    __device__ __forceinline__ uint32_t operator()(uint32_t i) const { return keys[i]; }
+};
+
+// ---------------------------------------------------------------------------
+// Up-front histogram: hist[p*256 + d] += #keys whose pass-p digit is d, for
+// every pass p. Also zeroes the look-back status table used by the passes.
+// Each block keeps a shared histogram; updates are warp-aggregated with
+// __match_any_sync so low-entropy digits (cell keys of spatially ordered
+// particles) do not serialise on one shared address.
+// ---------------------------------------------------------------------------
+template <class Src>
+__global__ void __launch_bounds__(kHistThreads)
+    digit_histogram_kernel(Src src, uint32_t n, uint32_t begin_bit, uint32_t end_bit,
+                           uint32_t passes, uint32_t* __restrict__ hist,
+                           uint4* __restrict__ status, uint32_t status_vec4) {
+    __shared__ uint32_t s_hist[kMaxPasses * kRadix];
+    for (uint32_t j = threadIdx.x; j < kMaxPasses * kRadix; j += kHistThreads) s_hist[j] = 0;
+
+    const uint32_t stride = gridDim.x * kHistThreads;
+    const uint4 zero = make_uint4(0, 0, 0, 0);
+    for (uint32_t j = blockIdx.x * kHistThreads + threadIdx.x; j < status_vec4; j += stride)
+        status[j] = zero;
+    __syncthreads();
+
+    const uint32_t lane_lt = lanemask_lt();
+    for (uint32_t base = blockIdx.x * kHistThreads; base < n; base += stride) {
+        const uint32_t i = base + threadIdx.x;
+        const bool valid = i < n;
+        const uint32_t key = valid ? src(i) : 0u;
+        for (uint32_t p = 0; p < passes; ++p) {
+            const uint32_t shift = begin_bit + p * kRadixBits;
+            const uint32_t bits = min((uint32_t)kRadixBits, end_bit - shift);
+            const uint32_t d = valid ? digit_of(key, shift, (1u << bits) - 1u) : 0xffffu;
+            const uint32_t peers = __match_any_sync(0xffffffffu, d);
+            if (valid && (peers & lane_lt) == 0)
+                atomicAdd(&s_hist[p * kRadix + d], (uint32_t)__popc(peers));
+        }
+    }
+    __syncthreads();
+    for (uint32_t j = threadIdx.x; j < passes * kRadix; j += kHistThreads) {
+        const uint32_t c = s_hist[j];
+        if (c) atomicAdd(&hist[j], c);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// One Onesweep pass. IOTA: the input values are the element indices (first
+// pass of the grid build), vals_in is not read.
+// ---------------------------------------------------------------------------
+template <bool IOTA>
+__global__ void __launch_bounds__(kThreads)
+    onesweep_pass_kernel(const uint32_t* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
+                         uint32_t* __restrict__ keys_out, uint32_t* __restrict__ vals_out,
+                         uint32_t n, uint32_t shift, uint32_t bits,
+                         const uint32_t* __restrict__ pass_hist,  // [256] of this pass
+                         uint32_t* status,                        // [tiles][256]
+                         uint32_t* tile_counter, uint32_t parity, uint32_t* err) {
+    __shared__ uint32_t s_whist[kWarps][kRadix];  // per-warp digit counts, then offsets
+    __shared__ uint32_t s_tile_off[kRadix];       // digit start inside the sorted tile
+    __shared__ uint32_t s_base[kRadix];           // global dst = s_base[d] + tile position
+    __shared__ uint32_t s_scan[kWarps + 1];
+    __shared__ uint32_t s_exchange[kTile];
+    __shared__ uint32_t s_tile;
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 0) s_tile = atomicAdd(tile_counter, 1u);
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) s_whist[w][tid] = 0;
+    __syncthreads();
+
+    const uint32_t tile = s_tile;
+    const uint32_t tile_start = tile * kTile;
+    const uint32_t mask = (1u << bits) - 1u;
+    const uint32_t warp_start = tile_start + warp * 32 * kItems;
+
+    // Load: warp-striped so each load instruction is 128 contiguous bytes and
+    // (item, lane) order equals input order.
+    uint32_t key[kItems], val[kItems];
+#pragma unroll
+    for (int k = 0; k < kItems; ++k) {
+        const uint32_t idx = warp_start + k * 32 + lane;
+        const bool ok = idx < n;
+        key[k] = ok ? keys_in[idx] : 0u;
+        if (IOTA) val[k] = idx;
+        else val[k] = ok ? vals_in[idx] : 0u;
+    }
+
+    // Stable warp-level ranking.
+    const uint32_t lt = lanemask_lt();
+    uint32_t rank[kItems];
+#pragma unroll
+    for (int k = 0; k < kItems; ++k) {
+        const uint32_t idx = warp_start + k * 32 + lane;
+        const bool ok = idx < n;
+        const uint32_t d = ok ? digit_of(key[k], shift, mask) : 0xffffu;
+        const uint32_t peers = __match_any_sync(0xffffffffu, d);
+        uint32_t before = 0;
+        if (ok) before = s_whist[warp][d];
+        __syncwarp();
+        if (ok && (peers & lt) == 0) s_whist[warp][d] = before + __popc(peers);
+        __syncwarp();
+        rank[k] = before + __popc(peers & lt);
+    }
+    __syncthreads();
+
+    // Per digit (thread tid == digit): exclusive offsets across warps and the
+    // tile count; publish the tile aggregate as early as possible.
+    uint32_t cnt = 0;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+        const uint32_t c = s_whist[w][tid];
+        s_whist[w][tid] = cnt;
+        cnt += c;
+    }
+    uint32_t* my_status = status + (size_t)tile * kRadix + tid;
+    const uint32_t par = parity ? kParityBit : 0u;
+    st_relaxed_u32(my_status, par | (tile == 0 ? kFlagPre : kFlagAgg) | cnt);
+
+    uint32_t total;
+    const uint32_t tile_off = block_exclusive_scan<kThreads>(cnt, s_scan, &total);
+    s_tile_off[tid] = tile_off;
+    const uint32_t hist_off = block_exclusive_scan<kThreads>(pass_hist[tid], s_scan, &total);
+
+    // Decoupled look-back for digit tid.
+    uint32_t excl = 0;
+    if (tile > 0) {
+        int t = (int)tile - 1;
+        uint32_t spins = 0;
+        while (true) {
+            const uint32_t v = ld_relaxed_u32(status + (size_t)t * kRadix + tid);
+            const bool ready = ((v & kParityBit) == par) && (v & kFlagMask) != 0;
+            if (!ready) {
+                if (++spins > kSpinLimit) {
+                    atomicOr(err, kDevTimeout);
+                    break;
+                }
+                if (spins > 64) __nanosleep(64);
+                continue;
+            }
+            excl += v & kCountMask;
+            if ((v & kFlagMask) == kFlagPre || t == 0) break;
+            --t;
+        }
+        st_relaxed_u32(my_status, par | kFlagPre | ((excl + cnt) & kCountMask));
+    }
+    s_base[tid] = hist_off + excl - tile_off;
+    __syncthreads();
+
+    // Stage the digit-sorted tile in shared memory (keys), write out.
+    uint32_t pos[kItems];
+#pragma unroll
+    for (int k = 0; k < kItems; ++k) {
+        const uint32_t idx = warp_start + k * 32 + lane;
+        if (idx < n) {
+            const uint32_t d = digit_of(key[k], shift, mask);
+            pos[k] = s_tile_off[d] + s_whist[warp][d] + rank[k];
+            s_exchange[pos[k]] = key[k];
+        } else {
+            pos[k] = 0xffffffffu;
+        }
+    }
+    __syncthreads();
+
+    const uint32_t tile_n = min((uint32_t)kTile, n - tile_start);
+    uint32_t dst[kItems];
+#pragma unroll
+    for (int k = 0; k < kItems; ++k) {
+        const uint32_t j = tid + k * kThreads;
+        dst[k] = 0xffffffffu;
+        if (j < tile_n) {
+            const uint32_t kk = s_exchange[j];
+            dst[k] = s_base[digit_of(kk, shift, mask)] + j;
+            keys_out[dst[k]] = kk;
+        }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < kItems; ++k)
+        if (pos[k] != 0xffffffffu) s_exchange[pos[k]] = val[k];
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < kItems; ++k) {
+        const uint32_t j = tid + k * kThreads;
+        if (j < tile_n) vals_out[dst[k]] = s_exchange[j];
+    }
+}
+
+}  // namespace radix
+}  // namespace forge

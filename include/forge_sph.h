@@ -1,0 +1,258 @@
+/*
+ * forge_sph.h -- C ABI of the B200 (sm_100a) particle hot path.
+ *
+ * This library replaces, for the particle hot path only, the NVRTC-compiled
+ * CUDA strings that huaying/forge-gpu launches through cudarc. Every entry
+ * point below names the reference interface it stands in for (paths are
+ * relative to the forge-gpu project root).
+ *
+ * Conventions
+ *  - All pointers are DEVICE pointers unless a comment says "host".
+ *  - All sizes are uint64_t element counts.
+ *  - `stream` is a cudaStream_t / CUstream passed as void* (NULL = legacy
+ *    default stream). Every call only enqueues work on that stream: no host
+ *    synchronisation and no device allocation happen inside build / sort /
+ *    density / force / step calls, so they may be recorded into a CUDA graph.
+ *    Temporaries are allocated once, in the *_create calls (the reference's
+ *    "pre-allocated for graph capture" contract, forge-runtime/src/radix_sort.rs:10).
+ *  - Return value: FORGE_OK (0) on success, a negative FORGE_ERR_* code
+ *    otherwise; forge_last_error() returns the calling thread's message.
+ *    Conditions the reference asserts/panics on (radix_sort.rs:86-87) are
+ *    returned as FORGE_ERR_INVALID_ARG here.
+ *  - A handle is used by one host thread at a time; distinct handles are
+ *    independent. Each handle is bound to the device ordinal given at create
+ *    (the reference pins everything to device 0, forge-runtime/src/cuda.rs:55-63).
+ *  - Device-side failures (a bounded wait that gave up, an out-of-range key)
+ *    are recorded in a per-handle status word and reported by *_check().
+ */
+#ifndef FORGE_SPH_H
+#define FORGE_SPH_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FORGE_SPH_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define FORGE_API __attribute__((visibility("default")))
+#else
+#define FORGE_API
+#endif
+
+enum forge_status {
+    FORGE_OK = 0,
+    FORGE_ERR_INVALID_ARG = -1, /* bad pointer / size / bit range          */
+    FORGE_ERR_CAPACITY = -2,    /* n > max_n given at create                */
+    FORGE_ERR_CUDA = -3,        /* a CUDA runtime call failed               */
+    FORGE_ERR_TIMEOUT = -4,     /* a bounded device wait gave up            */
+    FORGE_ERR_NCCL = -5,        /* reserved for the sharded path            */
+    FORGE_ERR_DEVICE = -6       /* device-side check failed (e.g. key >= C) */
+};
+
+/* Device status bits written by kernels (read back by *_check). */
+#define FORGE_DEV_TIMEOUT 0x1u
+#define FORGE_DEV_KEY_RANGE 0x2u
+#define FORGE_DEV_CAPACITY 0x4u
+
+/* Copy the calling thread's last error message into buf (NUL-terminated).
+ * Returns the full message length. */
+FORGE_API uint64_t forge_last_error(char* buf, uint64_t len);
+
+/* ABI version of the loaded library (FORGE_SPH_ABI_VERSION). */
+FORGE_API int forge_abi_version(void);
+
+/* ------------------------------------------------------------------------ */
+/* Radix sort -- replaces RadixSorter (forge-runtime/src/radix_sort.rs:26-220) */
+/* ------------------------------------------------------------------------ */
+
+typedef struct forge_sorter forge_sorter;
+
+/* RadixSorter::new(max_n, ordinal) -- radix_sort.rs:55-70.
+ * Allocates alternate key/value buffers for max_n pairs plus the Onesweep
+ * histogram and look-back status tables. max_n < 2^30. */
+FORGE_API int forge_sorter_create(uint64_t max_n, int device, forge_sorter** out);
+
+/* RadixSorter::sort(keys, values, n, num_bits) -- radix_sort.rs:79-220.
+ * Stable LSD sort of (keys[i], vals[i]) by key bits [begin_bit, end_bit).
+ * Equal keys keep their input order (bit-exact equal to std::stable_sort by
+ * (key >> begin_bit) & mask). Bits outside the range are carried, not sorted.
+ * vals may be NULL: the sort then behaves as if vals[i] == i (the particle
+ * index) and writes the permutation into the value output.
+ *
+ * Result location: if keys_alt/vals_alt are NULL the result is always left in
+ * keys/vals (the sorter's own alternate buffers are used, and vals must not be
+ * NULL). If the caller passes its own alternate buffers the sorter ping-pongs
+ * between the pairs and reports in *result_in_alt (host, nullable) whether
+ * the sorted data ended in keys_alt/vals_alt -- the caller then swaps its
+ * Arrays, exactly like the reference's std::mem::swap (radix_sort.rs:215-216). */
+FORGE_API int forge_sorter_sort_pairs(forge_sorter* s, uint32_t* keys, uint32_t* vals,
+                            uint32_t* keys_alt, uint32_t* vals_alt, uint64_t n,
+                            uint32_t begin_bit, uint32_t end_bit,
+                            int* result_in_alt, void* stream);
+
+/* Synchronise `stream` and report any device-side failure of this sorter
+ * (FORGE_ERR_TIMEOUT if a look-back wait gave up). Clears the status. */
+FORGE_API int forge_sorter_check(forge_sorter* s, void* stream);
+
+FORGE_API void forge_sorter_destroy(forge_sorter* s);
+
+/* find_cell_boundaries(sorted_ids, start, end, n, num_cells, ordinal)
+ * -- radix_sort.rs:229-317, kernel :444-466.
+ * start[c] = first index of cell c in sorted_ids or 0xFFFFFFFF if empty,
+ * end[c]   = one past its last index, or 0 if empty. Every one of the
+ * num_cells entries is written exactly once (no fill pass). Ids >= num_cells
+ * are skipped. */
+FORGE_API int forge_cell_bounds(const uint32_t* sorted_ids, uint32_t* start, uint32_t* end,
+                      uint64_t n, uint64_t num_cells, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Uniform hash grid -- replaces HashGrid (forge-runtime/src/hashgrid.rs)  and */
+/* the GPU grid rebuild of SphFusedModule (forge-manifest/src/modules/builtins/ */
+/* sph_fused.rs:36-408).                                                        */
+/* ------------------------------------------------------------------------ */
+
+typedef struct forge_grid forge_grid;
+
+/* HashGrid::new(cell_size, (nx,ny,nz), origin, max_particles, device)
+ * -- hashgrid.rs:50-72. origin is host float[3] (NULL = 0,0,0, the SPH
+ * modules' convention, sph_fused.rs:91-99). nx*ny*nz < 2^31. Pre-allocates
+ * every temporary for max_n particles (sort buffers, cell table, packed
+ * cell-ordered particle arrays). */
+FORGE_API int forge_grid_create(float cell_size, uint32_t nx, uint32_t ny, uint32_t nz,
+                      const float* origin, uint64_t max_n, int device,
+                      forge_grid** out);
+
+/* GPU HashGrid::build (hashgrid.rs:82-125) from SoA positions (the manifest
+ * FieldSet layout pos_x/pos_y/pos_z). Outputs (each nullable; the grid keeps
+ * its own copy either way for later density/force/query calls):
+ *   cell_idx[n]          cell of particle i (hashgrid.rs:128-139 / sph_fused.rs:84-100)
+ *   sorted_idx[n]        particle indices ordered by cell, ascending index
+ *                        within a cell (the stable order of hashgrid.rs:109-117)
+ *   cell_start[C+1]      exclusive prefix of per-cell counts, cell_start[C] = n */
+FORGE_API int forge_grid_build(forge_grid* g, const float* px, const float* py,
+                     const float* pz, uint64_t n, uint32_t* cell_idx,
+                     uint32_t* sorted_idx, uint32_t* cell_start, void* stream);
+
+/* Same as forge_grid_build for Vec3f AoS positions (12-byte x,y,z records,
+ * forge-core/src/vec.rs:137-143), the HashGrid::build input type. */
+FORGE_API int forge_grid_build_aos(forge_grid* g, const float* xyz, uint64_t n,
+                         uint32_t* cell_idx, uint32_t* sorted_idx,
+                         uint32_t* cell_start, void* stream);
+
+/* Batched GPU HashGrid::query_neighbors (hashgrid.rs:145-193): for each
+ * query point q (SoA qx/qy/qz, nq of them) list the particles of the last
+ * build within `radius` (dist^2 <= radius^2, the reference's `<=`), walking
+ * the 3x3x3 cells around q in the reference order. Output is CSR:
+ *   counts[nq]         number of hits per query (always written)
+ *   offsets[nq+1]      exclusive prefix of counts (nullable)
+ *   hits[max_hits]     hit indices, query-major, in walk order (nullable)
+ * Call once with hits == NULL to size, then again with hits; if the total
+ * exceeds max_hits, only counts/offsets are written and FORGE_ERR_CAPACITY
+ * is returned by forge_grid_check. positions are the SoA arrays the grid was
+ * built from. */
+FORGE_API int forge_grid_query(forge_grid* g, const float* px, const float* py,
+                     const float* pz, const float* qx, const float* qy,
+                     const float* qz, uint64_t nq, float radius,
+                     uint32_t* counts, uint32_t* offsets, uint32_t* hits,
+                     uint64_t max_hits, void* stream);
+
+/* Synchronise `stream`; report and clear device-side failures of this grid. */
+FORGE_API int forge_grid_check(forge_grid* g, void* stream);
+
+FORGE_API void forge_grid_destroy(forge_grid* g);
+
+/* ------------------------------------------------------------------------ */
+/* SPH passes -- replace SphDensityModule / SphPressureModule /             */
+/* SphViscosityModule / SphFusedModule::execute                             */
+/* (forge-manifest/src/modules/builtins/sph_*.rs)                           */
+/* ------------------------------------------------------------------------ */
+
+/* Module parameters (SphFusedModule fields, sph_fused.rs:14-22; cell size,
+ * grid dims and origin live in the forge_grid). */
+typedef struct forge_sph_params {
+    float h;             /* smoothing_radius                 */
+    float mass;          /* particle_mass                    */
+    float gas_constant;  /* stiffness k, p = k (rho - rho0)  */
+    float rest_density;  /* rho0                             */
+    float viscosity;     /* viscosity_coefficient mu         */
+} forge_sph_params;
+
+/* Which terms forge_sph_force evaluates. */
+#define FORGE_TERM_PRESSURE 0x1u  /* sph_pressure.rs:28-112   */
+#define FORGE_TERM_VISCOSITY 0x2u /* sph_viscosity.rs:27-106  */
+
+/* Per-step epilogue of the manifest pipeline after the SPH module
+ * (manifest_runner.rs:371-541): GravityModule (gravity.rs:31-34),
+ * IntegrateModule (integrate.rs:16-31), BoxColliderModule (box_collider.rs:26-47). */
+typedef struct forge_step_params {
+    float dt;
+    float gravity[3];    /* v += g dt                     (flags & FORGE_STEP_GRAVITY)   */
+    float box_min[3];    /* clamp + reflect               (flags & FORGE_STEP_BOX)       */
+    float box_max[3];
+    float restitution;
+    uint32_t flags;
+} forge_step_params;
+
+#define FORGE_STEP_GRAVITY 0x1u
+#define FORGE_STEP_INTEGRATE 0x2u
+#define FORGE_STEP_BOX 0x4u
+
+/* SphDensityModule::execute (sph_density.rs:388-501): rebuilds the grid
+ * from (px,py,pz) and writes the poly6 density of every particle, self
+ * included, into density[n] (original particle order):
+ *   rho_i = sum_{j: r2 < h2} m * 315/(64 pi h^9) * (h2 - r2)^3
+ * Neighbours are summed in the reference order (dz, dy, dx from -1..1, then
+ * ascending particle index within a cell). */
+FORGE_API int forge_sph_density(forge_grid* g, const forge_sph_params* p,
+                      const float* px, const float* py, const float* pz,
+                      uint64_t n, float* density, void* stream);
+
+/* Pressure and/or viscosity pass over the grid of the last build
+ * (sph_pressure.rs:28-112, sph_viscosity.rs:27-106, fused as in
+ * sph_fused.rs:518-639). Velocities are read from vel_in and written to
+ * vel_out (Jacobi update: every neighbour term sees the velocities at the
+ * start of the pass). vel_out may alias vel_in. accel_out (nullable, 3
+ * arrays) receives (a_p + a_v) / rho_i, the per-particle acceleration
+ * before the dt multiply. Particles with rho_i < 1e-6 keep their velocity
+ * (accel 0). positions must be the ones the grid was last built from. */
+FORGE_API int forge_sph_force(forge_grid* g, const forge_sph_params* p, uint32_t terms,
+                    const float* px, const float* py, const float* pz,
+                    const float* vx_in, const float* vy_in, const float* vz_in,
+                    const float* density, uint64_t n, float dt,
+                    float* vx_out, float* vy_out, float* vz_out,
+                    float* ax_out, float* ay_out, float* az_out, void* stream);
+
+/* One fused SPH step in place on the FieldSet arrays: grid rebuild,
+ * density, pressure+viscosity (Jacobi), then the optional gravity /
+ * integrate / box epilogue in pipeline order -- the work of
+ * SphFusedModule::execute followed by GravityModule, IntegrateModule and
+ * BoxColliderModule (manifest_runner.rs:371-541). density (nullable)
+ * receives rho in original order. Capture-safe. */
+FORGE_API int forge_sph_step(forge_grid* g, const forge_sph_params* p,
+                   const forge_step_params* sp, float* px, float* py,
+                   float* pz, float* vx, float* vy, float* vz, float* density,
+                   uint64_t n, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Benchmark aid (no reference counterpart; the reference only times the    */
+/* whole run with a wall clock, manifest_runner.rs:40-80).                  */
+/* ------------------------------------------------------------------------ */
+
+/* Record CUDA events at the phase boundaries of each forge_sph_step call
+ * (a ring of max_steps steps; 0 disables). Not for use under stream capture. */
+FORGE_API int forge_grid_profile_enable(forge_grid* g, uint32_t max_steps);
+
+/* Synchronise and write the phase times (ms) of the recorded steps, oldest
+ * first: out[s*4 + k] with k = 0 hash + radix sort, 1 cell table + gather,
+ * 2 density, 3 force + epilogue. *steps receives the count written
+ * (<= cap_steps). Clears the ring. */
+FORGE_API int forge_grid_profile_read(forge_grid* g, float* out, uint32_t cap_steps, uint32_t* steps);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FORGE_SPH_H */

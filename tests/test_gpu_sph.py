@@ -1,0 +1,234 @@
+"""GPU parity: SPH density, pressure/viscosity forces, the fused step and
+100-step trajectories, against the oracle.
+
+Tolerances (fp32; the GPU fuses multiply-adds, the oracle rounds every op):
+  density  |rho_gpu - rho_cpu| <= 1e-5 * rho_cpu            (per particle)
+  accel    |a_gpu - a_cpu|     <= 1e-4 * sum_j |term_j|/rho_i (per component)
+  trajectory (100 steps, cfg0) |x_gpu - x_cpu| <= 1e-5 (positions in [0,1]),
+             |v_gpu - v_cpu| <= 1e-4 * (|v_cpu| + 1e-3)
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+import forge_sph
+import oracle
+import workloads
+from _util import assert_force_close, dev, host_f32
+
+pytestmark = pytest.mark.gpu
+RHO_TOL = 1e-5
+
+
+def oparams(cfg):
+    return oracle.SphParams(cfg.h, cfg.mass, cfg.gas_constant, cfg.rest_density, cfg.viscosity)
+
+
+def gparams(cfg):
+    return forge_sph.SphParams(cfg.h, cfg.mass, cfg.gas_constant, cfg.rest_density, cfg.viscosity)
+
+
+def run_density(torch, cfg, pos):
+    g = forge_sph.HashGrid(cfg.cell_size, cfg.dims, (0, 0, 0), cfg.n, 0)
+    d = [dev(torch, p) for p in pos]
+    rho = torch.empty(cfg.n, dtype=torch.float32, device="cuda")
+    forge_sph.check(forge_sph.lib().forge_sph_density(g.handle, ctypes.byref(gparams(cfg)), *(x.data_ptr() for x in d),
+                                                      cfg.n, rho.data_ptr(), None))
+    g.check()
+    return g, d, rho
+
+
+def oracle_density(cfg, pos, threads=None):
+    ci, si, cst = oracle.grid_build(*pos, cfg.cell_size, cfg.dims)
+    rho = oracle.density(oparams(cfg), *pos, cfg.cell_size, cfg.dims, cst, si,
+                         threads or oracle.max_threads())
+    return rho, si, cst
+
+
+def check_density(cfg, pos, rho_gpu):
+    rho, si, cst = oracle_density(cfg, pos)
+    np.testing.assert_allclose(host_f32(rho_gpu), rho, rtol=RHO_TOL, atol=0)
+    return rho, si, cst
+
+
+def test_density_cfg0(cuda):
+    cfg = workloads.config("ref65k")
+    pos, _ = workloads.particles(cfg)
+    _, _, rho = run_density(cuda, cfg, pos)
+    check_density(cfg, pos, rho)
+
+
+@pytest.mark.parametrize("n,dims", [(1, (4, 4, 4)), (5, (3, 2, 1)), (4097, (1, 1, 1)), (30_000, (25, 7, 3))])
+def test_density_ragged_and_degenerate_grids(cuda, n, dims):
+    cfg = workloads.small("ref65k", n, dims)
+    pos, _ = workloads.uniform_particles(n, seed=n, lo=-0.05, hi=1.05)
+    _, _, rho = run_density(cuda, cfg, pos)
+    check_density(cfg, pos, rho)
+
+
+def test_density_dense_cells_dambreak65k(cuda):
+    cfg = workloads.config("dambreak65k")
+    pos, _ = workloads.particles(cfg)
+    _, _, rho = run_density(cuda, cfg, pos)
+    check_density(cfg, pos, rho)
+
+
+def run_force(torch, cfg, pos, vel, terms, dt=1e-4):
+    g, d, rho = run_density(torch, cfg, pos)
+    v = [dev(torch, x) for x in vel]
+    vo = [torch.empty_like(x) for x in v]
+    a = [torch.empty_like(x) for x in v]
+    forge_sph.check(forge_sph.lib().forge_sph_force(
+        g.handle, ctypes.byref(gparams(cfg)), terms, *(x.data_ptr() for x in d), *(x.data_ptr() for x in v),
+        rho.data_ptr(), cfg.n, dt, *(x.data_ptr() for x in vo), *(x.data_ptr() for x in a), None))
+    g.check()
+    return rho, [host_f32(x) for x in vo], [host_f32(x) for x in a]
+
+
+@pytest.mark.parametrize("terms", [1, 2, 3])
+def test_force_terms_cfg0(cuda, terms):
+    cfg = workloads.config("ref65k")
+    pos, vel = workloads.particles(cfg)
+    rho_g, vo_g, a_g = run_force(cuda, cfg, pos, vel, terms)
+    rho, si, cst = check_density(cfg, pos, rho_g)
+    p = oparams(cfg)
+    args = (*pos, *vel, rho, cfg.cell_size, cfg.dims, cst, si, 1e-4)
+    th = oracle.max_threads()
+    vo, a = oracle.force(p, terms, *args, threads=th)
+    _, scale = oracle.force(p, terms | 4, *args, threads=th)
+    assert_force_close(a_g, a, scale)
+    for k in range(3):
+        np.testing.assert_allclose(vo_g[k], vo[k], rtol=1e-5, atol=1e-4 * 1e-4 * scale[k].max())
+
+
+def test_force_dense_lattice_dambreak65k(cuda):
+    cfg = workloads.config("dambreak65k")
+    pos, vel = workloads.particles(cfg)
+    vel = [np.asarray(workloads.uniform_particles(cfg.n, seed=4)[1][k]) for k in range(3)]
+    rho_g, _, a_g = run_force(cuda, cfg, pos, vel, 3)
+    rho, si, cst = oracle_density(cfg, pos)
+    args = (*pos, *vel, rho, cfg.cell_size, cfg.dims, cst, si, 1e-4)
+    _, a = oracle.force(oparams(cfg), 3, *args, threads=oracle.max_threads())
+    _, scale = oracle.force(oparams(cfg), 7, *args, threads=oracle.max_threads())
+    assert_force_close(a_g, a, scale)
+
+
+def make_step(cfg):
+    sp = forge_sph.StepParams()
+    sp.dt = cfg.dt
+    sp.gravity[:] = list(cfg.gravity)
+    sp.box_min[:] = list(cfg.box_min)
+    sp.box_max[:] = list(cfg.box_max)
+    sp.restitution = cfg.restitution
+    sp.flags = 7
+    osp = oracle.StepParams(cfg.dt, cfg.gravity, cfg.box_min, cfg.box_max, cfg.restitution, 7)
+    return sp, osp
+
+
+def gpu_steps(torch, cfg, pos, vel, steps):
+    g = forge_sph.HashGrid(cfg.cell_size, cfg.dims, (0, 0, 0), cfg.n, 0)
+    p, v = [dev(torch, x) for x in pos], [dev(torch, x) for x in vel]
+    rho = torch.empty(cfg.n, dtype=torch.float32, device="cuda")
+    sp, _ = make_step(cfg)
+    L = forge_sph.lib()
+    for _ in range(steps):
+        forge_sph.check(L.forge_sph_step(g.handle, ctypes.byref(gparams(cfg)), ctypes.byref(sp),
+                                         *(x.data_ptr() for x in p), *(x.data_ptr() for x in v), rho.data_ptr(),
+                                         cfg.n, None))
+    g.check()
+    return [host_f32(x) for x in p], [host_f32(x) for x in v], host_f32(rho)
+
+
+def test_single_step_vs_oracle(cuda):
+    cfg = workloads.config("ref65k")
+    pos, vel = workloads.particles(cfg)
+    pg, vg, rg = gpu_steps(cuda, cfg, pos, vel, 1)
+    po, vo = [x.copy() for x in pos], [x.copy() for x in vel]
+    _, osp = make_step(cfg)
+    ro = oracle.step(oparams(cfg), osp, po, vo, cfg.cell_size, cfg.dims, threads=oracle.max_threads(),
+                     want_density=True)
+    np.testing.assert_allclose(rg, ro, rtol=RHO_TOL)
+    for k in range(3):
+        np.testing.assert_allclose(pg[k], po[k], rtol=0, atol=1e-6)
+        np.testing.assert_allclose(vg[k], vo[k], rtol=1e-4, atol=1e-6)
+
+
+def test_trajectory_100_steps_cfg0(cuda):
+    cfg = workloads.config("ref65k")
+    pos, vel = workloads.particles(cfg)
+    pg, vg, _ = gpu_steps(cuda, cfg, pos, vel, 100)
+    po, vo = [x.copy() for x in pos], [x.copy() for x in vel]
+    _, osp = make_step(cfg)
+    for _ in range(100):
+        oracle.step(oparams(cfg), osp, po, vo, cfg.cell_size, cfg.dims, threads=oracle.max_threads())
+    for k in range(3):
+        np.testing.assert_allclose(pg[k], po[k], rtol=0, atol=1e-5)
+        np.testing.assert_allclose(vg[k], vo[k], rtol=1e-4, atol=1e-4 * 1e-3)
+
+
+def test_step_is_deterministic(cuda):
+    cfg = workloads.config("ref65k")
+    pos, vel = workloads.particles(cfg)
+    a = gpu_steps(cuda, cfg, pos, vel, 5)
+    b = gpu_steps(cuda, cfg, pos, vel, 5)
+    for x, y in zip(a[0] + a[1], b[0] + b[1]):
+        assert np.array_equal(x, y)
+
+
+def test_pipeline_modules_match_fused_step(cuda):
+    """Pipeline(SphFused, Gravity, Integrate, BoxCollider) takes the fused
+    forge_sph_step path; the same modules run one by one must agree."""
+    torch = cuda
+    cfg = workloads.config("ref65k")
+    pos, vel = workloads.particles(cfg)
+
+    def fields():
+        f = forge_sph.FieldSet(cfg.n, 0)
+        for a, x in zip("xyz", pos):
+            f.add_f32("pos_" + a, x)
+        for a, x in zip("xyz", vel):
+            f.add_f32("vel_" + a, x)
+        return f
+
+    mods = [forge_sph.SphFusedModule(cfg.h, cfg.cell_size, cfg.dims, cfg.mass, cfg.gas_constant, cfg.rest_density,
+                                     cfg.viscosity),
+            forge_sph.GravityModule(*cfg.gravity), forge_sph.IntegrateModule(),
+            forge_sph.BoxColliderModule(*cfg.box_min, *cfg.box_max, cfg.restitution)]
+    fused = forge_sph.Pipeline()
+    for m in mods:
+        fused.add(m)
+    f1 = fields()
+    for _ in range(3):
+        fused.step(f1, cfg.dt)
+    f2 = fields()
+    for _ in range(3):
+        for m in mods:
+            m.execute(f2, cfg.dt)
+    torch.cuda.synchronize()
+    for k in ("pos_x", "pos_y", "pos_z", "vel_x", "vel_y", "vel_z"):
+        np.testing.assert_allclose(host_f32(f1.f32_fields[k]), host_f32(f2.f32_fields[k]), rtol=1e-5, atol=1e-7)
+
+
+def test_unfused_modules_sequence(cuda):
+    """SphDensity -> SphPressure -> SphViscosity (manifest_runner.rs:405-497):
+    viscosity sees the pressure-updated velocities."""
+    cfg = workloads.config("ref65k")
+    pos, vel = workloads.particles(cfg)
+    f = forge_sph.FieldSet(cfg.n, 0)
+    for a, x in zip("xyz", pos):
+        f.add_f32("pos_" + a, x)
+    for a, x in zip("xyz", vel):
+        f.add_f32("vel_" + a, x)
+    pipe = forge_sph.Pipeline()
+    pipe.add(forge_sph.SphDensityModule(cfg.h, cfg.cell_size, cfg.dims, cfg.mass))
+    pipe.add(forge_sph.SphPressureModule(cfg.h, cfg.mass, cfg.gas_constant, cfg.rest_density))
+    pipe.add(forge_sph.SphViscosityModule(cfg.h, cfg.mass, cfg.viscosity))
+    pipe.step(f, cfg.dt)
+    rho, si, cst = oracle_density(cfg, pos)
+    p = oparams(cfg)
+    th = oracle.max_threads()
+    v1, _ = oracle.force(p, 1, *pos, *vel, rho, cfg.cell_size, cfg.dims, cst, si, cfg.dt, threads=th)
+    v2, _ = oracle.force(p, 2, *pos, *v1, rho, cfg.cell_size, cfg.dims, cst, si, cfg.dt, threads=th)
+    for k, a in enumerate("xyz"):
+        np.testing.assert_allclose(host_f32(f.f32_fields["vel_" + a]), v2[k], rtol=1e-4, atol=1e-6)

@@ -1,0 +1,139 @@
+"""CPU tests: pin the oracle against the reference's own known-answer tests
+(tests/golden/reference_kats.json) and check its internal consistency."""
+import json
+import os
+
+import numpy as np
+import pytest
+
+import oracle
+import workloads
+
+GOLD = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "reference_kats.json")))
+
+
+def test_radix_small_kat():
+    k = GOLD["radix_small"]
+    sk, sv = oracle.sort_pairs(k["keys"], range(16), 0, k["num_bits"])
+    assert sk.tolist() == k["sorted_keys"]
+    assert sv.tolist() == k["sorted_vals"]
+
+
+@pytest.mark.parametrize("name", ["radix_medium", "radix_cpu_ref"])
+def test_radix_xorshift_kats(name):
+    k = GOLD[name]
+    keys = oracle.xorshift32_keys(k["seed"], k["n"], k["mask"])
+    assert keys[:8].tolist() == k["keys_head"]
+    sk, sv = oracle.sort_pairs(keys, np.arange(k["n"], dtype=np.uint32), 0, k["num_bits"])
+    assert sk.tolist() == k["sorted_keys"]
+    assert sv.tolist() == k["sorted_vals"]
+    # key/value correspondence as the reference asserts (radix_sort_test.rs:85-88)
+    assert np.array_equal(keys[sv], sk)
+
+
+def test_sort_partial_bits_is_stable_by_masked_key():
+    rng = np.random.default_rng(1)
+    keys = rng.integers(0, 2 ** 32, 20000, dtype=np.uint64).astype(np.uint32)
+    for lo, hi in ((0, 12), (4, 20), (0, 32), (8, 30)):
+        sk, sv = oracle.sort_pairs(keys, np.arange(keys.size, dtype=np.uint32), lo, hi)
+        masked = (keys >> np.uint32(lo)) & np.uint32((1 << (hi - lo)) - 1)
+        order = np.argsort(masked, kind="stable")
+        assert np.array_equal(sv, order.astype(np.uint32))
+        assert np.array_equal(sk, keys[order])
+
+
+def test_cell_bounds_kat():
+    k = GOLD["cell_bounds"]
+    s, e = oracle.cell_bounds(k["sorted"], k["num_cells"])
+    assert s.tolist() == k["start"]
+    assert e.tolist() == k["end"]
+
+
+def test_hashgrid_basic_kat():
+    k = GOLD["hashgrid_basic"]
+    xyz = np.array(k["positions"], np.float32)
+    ci, si, cs = oracle.grid_build_aos(xyz, k["cell_size"], k["dims"], k["origin"])
+    hits = oracle.query(xyz[:, 0], xyz[:, 1], xyz[:, 2], cs, si, k["cell_size"], k["dims"], k["query"],
+                        k["radius"], k["origin"]).tolist()
+    for j in k["must_contain"]:
+        assert j in hits
+    for j in k["must_not_contain"]:
+        assert j not in hits
+
+
+def test_hashgrid_uniform_kat():
+    k = GOLD["hashgrid_uniform"]
+    xyz = np.array(k["positions"], np.float32)
+    ci, si, cs = oracle.grid_build_aos(xyz, k["cell_size"], k["dims"], k["origin"])
+    hits = oracle.query(xyz[:, 0], xyz[:, 1], xyz[:, 2], cs, si, k["cell_size"], k["dims"], k["query"],
+                        k["radius"], k["origin"])
+    assert hits.size >= k["min_hits"]
+    q = np.array(k["query"], np.float32)
+    d = np.sqrt(((xyz[hits] - q) ** 2).sum(1))
+    assert (d <= k["radius"]).all()
+
+
+def test_grid_build_is_stable_counting_sort():
+    pos, _ = workloads.uniform_particles(5000, seed=3, lo=-0.1, hi=1.1)  # some outside: clamped
+    dims = (12, 9, 7)
+    ci, si, cs = oracle.grid_build(*pos, 1.0 / 9, dims)
+    order = np.argsort(ci, kind="stable")
+    assert np.array_equal(si, order.astype(np.uint32))
+    counts = np.bincount(ci, minlength=12 * 9 * 7)
+    assert cs[0] == 0 and cs[-1] == 5000
+    assert np.array_equal(np.diff(cs.astype(np.int64)), counts)
+
+
+def test_cell_of_edge_cases():
+    dims = (4, 4, 4)
+    assert oracle.cell_of((np.float32("nan"), 0.5, 0.5), None, 0.25, dims) == 0 + 2 * 4 + 2 * 16
+    assert oracle.cell_of((-1e30, 0.0, 0.0), None, 0.25, dims) == 0
+    assert oracle.cell_of((1e30, 1e30, 1e30), None, 0.25, dims) == 63
+    assert oracle.cell_of((0.25, 0.0, 0.0), None, 0.25, dims) == 1
+    assert oracle.cell_of((1.0, 0.0, 0.0), (0.5, 0, 0), 0.25, dims) == 2
+
+
+def _sph_small(n=3000, dims=(10, 10, 10), seed=5):
+    cfg = workloads.small("ref65k", n, dims)
+    pos, vel = workloads.uniform_particles(n, seed=seed)
+    p = oracle.SphParams(cfg.h, cfg.mass, cfg.gas_constant, cfg.rest_density, cfg.viscosity)
+    ci, si, cs = oracle.grid_build(*pos, cfg.cell_size, dims)
+    return cfg, p, pos, vel, si, cs
+
+
+def test_density_matches_brute_force_fp64():
+    cfg, p, pos, vel, si, cs = _sph_small()
+    rho = oracle.density(p, *pos, cfg.cell_size, cfg.dims, cs, si)
+    X = np.stack(pos, 1).astype(np.float64)
+    d2 = ((X[:, None, :] - X[None, :, :]) ** 2).sum(-1)
+    h2 = cfg.h ** 2
+    w = np.where(d2 < h2, (h2 - d2) ** 3, 0.0)
+    ref = cfg.mass * 315.0 / (64.0 * np.pi * cfg.h ** 9) * w.sum(1)
+    np.testing.assert_allclose(rho, ref, rtol=2e-5)
+
+
+def test_force_terms_add_up_and_threads_agree():
+    cfg, p, pos, vel, si, cs = _sph_small()
+    rho = oracle.density(p, *pos, cfg.cell_size, cfg.dims, cs, si)
+    args = (*pos, *vel, rho, cfg.cell_size, cfg.dims, cs, si, 1e-4)
+    _, a3 = oracle.force(p, 3, *args)
+    _, a1 = oracle.force(p, 1, *args)
+    _, a2 = oracle.force(p, 2, *args)
+    for k in range(3):
+        np.testing.assert_allclose(a3[k], a1[k] + a2[k], rtol=1e-4, atol=1e-3 * np.abs(a3[k]).max())
+    _, a3t = oracle.force(p, 3, *args, threads=4)
+    for k in range(3):
+        assert np.array_equal(a3[k], a3t[k])  # same per-particle order -> same bits
+
+
+def test_step_conserves_box_and_is_deterministic():
+    cfg, p, pos, vel, si, cs = _sph_small()
+    sp = oracle.StepParams(1e-4, (0.0, -9.81, 0.0), (0, 0, 0), (1, 1, 1), 1.0, 7)
+    a = [x.copy() for x in pos], [v.copy() for v in vel]
+    b = [x.copy() for x in pos], [v.copy() for v in vel]
+    for _ in range(3):
+        oracle.step(p, sp, a[0], a[1], cfg.cell_size, cfg.dims)
+        oracle.step(p, sp, b[0], b[1], cfg.cell_size, cfg.dims, threads=4)
+    for k in range(3):
+        assert np.array_equal(a[0][k], b[0][k])
+        assert (a[0][k] >= 0).all() and (a[0][k] <= 1).all()
