@@ -147,7 +147,12 @@ __global__ void __launch_bounds__(128)
                         const float4 vj = __ldg(vel4 + j);
                         const float rho_j = vj.w;
                         if (rho_j < 1e-6f) continue;
-                        const float r = sqrtf(r2);
+                        // diff = h - r cancels for r close to h; recompute r2
+                        // with the reference's rounding (no multiply-add
+                        // contraction) so r and diff carry no extra error.
+                        const float r2e = __fadd_rn(__fadd_rn(__fmul_rn(djx, djx), __fmul_rn(djy, djy)),
+                                                    __fmul_rn(djz, djz));
+                        const float r = sqrtf(r2e);
                         const float diff = c.h - r;
                         if (TERMS & 1) {
                             const float p_j = c.k * (rho_j - c.rho0);
