@@ -303,7 +303,8 @@ struct forge_grid {
     uint32_t* vc = nullptr;
     uint32_t* cell_start = nullptr;  // C + 1
     float4* pos4 = nullptr;          // cell-ordered (x, y, z, key)
-    float4* vel4 = nullptr;          // cell-ordered (vx, vy, vz, rho)
+    float4* vel4 = nullptr;          // cell-ordered (vx, vy, vz, 1/rho)
+    float2* aux = nullptr;           // cell-ordered (p/rho, rho)
     uint32_t* scan_sums = nullptr;   // query scan tile sums
     uint32_t* q_offsets = nullptr;   // max_n + 1
     SortScratch scratch;
@@ -366,6 +367,7 @@ extern "C" int forge_grid_create(float cell_size, uint32_t nx, uint32_t ny, uint
               dalloc(&g->vb, m) == cudaSuccess && dalloc(&g->kc, m) == cudaSuccess &&
               dalloc(&g->vc, m) == cudaSuccess && dalloc(&g->cell_start, C + 1) == cudaSuccess &&
               dalloc(&g->pos4, m) == cudaSuccess && dalloc(&g->vel4, m) == cudaSuccess &&
+              dalloc(&g->aux, m) == cudaSuccess &&
               dalloc(&g->scan_sums, m / grid::kScanTile + 1) == cudaSuccess &&
               dalloc(&g->q_offsets, m + 1) == cudaSuccess;
     if (!ok) rc = set_error(FORGE_ERR_CUDA, "forge_grid_create: cudaMalloc failed (max_n=%llu, cells=%llu)",
@@ -390,6 +392,7 @@ extern "C" void forge_grid_destroy(forge_grid* g) {
     cudaFree(g->cell_start);
     cudaFree(g->pos4);
     cudaFree(g->vel4);
+    cudaFree(g->aux);
     cudaFree(g->scan_sums);
     cudaFree(g->q_offsets);
     scratch_free(g->scratch);
@@ -450,26 +453,31 @@ sph::SphConsts make_consts(const forge_sph_params* p) {
     const float h9 = h2 * h2 * h2 * h2 * h;
     const float poly6 = 315.0f / (64.0f * 3.14159265f * h9);
     const float h6 = h2 * h2 * h2;
+    const float spiky = -45.0f / (3.14159265f * h6);
+    const float visc_lap = 45.0f / (3.14159265f * h6);
     c.h = h;
     c.h2 = h2;
+    c.h2_skip = h2 * (1.0f + 1e-4f);
     c.mass_poly6 = p->mass * poly6;
     c.mass = p->mass;
     c.k = p->gas_constant;
     c.rho0 = p->rest_density;
     c.mu = p->viscosity;
-    c.spiky = -45.0f / (3.14159265f * h6);
-    c.visc_lap = 45.0f / (3.14159265f * h6);
+    c.kp = -0.5f * p->mass * spiky;
+    c.kv = p->viscosity * p->mass * visc_lap;
     return c;
 }
 
-sph::Dims dims_of(const forge_grid* g) { return sph::Dims{g->geom.nx, g->geom.ny, g->geom.nz}; }
+sph::Geom geom_of(const forge_grid* g) {
+    return sph::Geom{g->geom.ox, g->geom.oy, g->geom.oz, g->geom.cs, g->geom.nx, g->geom.ny, g->geom.nz};
+}
 
 constexpr uint32_t kSphThreads = 128;
 
 int launch_density(forge_grid* g, const forge_sph_params* p, float* density, cudaStream_t st) {
     if (g->n == 0) return FORGE_OK;
     sph::density_kernel<<<grid_blocks(g->n, kSphThreads), kSphThreads, 0, st>>>(
-        g->pos4, g->cell_start, g->sorted_idx, (uint32_t)g->n, dims_of(g), make_consts(p), g->vel4, density);
+        g->pos4, g->cell_start, g->sorted_idx, (uint32_t)g->n, geom_of(g), make_consts(p), g->vel4, g->aux, density);
     FORGE_LAUNCHED();
     return FORGE_OK;
 }
@@ -478,7 +486,7 @@ template <int TERMS, int EPI>
 void launch_force_t(forge_grid* g, const sph::SphConsts& c, const sph::StepEpi& ep, const sph::ForceOut& o,
                     cudaStream_t st) {
     sph::force_kernel<TERMS, EPI><<<grid_blocks(g->n, kSphThreads), kSphThreads, 0, st>>>(
-        g->pos4, g->vel4, g->cell_start, g->sorted_idx, (uint32_t)g->n, dims_of(g), c, ep, o);
+        g->pos4, g->vel4, g->aux, g->cell_start, g->sorted_idx, (uint32_t)g->n, geom_of(g), c, ep, o);
 }
 
 }  // namespace
@@ -584,10 +592,10 @@ extern "C" int forge_sph_force(forge_grid* g, const forge_sph_params* p, uint32_
         return set_error(FORGE_ERR_INVALID_ARG, "forge_sph_force: pass all three accel arrays or none");
     FORGE_DEVICE_SCOPE(g->device);
     cudaStream_t st = as_stream(stream);
-    grid::gather_vel_rho_kernel<<<grid_blocks(n, 256), 256, 0, st>>>(g->sorted_idx, (uint32_t)n, vx_in, vy_in,
-                                                                     vz_in, density, g->vel4);
-    FORGE_LAUNCHED();
     const sph::SphConsts c = make_consts(p);
+    sph::gather_vel_rho_kernel<<<grid_blocks(n, 256), 256, 0, st>>>(g->sorted_idx, (uint32_t)n, vx_in, vy_in,
+                                                                    vz_in, density, c, g->vel4, g->aux);
+    FORGE_LAUNCHED();
     sph::StepEpi ep{};
     ep.dt = dt;
     sph::ForceOut o{vx_out, vy_out, vz_out, ax_out, ay_out, az_out, nullptr, nullptr, nullptr};

@@ -107,17 +107,6 @@ __global__ void __launch_bounds__(256)
     }
 }
 
-// vel4[s] = (vx[i], vy[i], vz[i], rho[i]) with i = svals[s].
-__global__ void __launch_bounds__(256)
-    gather_vel_rho_kernel(const uint32_t* __restrict__ svals, uint32_t n, const float* __restrict__ vx,
-                          const float* __restrict__ vy, const float* __restrict__ vz,
-                          const float* __restrict__ rho, float4* __restrict__ vel4) {
-    const uint32_t s = blockIdx.x * blockDim.x + threadIdx.x;
-    if (s >= n) return;
-    const uint32_t i = svals[s];
-    vel4[s] = make_float4(vx[i], vy[i], vz[i], rho[i]);
-}
-
 // find_cell_boundaries (radix_sort.rs:444-466 plus the two fills :259-293)
 // in one pass: thread s in [0, n] handles the boundary between sorted
 // positions s-1 and s, and the empty cells strictly between their ids.
