@@ -5,6 +5,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -254,6 +255,80 @@ extern "C" int forge_sorter_sort_pairs(forge_sorter* s, uint32_t* keys, uint32_t
         } else if (result_in_alt) {
             *result_in_alt = 1;
         }
+    }
+    return FORGE_OK;
+}
+
+// ===========================================================================
+// Allocation-free sort: scratch in a file-scope device array
+// ===========================================================================
+namespace {
+
+constexpr uint64_t kStaticMaxN = FORGE_STATIC_SORT_MAX_N;
+constexpr size_t kStaticTiles = (kStaticMaxN + radix::kTile - 1) / radix::kTile;
+// [meta | look-back status | alternate keys | alternate values], in words;
+// each part starts on a 16-byte boundary (kMetaWords rounded up to 4).
+constexpr size_t kStaticMetaWords = (kMetaWords + 3) / 4 * 4;
+constexpr size_t kStaticStatusWords = kStaticTiles * radix::kRadix;
+constexpr size_t kStaticWords = kStaticMetaWords + kStaticStatusWords + 2 * kStaticMaxN;
+
+static __device__ __align__(256) uint32_t g_static_sort_scratch[kStaticWords];
+
+// Device address of g_static_sort_scratch per device ordinal. In host code the
+// symbol's name is only a host-side stand-in, so the address is looked up
+// with cudaGetSymbolAddress (once per device, with that device current).
+std::mutex g_static_mu;
+uint32_t* g_static_addr[64] = {};
+
+int static_scratch(int dev, uint32_t** out) {
+    if (dev < 0 || dev >= 64) return set_error(FORGE_ERR_INVALID_ARG, "forge_sort_pairs_static: device %d", dev);
+    std::lock_guard<std::mutex> lock(g_static_mu);
+    if (!g_static_addr[dev]) {
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_static_sort_scratch);
+        if (e != cudaSuccess)
+            return set_error(FORGE_ERR_CUDA, "forge_sort_pairs_static: cudaGetSymbolAddress failed: %s",
+                             cudaGetErrorString(e));
+        g_static_addr[dev] = static_cast<uint32_t*>(p);
+    }
+    *out = g_static_addr[dev];
+    return FORGE_OK;
+}
+
+}  // namespace
+
+extern "C" int forge_sort_pairs_static(uint32_t* keys, uint32_t* vals, uint64_t n, uint32_t begin_bit,
+                                       uint32_t end_bit, void* stream) {
+    if (n > kStaticMaxN)
+        return set_error(FORGE_ERR_CAPACITY, "forge_sort_pairs_static: n=%llu exceeds the static maximum %llu",
+                         (unsigned long long)n, (unsigned long long)kStaticMaxN);
+    if (begin_bit >= end_bit || end_bit > 32)
+        return set_error(FORGE_ERR_INVALID_ARG, "forge_sort_pairs_static: bad bit range [%u, %u)", begin_bit,
+                         end_bit);
+    if (n == 0) return FORGE_OK;
+    if (!keys || !vals) return set_error(FORGE_ERR_INVALID_ARG, "forge_sort_pairs_static: keys/vals NULL");
+    int dev = 0;
+    FORGE_CUDA(cudaGetDevice(&dev));
+    uint32_t* base = nullptr;
+    int rc = static_scratch(dev, &base);
+    if (rc != FORGE_OK) return rc;
+    SortScratch s;
+    s.meta = base;
+    s.status = base + kStaticMetaWords;
+    s.max_tiles = (uint32_t)kStaticTiles;
+    s.sms = num_sms(dev);
+    uint32_t* ka = s.status + kStaticStatusWords;
+    uint32_t* va = ka + kStaticMaxN;
+    cudaStream_t st = as_stream(stream);
+    int where = 0;
+    // run_onesweep clears the histograms and tile counters (memset) and the
+    // look-back table (histogram kernel) left by the previous call.
+    rc = run_onesweep(s, radix::KeysFromArray{keys}, keys, vals, ka, va, keys, vals, (uint32_t)n, begin_bit,
+                      end_bit, st, &where);
+    if (rc != FORGE_OK) return rc;
+    if (where == 0) {  // odd pass count: result is in the static alternate pair
+        FORGE_CUDA(cudaMemcpyAsync(keys, ka, n * 4, cudaMemcpyDeviceToDevice, st));
+        FORGE_CUDA(cudaMemcpyAsync(vals, va, n * 4, cudaMemcpyDeviceToDevice, st));
     }
     return FORGE_OK;
 }

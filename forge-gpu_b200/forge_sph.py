@@ -61,7 +61,9 @@ EXPORTED = (
     "forge_grid_check", "forge_grid_destroy",
     "forge_sph_density", "forge_sph_force", "forge_sph_step",
     "forge_grid_profile_enable", "forge_grid_profile_read",
+    "forge_sort_pairs_static",
 )
+STATIC_SORT_MAX_N = 1 << 20
 
 
 class ForgeError(RuntimeError):
@@ -115,6 +117,7 @@ def lib() -> ctypes.CDLL:
         "forge_sph_step": (i32, [vp, ctypes.POINTER(SphParams), ctypes.POINTER(StepParams), vp, vp, vp, vp, vp,
                                  vp, vp, u64, vp]),
         "forge_grid_profile_enable": (i32, [vp, u32]),
+        "forge_sort_pairs_static": (i32, [vp, vp, u64, u32, u32, vp]),
         "forge_grid_profile_read": (i32, [vp, ctypes.POINTER(f32), u32, ctypes.POINTER(u32)]),
     }
     for name, (res, args) in sig.items():

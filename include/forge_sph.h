@@ -93,6 +93,28 @@ FORGE_API int forge_sorter_sort_pairs(forge_sorter* s, uint32_t* keys, uint32_t*
                             uint32_t begin_bit, uint32_t end_bit,
                             int* result_in_alt, void* stream);
 
+/* Stable key/value sort that allocates nothing. No counterpart in the
+ * reference: this entry point exists for callers that cannot call
+ * cudaMalloc -- hosts that fix their device-memory budget at start-up,
+ * plug-in hosts whose allocator belongs to someone else, and latency-critical
+ * loops where an allocation's implicit device synchronisation is not
+ * acceptable. Same result as forge_sorter_sort_pairs with NULL alternate
+ * buffers (sorted data left in keys/vals), for n <= FORGE_STATIC_SORT_MAX_N.
+ *
+ * Its scratch (look-back table, digit histograms, one alternate key/value
+ * pair) is a fixed ~8.3 MiB array inside the library that every GPU which
+ * loads the library holds until process exit. Runs on the calling thread's
+ * current device. The first call on a device looks the array up (once per
+ * device): make that first call before any stream capture. All calls share
+ * the array, so calls whose work overlaps on the GPU (different streams, or
+ * different host threads on one device) race; serialise them. A device-side
+ * wait that gives up is not reported by this entry point (use the
+ * handle-based sorter and forge_sorter_check when that matters).
+ * Returns FORGE_ERR_CAPACITY for n > FORGE_STATIC_SORT_MAX_N. */
+#define FORGE_STATIC_SORT_MAX_N (1ull << 20)
+FORGE_API int forge_sort_pairs_static(uint32_t* keys, uint32_t* vals, uint64_t n, uint32_t begin_bit,
+                                      uint32_t end_bit, void* stream);
+
 /* Synchronise `stream` and report any device-side failure of this sorter
  * (FORGE_ERR_TIMEOUT if a look-back wait gave up). Clears the status. */
 FORGE_API int forge_sorter_check(forge_sorter* s, void* stream);
