@@ -8,8 +8,8 @@
 //  * One up-front kernel builds the digit histograms of every pass at once
 //    (one read of the keys), so each pass is a single kernel.
 //  * Each pass kernel takes a tile of kTile keys, ranks them inside the tile
-//    with warp-level __match_any_sync (stable: item-major, lane-minor order is
-//    the input order), finds the tile's global offset per digit with a
+//    with warp-level digit matching from bit-sliced ballots (stable:
+//    item-major, lane-minor order is the input order), finds the tile's global offset per digit with a
 //    decoupled look-back over earlier tiles (bounded waits), stages the
 //    digit-sorted tile in shared memory and writes it out coalesced.
 //  * Tile ids come from an atomic counter, so every tile a CTA waits on
@@ -44,6 +44,20 @@ __host__ __device__ constexpr uint32_t num_tiles(uint64_t n) {
     return (uint32_t)((n + kTile - 1) / kTile);
 }
 
+// Lanes of the warp holding the same 8-bit digit as this lane, from eight
+// ballots (bit slicing); cheaper than the MATCH instruction on this part.
+// Lanes with valid == false are excluded from every lane's mask.
+__device__ __forceinline__ uint32_t warp_same_digit(uint32_t d, bool valid) {
+    uint32_t peers = __ballot_sync(0xffffffffu, valid);
+#pragma unroll
+    for (int b = 0; b < kRadixBits; ++b) {
+        const bool bit = (d >> b) & 1u;
+        const uint32_t v = __ballot_sync(0xffffffffu, bit);
+        peers &= bit ? v : ~v;
+    }
+    return peers;
+}
+
 // Digit of `key` for a pass starting at `shift` with `bits` bits.
 __device__ __forceinline__ uint32_t digit_of(uint32_t key, uint32_t shift, uint32_t mask) {
     return (key >> shift) & mask;
@@ -60,17 +74,20 @@ struct KeysFromArray {
 // ---------------------------------------------------------------------------
 // Up-front histogram: hist[p*256 + d] += #keys whose pass-p digit is d, for
 // every pass p. Also zeroes the look-back status table used by the passes.
-// Each block keeps a shared histogram; updates are warp-aggregated with
-// __match_any_sync so low-entropy digits (cell keys of spatially ordered
-// particles) do not serialise on one shared address.
+// Each warp keeps its own shared histograms; a warp whose 32 keys share a
+// digit (common for cell keys of spatially ordered particles) adds 32 once
+// instead of serialising 32 atomics on one shared address.
 // ---------------------------------------------------------------------------
 template <class Src>
 __global__ void __launch_bounds__(kHistThreads)
     digit_histogram_kernel(Src src, uint32_t n, uint32_t begin_bit, uint32_t end_bit,
                            uint32_t passes, uint32_t* __restrict__ hist,
                            uint4* __restrict__ status, uint32_t status_vec4) {
-    __shared__ uint32_t s_hist[kMaxPasses * kRadix];
-    for (uint32_t j = threadIdx.x; j < kMaxPasses * kRadix; j += kHistThreads) s_hist[j] = 0;
+    constexpr int kW = kHistThreads / 32;
+    // Per-warp histograms: a warp's shared atomics only contend with itself.
+    __shared__ uint32_t s_hist[kW][kMaxPasses * kRadix];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (uint32_t j = threadIdx.x; j < kW * kMaxPasses * kRadix; j += kHistThreads) (&s_hist[0][0])[j] = 0;
 
     const uint32_t stride = gridDim.x * kHistThreads;
     const uint4 zero = make_uint4(0, 0, 0, 0);
@@ -78,7 +95,7 @@ __global__ void __launch_bounds__(kHistThreads)
         status[j] = zero;
     __syncthreads();
 
-    const uint32_t lane_lt = lanemask_lt();
+    uint32_t* wh = s_hist[warp];
     for (uint32_t base = blockIdx.x * kHistThreads; base < n; base += stride) {
         const uint32_t i = base + threadIdx.x;
         const bool valid = i < n;
@@ -86,15 +103,23 @@ __global__ void __launch_bounds__(kHistThreads)
         for (uint32_t p = 0; p < passes; ++p) {
             const uint32_t shift = begin_bit + p * kRadixBits;
             const uint32_t bits = min((uint32_t)kRadixBits, end_bit - shift);
-            const uint32_t d = valid ? digit_of(key, shift, (1u << bits) - 1u) : 0xffffu;
-            const uint32_t peers = __match_any_sync(0xffffffffu, d);
-            if (valid && (peers & lane_lt) == 0)
-                atomicAdd(&s_hist[p * kRadix + d], (uint32_t)__popc(peers));
+            const uint32_t d = digit_of(key, shift, (1u << bits) - 1u);
+            // Spatially ordered cell keys often give a whole warp one digit:
+            // one add of 32 instead of 32 conflicting atomics.
+            const uint32_t d0 = __shfl_sync(0xffffffffu, d, 0);
+            if (__all_sync(0xffffffffu, valid && d == d0)) {
+                if (lane == 0) wh[p * kRadix + d0] += 32u;
+            } else if (valid) {
+                atomicAdd(&wh[p * kRadix + d], 1u);
+            }
+            __syncwarp();
         }
     }
     __syncthreads();
     for (uint32_t j = threadIdx.x; j < passes * kRadix; j += kHistThreads) {
-        const uint32_t c = s_hist[j];
+        uint32_t c = 0;
+#pragma unroll
+        for (int w = 0; w < kW; ++w) c += s_hist[w][j];
         if (c) atomicAdd(&hist[j], c);
     }
 }
@@ -104,7 +129,7 @@ __global__ void __launch_bounds__(kHistThreads)
 // pass of the grid build), vals_in is not read.
 // ---------------------------------------------------------------------------
 template <bool IOTA>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 3)
     onesweep_pass_kernel(const uint32_t* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
                          uint32_t* __restrict__ keys_out, uint32_t* __restrict__ vals_out,
                          uint32_t n, uint32_t shift, uint32_t bits,
@@ -148,8 +173,8 @@ __global__ void __launch_bounds__(kThreads)
     for (int k = 0; k < kItems; ++k) {
         const uint32_t idx = warp_start + k * 32 + lane;
         const bool ok = idx < n;
-        const uint32_t d = ok ? digit_of(key[k], shift, mask) : 0xffffu;
-        const uint32_t peers = __match_any_sync(0xffffffffu, d);
+        const uint32_t d = digit_of(key[k], shift, mask);
+        const uint32_t peers = warp_same_digit(d, ok);
         uint32_t before = 0;
         if (ok) before = s_whist[warp][d];
         __syncwarp();
