@@ -124,7 +124,7 @@ int run_onesweep(const SortScratch& s, Src src, const uint32_t* keys0, const uin
     FORGE_CUDA(cudaMemsetAsync(s.meta, 0, kMetaErr * sizeof(uint32_t), st));
     const uint32_t status_vec4 = (uint32_t)(((size_t)tiles * radix::kRadix + 3) / 4);
     const uint32_t hblocks =
-        std::max(1u, std::min(grid_blocks(n, radix::kHistThreads), (uint32_t)s.sms * 8u));
+        std::max(1u, std::min(grid_blocks(n, radix::kHistThreads * radix::kHistItems), (uint32_t)s.sms * 8u));
     radix::digit_histogram_kernel<Src><<<hblocks, radix::kHistThreads, 0, st>>>(
         src, n, begin_bit, end_bit, passes, s.meta, reinterpret_cast<uint4*>(s.status), status_vec4);
     FORGE_LAUNCHED();
@@ -551,17 +551,26 @@ constexpr uint32_t kSphThreads = 128;
 
 int launch_density(forge_grid* g, const forge_sph_params* p, float* density, cudaStream_t st) {
     if (g->n == 0) return FORGE_OK;
-    sph::density_kernel<<<grid_blocks(g->n, kSphThreads), kSphThreads, 0, st>>>(
+    sph::density_pair_kernel<<<grid_blocks((g->n + 1) / 2, kSphThreads), kSphThreads, 0, st>>>(
         g->pos4, g->cell_start, g->sorted_idx, (uint32_t)g->n, geom_of(g), make_consts(p), g->vel4, g->aux, density);
     FORGE_LAUNCHED();
     return FORGE_OK;
 }
 
+// Two particles per thread pay off when cells are sparse (the candidate scan
+// dominates); with dense cells the per-hit work dominates and one particle
+// per thread diverges less. Mean occupancy n / C selects the kernel.
+constexpr double kPairMaxOccupancy = 8.0;
+
 template <int TERMS, int EPI>
 void launch_force_t(forge_grid* g, const sph::SphConsts& c, const sph::StepEpi& ep, const sph::ForceOut& o,
                     cudaStream_t st) {
-    sph::force_kernel<TERMS, EPI><<<grid_blocks(g->n, kSphThreads), kSphThreads, 0, st>>>(
-        g->pos4, g->vel4, g->aux, g->cell_start, g->sorted_idx, (uint32_t)g->n, geom_of(g), c, ep, o);
+    if ((double)g->n / (double)g->C < kPairMaxOccupancy)
+        sph::force_kernel<TERMS, EPI><<<grid_blocks((g->n + 1) / 2, kSphThreads), kSphThreads, 0, st>>>(
+            g->pos4, g->vel4, g->aux, g->cell_start, g->sorted_idx, (uint32_t)g->n, geom_of(g), c, ep, o);
+    else
+        sph::force_single_kernel<TERMS, EPI><<<grid_blocks(g->n, kSphThreads), kSphThreads, 0, st>>>(
+            g->pos4, g->vel4, g->aux, g->cell_start, g->sorted_idx, (uint32_t)g->n, geom_of(g), c, ep, o);
 }
 
 }  // namespace

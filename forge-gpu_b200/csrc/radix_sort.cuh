@@ -39,6 +39,7 @@ constexpr uint32_t kCountMask = (1u << 29) - 1;
 constexpr uint64_t kMaxN = (1ull << 29) - 1;
 
 constexpr int kHistThreads = 256;
+constexpr int kHistItems = 8;
 
 __host__ __device__ constexpr uint32_t num_tiles(uint64_t n) {
     return (uint32_t)((n + kTile - 1) / kTile);
@@ -96,23 +97,31 @@ __global__ void __launch_bounds__(kHistThreads)
     __syncthreads();
 
     uint32_t* wh = s_hist[warp];
-    for (uint32_t base = blockIdx.x * kHistThreads; base < n; base += stride) {
-        const uint32_t i = base + threadIdx.x;
-        const bool valid = i < n;
-        const uint32_t key = valid ? src(i) : 0u;
-        for (uint32_t p = 0; p < passes; ++p) {
-            const uint32_t shift = begin_bit + p * kRadixBits;
-            const uint32_t bits = min((uint32_t)kRadixBits, end_bit - shift);
-            const uint32_t d = digit_of(key, shift, (1u << bits) - 1u);
-            // Spatially ordered cell keys often give a whole warp one digit:
-            // one add of 32 instead of 32 conflicting atomics.
-            const uint32_t d0 = __shfl_sync(0xffffffffu, d, 0);
-            if (__all_sync(0xffffffffu, valid && d == d0)) {
-                if (lane == 0) wh[p * kRadix + d0] += 32u;
-            } else if (valid) {
-                atomicAdd(&wh[p * kRadix + d], 1u);
+    // kHistItems independent loads per thread in flight before any counting.
+    for (uint32_t base = blockIdx.x * kHistThreads * kHistItems; base < n; base += stride * kHistItems) {
+        uint32_t key[kHistItems];
+#pragma unroll
+        for (int k = 0; k < kHistItems; ++k) {
+            const uint32_t i = base + k * kHistThreads + threadIdx.x;
+            key[k] = i < n ? src(i) : 0u;
+        }
+#pragma unroll
+        for (int k = 0; k < kHistItems; ++k) {
+            const bool valid = base + k * kHistThreads + threadIdx.x < n;
+            for (uint32_t p = 0; p < passes; ++p) {
+                const uint32_t shift = begin_bit + p * kRadixBits;
+                const uint32_t bits = min((uint32_t)kRadixBits, end_bit - shift);
+                const uint32_t d = digit_of(key[k], shift, (1u << bits) - 1u);
+                // Spatially ordered cell keys often give a whole warp one digit:
+                // one add of 32 instead of 32 conflicting atomics.
+                const uint32_t d0 = __shfl_sync(0xffffffffu, d, 0);
+                if (__all_sync(0xffffffffu, valid && d == d0)) {
+                    if (lane == 0) wh[p * kRadix + d0] += 32u;
+                } else if (valid) {
+                    atomicAdd(&wh[p * kRadix + d], 1u);
+                }
+                __syncwarp();
             }
-            __syncwarp();
         }
     }
     __syncthreads();

@@ -66,13 +66,21 @@ __device__ __forceinline__ float gap2(float raw, float slack) {
     return g * g;
 }
 
-// Calls f(b, e) for each trimmed contiguous candidate range of particle p
-// (cell-ordered indices), in reference order.
-template <class F>
-__device__ __forceinline__ void for_each_range(const float4& p, const Geom& g, const uint32_t* __restrict__ cell_start,
-                                               float H, F&& f) {
+// A particle's cell and its trimmed search window, packed: for row
+// r = (dz+1)*3 + (dy+1), bit 3r = row visited, bit 3r+1 = window starts at
+// cx-1 (else cx), bit 3r+2 = window ends after cx+1 (else after cx).
+struct Window {
     int cx, cy, cz;
-    key_to_cell(__float_as_uint(p.w), g, cx, cy, cz);
+    uint32_t bits;
+    __device__ __forceinline__ bool on(int r) const { return (bits >> (3 * r)) & 1u; }
+    __device__ __forceinline__ int lo(int r) const { return cx - (int)((bits >> (3 * r + 1)) & 1u); }
+    __device__ __forceinline__ int hi(int r) const { return cx + 1 + (int)((bits >> (3 * r + 2)) & 1u); }
+};
+
+__device__ __forceinline__ Window make_window(const float4& p, const Geom& g, float H) {
+    Window w;
+    key_to_cell(__float_as_uint(p.w), g, w.cx, w.cy, w.cz);
+    const int cx = w.cx, cy = w.cy, cz = w.cz;
     const float bx = g.ox + (float)cx * g.cs, by = g.oy + (float)cy * g.cs, bz = g.oz + (float)cz * g.cs;
     const float sx = 4e-7f * (fabsf(p.x) + fabsf(bx) + g.cs);
     const float sy = 4e-7f * (fabsf(p.y) + fabsf(by) + g.cs);
@@ -80,20 +88,39 @@ __device__ __forceinline__ void for_each_range(const float4& p, const Geom& g, c
     const float gxl = gap2(p.x - bx, sx), gxr = gap2(bx + g.cs - p.x, sx);
     const float gyl = gap2(p.y - by, sy), gyr = gap2(by + g.cs - p.y, sy);
     const float gzl = gap2(p.z - bz, sz), gzr = gap2(bz + g.cs - p.z, sz);
-    for (int dz = -1; dz <= 1; ++dz) {
-        const int z = cz + dz;
-        if (z < 0 || z >= g.nz) continue;
-        const float gz = dz < 0 ? gzl : (dz > 0 ? gzr : 0.f);
-        for (int dy = -1; dy <= 1; ++dy) {
-            const int y = cy + dy;
-            if (y < 0 || y >= g.ny) continue;
-            const float base = gz + (dy < 0 ? gyl : (dy > 0 ? gyr : 0.f));
-            if (base > H) continue;
-            const int lo = (cx > 0 && base + gxl <= H) ? cx - 1 : cx;
-            const int hi = (cx < g.nx - 1 && base + gxr <= H) ? cx + 2 : cx + 1;
-            const uint32_t row = ((uint32_t)z * (uint32_t)g.ny + (uint32_t)y) * (uint32_t)g.nx;
-            f(__ldg(cell_start + row + lo), __ldg(cell_start + row + hi));
-        }
+    uint32_t bits = 0;
+#pragma unroll
+    for (int r = 0; r < 9; ++r) {
+        const int dz = r / 3 - 1, dy = r % 3 - 1;
+        const int z = cz + dz, y = cy + dy;
+        const float base = (dz < 0 ? gzl : (dz > 0 ? gzr : 0.f)) + (dy < 0 ? gyl : (dy > 0 ? gyr : 0.f));
+        const bool on = z >= 0 && z < g.nz && y >= 0 && y < g.ny && base <= H;
+        const bool l = cx > 0 && base + gxl <= H;
+        const bool rr = cx < g.nx - 1 && base + gxr <= H;
+        bits |= (on ? 1u : 0u) << (3 * r);
+        bits |= (l ? 1u : 0u) << (3 * r + 1);
+        bits |= (rr ? 1u : 0u) << (3 * r + 2);
+    }
+    w.bits = bits;
+    return w;
+}
+
+__device__ __forceinline__ uint32_t row_base(const Geom& g, int cy, int cz, int r) {
+    const int dz = r / 3 - 1, dy = r % 3 - 1;
+    return ((uint32_t)(cz + dz) * (uint32_t)g.ny + (uint32_t)(cy + dy)) * (uint32_t)g.nx;
+}
+
+// Calls f(b, e) for each trimmed contiguous candidate range of particle p
+// (cell-ordered indices), in reference order.
+template <class F>
+__device__ __forceinline__ void for_each_range(const float4& p, const Geom& g, const uint32_t* __restrict__ cell_start,
+                                               float H, F&& f) {
+    const Window w = make_window(p, g, H);
+#pragma unroll
+    for (int r = 0; r < 9; ++r) {
+        if (!w.on(r)) continue;
+        const uint32_t row = row_base(g, w.cy, w.cz, r);
+        f(__ldg(cell_start + row + w.lo(r)), __ldg(cell_start + row + w.hi(r)));
     }
 }
 
@@ -111,32 +138,100 @@ __device__ __forceinline__ void density_derived(float rho, const SphConsts& c, f
 // the sum equals the reference's branchy one. Writes 1/rho to vel4[s].w, aux[s]
 // and, if given, density_out[i] (original order).
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(128)
-    density_kernel(const float4* __restrict__ pos4, const uint32_t* __restrict__ cell_start,
-                   const uint32_t* __restrict__ sorted_idx, uint32_t n, Geom g, SphConsts c,
-                   float4* __restrict__ vel4, float2* __restrict__ aux, float* __restrict__ density_out) {
-    const uint32_t s = blockIdx.x * blockDim.x + threadIdx.x;
-    if (s >= n) return;
-    const float4 pi = pos4[s];
-    float rho = 0.f;
-    for_each_range(pi, g, cell_start, c.h2_skip, [&](uint32_t b, uint32_t e) {
+// Poly6 contributions of candidates [b, e) to one or two particles.
+__device__ __forceinline__ void poly6_one(const float4* __restrict__ pos4, uint32_t b, uint32_t e, const float4& p,
+                                          const SphConsts& c, float& rho) {
 #pragma unroll 4
-        for (uint32_t j = b; j < e; ++j) {
-            const float4 q = __ldg(pos4 + j);
-            const float dx = pi.x - q.x, dy = pi.y - q.y, dz = pi.z - q.z;
-            const float r2 = dx * dx + dy * dy + dz * dz;
-            const float d = fmaxf(c.h2 - r2, 0.f);
-            rho += c.mass_poly6 * d * d * d;
+    for (uint32_t j = b; j < e; ++j) {
+        const float4 q = __ldg(pos4 + j);
+        const float dx = p.x - q.x, dy = p.y - q.y, dz = p.z - q.z;
+        const float d = fmaxf(c.h2 - (dx * dx + dy * dy + dz * dz), 0.f);
+        rho += c.mass_poly6 * d * d * d;
+    }
+}
+
+__device__ __forceinline__ void poly6_two(const float4* __restrict__ pos4, uint32_t b, uint32_t e, const float4& p0,
+                                          const float4& p1, const SphConsts& c, float& rho0, float& rho1) {
+#pragma unroll 2
+    for (uint32_t j = b; j < e; ++j) {
+        const float4 q = __ldg(pos4 + j);
+        const float ax = p0.x - q.x, ay = p0.y - q.y, az = p0.z - q.z;
+        const float bx = p1.x - q.x, by = p1.y - q.y, bz = p1.z - q.z;
+        const float d0 = fmaxf(c.h2 - (ax * ax + ay * ay + az * az), 0.f);
+        const float d1 = fmaxf(c.h2 - (bx * bx + by * by + bz * bz), 0.f);
+        rho0 += c.mass_poly6 * d0 * d0 * d0;
+        rho1 += c.mass_poly6 * d1 * d1 * d1;
+    }
+}
+
+// Density, two consecutive cell-ordered particles per thread: each neighbour
+// load feeds two pair evaluations (the one-particle walk is bound by L1
+// wavefronts, not arithmetic). Same cell: walk the union of both trimmed
+// windows -- every extra candidate lies in the other particle's untrimmed
+// window and was trimmed only because it cannot be within h, so it adds +0,
+// exactly as in the reference. Adjacent cells of one row: walk three
+// segments (first only, both, second only) of their ordered ranges.
+// Different rows: two single walks. Each particle's sum keeps the reference
+// order.
+__global__ void __launch_bounds__(128)
+    density_pair_kernel(const float4* __restrict__ pos4, const uint32_t* __restrict__ cell_start,
+                        const uint32_t* __restrict__ sorted_idx, uint32_t n, Geom g, SphConsts c,
+                        float4* __restrict__ vel4, float2* __restrict__ aux, float* __restrict__ density_out) {
+    const uint32_t s0 = 2u * (blockIdx.x * blockDim.x + threadIdx.x);
+    if (s0 >= n) return;
+    const bool has1 = s0 + 1 < n;
+    const float4 p0 = pos4[s0];
+    const float4 p1 = has1 ? pos4[s0 + 1] : p0;
+    const Window w0 = make_window(p0, g, c.h2_skip);
+    const Window w1 = make_window(p1, g, c.h2_skip);
+    float rho0 = 0.f, rho1 = 0.f;
+    if (has1 && w0.cy == w1.cy && w0.cz == w1.cz) {
+        const bool same_cell = w0.cx == w1.cx;
+#pragma unroll
+        for (int r = 0; r < 9; ++r) {
+            const bool e0 = w0.on(r), e1 = w1.on(r);
+            if (!e0 && !e1) continue;
+            const uint32_t row = row_base(g, w0.cy, w0.cz, r);
+            if (same_cell) {
+                const int lo = e0 ? (e1 ? min(w0.lo(r), w1.lo(r)) : w0.lo(r)) : w1.lo(r);
+                const int hi = e0 ? (e1 ? max(w0.hi(r), w1.hi(r)) : w0.hi(r)) : w1.hi(r);
+                poly6_two(pos4, __ldg(cell_start + row + lo), __ldg(cell_start + row + hi), p0, p1, c, rho0, rho1);
+            } else {
+                // cx0 < cx1, so lb0 <= lb1 and le0 <= le1 for the trimmed ranges.
+                uint32_t lb0 = e0 ? __ldg(cell_start + row + w0.lo(r)) : 0u;
+                uint32_t le0 = e0 ? __ldg(cell_start + row + w0.hi(r)) : 0u;
+                uint32_t lb1 = e1 ? __ldg(cell_start + row + w1.lo(r)) : 0u;
+                uint32_t le1 = e1 ? __ldg(cell_start + row + w1.hi(r)) : 0u;
+                if (!e0) lb0 = le0 = lb1;
+                if (!e1) lb1 = le1 = le0;
+                poly6_one(pos4, lb0, min(lb1, le0), p0, c, rho0);
+                if (lb1 < le0) poly6_two(pos4, lb1, le0, p0, p1, c, rho0, rho1);
+                poly6_one(pos4, max(le0, lb1), le1, p1, c, rho1);
+            }
         }
-    });
+    } else {
+        for_each_range(p0, g, cell_start, c.h2_skip,
+                       [&](uint32_t b, uint32_t e) { poly6_one(pos4, b, e, p0, c, rho0); });
+        if (has1)
+            for_each_range(p1, g, cell_start, c.h2_skip,
+                           [&](uint32_t b, uint32_t e) { poly6_one(pos4, b, e, p1, c, rho1); });
+    }
     float inv_rho;
     float2 a;
-    density_derived(rho, c, inv_rho, a);
+    density_derived(rho0, c, inv_rho, a);
     if (vel4 != nullptr) {
-        vel4[s].w = inv_rho;
-        aux[s] = a;
+        vel4[s0].w = inv_rho;
+        aux[s0] = a;
     }
-    if (density_out != nullptr) density_out[sorted_idx[s]] = rho;
+    if (density_out != nullptr) density_out[sorted_idx[s0]] = rho0;
+    if (has1) {
+        density_derived(rho1, c, inv_rho, a);
+        if (vel4 != nullptr) {
+            vel4[s0 + 1].w = inv_rho;
+            aux[s0 + 1] = a;
+        }
+        if (density_out != nullptr) density_out[sorted_idx[s0 + 1]] = rho1;
+    }
 }
 
 // vel4[s] = (vx[i], vy[i], vz[i], 1/rho[i]), aux[s] = (p/rho, rho), i = svals[s]
@@ -195,77 +290,109 @@ struct StepEpi {
     uint32_t flags;  // FORGE_STEP_* bits
 };
 
-template <int TERMS, int EPI>
-__global__ void __launch_bounds__(128)
-    force_kernel(const float4* __restrict__ pos4, const float4* __restrict__ vel4, const float2* __restrict__ aux,
-                 const uint32_t* __restrict__ cell_start, const uint32_t* __restrict__ sorted_idx, uint32_t n, Geom g,
-                 SphConsts c, StepEpi ep, ForceOut out) {
-    const uint32_t s = blockIdx.x * blockDim.x + threadIdx.x;
-    if (s >= n) return;
-    const float4 pi = pos4[s];
-    const float4 vi = vel4[s];
-    const float rho_i = aux[s].y;
-    const bool valid = !(rho_i < 1e-6f);
-    const float p_i = c.k * (rho_i - c.rho0);
-    const float* __restrict__ pj_over_rho = reinterpret_cast<const float*>(aux);
+// One particle's state in the force pass.
+struct ForceAcc {
+    float4 p;   // position, w = bits(cell key)
+    float4 v;   // velocity, w = 1/rho
+    float pres; // p_i = k (rho_i - rho0)
+    float pax, pay, paz, vax, vay, vaz;
+};
 
-    float pax = 0.f, pay = 0.f, paz = 0.f;
-    float vax = 0.f, vay = 0.f, vaz = 0.f;
-    if (valid) {
-        for_each_range(pi, g, cell_start, c.h2_skip, [&](uint32_t b, uint32_t e) {
-            for (uint32_t j0 = b; j0 < e; j0 += 32) {
-                const uint32_t cnt = min(32u, e - j0);
-                // Phase 1: which of the next <= 32 candidates are in range.
-                uint32_t hit = 0;
-#pragma unroll 4
-                for (uint32_t k = 0; k < cnt; ++k) {
-                    const float4 q = __ldg(pos4 + j0 + k);
-                    const float dx = pi.x - q.x, dy = pi.y - q.y, dz = pi.z - q.z;
-                    const float r2 = dx * dx + dy * dy + dz * dz;
-                    hit |= (r2 < c.h2 && r2 > 1e-12f) ? (1u << k) : 0u;
-                }
-                // Phase 2: pair terms for the hits, ascending j.
-                while (hit) {
-                    const uint32_t j = j0 + (uint32_t)(__ffs(hit) - 1);
-                    hit &= hit - 1;
-                    const float4 q = __ldg(pos4 + j);
-                    const float4 vj = __ldg(vel4 + j);
-                    const float djx = pi.x - q.x, djy = pi.y - q.y, djz = pi.z - q.z;
-                    const float r2 = __fadd_rn(__fadd_rn(__fmul_rn(djx, djx), __fmul_rn(djy, djy)),
-                                               __fmul_rn(djz, djz));
-                    const float diff = c.h - sqrtf(r2);
-                    const float inv_rho_j = vj.w;
-                    if (TERMS & 1) {
-                        const float pp = fmaf(p_i, inv_rho_j, __ldg(pj_over_rho + 2 * j));
-                        const float f = c.kp * pp * (diff * diff) * rsqrtf(r2);
-                        pax = fmaf(f, djx, pax);
-                        pay = fmaf(f, djy, pay);
-                        paz = fmaf(f, djz, paz);
-                    }
-                    if (TERMS & 2) {
-                        const float v = c.kv * inv_rho_j * diff;
-                        vax = fmaf(v, vj.x - vi.x, vax);
-                        vay = fmaf(v, vj.y - vi.y, vay);
-                        vaz = fmaf(v, vj.z - vi.z, vaz);
-                    }
-                }
-            }
-        });
+__device__ __forceinline__ ForceAcc force_acc(const float4* __restrict__ pos4, const float4* __restrict__ vel4,
+                                              const float2* __restrict__ aux, uint32_t s, const SphConsts& c) {
+    ForceAcc A;
+    A.p = pos4[s];
+    A.v = vel4[s];
+    A.pres = c.k * (aux[s].y - c.rho0);
+    A.pax = A.pay = A.paz = A.vax = A.vay = A.vaz = 0.f;
+    return A;
+}
+
+__device__ __forceinline__ uint32_t in_range_bit(const float4& p, const float4& q, const SphConsts& c, uint32_t k) {
+    const float dx = p.x - q.x, dy = p.y - q.y, dz = p.z - q.z;
+    const float r2 = dx * dx + dy * dy + dz * dz;
+    return (r2 < c.h2 && r2 > 1e-12f) ? (1u << k) : 0u;
+}
+
+// Pair terms of the hits (bit k = candidate j0 + k), ascending j.
+template <int TERMS>
+__device__ __forceinline__ void force_hits(const float4* __restrict__ pos4, const float4* __restrict__ vel4,
+                                           const float* __restrict__ pj_over_rho, uint32_t j0, uint32_t hit,
+                                           ForceAcc& A, const SphConsts& c) {
+    while (hit) {
+        const uint32_t j = j0 + (uint32_t)(__ffs(hit) - 1);
+        hit &= hit - 1;
+        const float4 q = __ldg(pos4 + j);
+        const float4 vj = __ldg(vel4 + j);
+        const float djx = A.p.x - q.x, djy = A.p.y - q.y, djz = A.p.z - q.z;
+        const float r2 = __fadd_rn(__fadd_rn(__fmul_rn(djx, djx), __fmul_rn(djy, djy)), __fmul_rn(djz, djz));
+        const float diff = c.h - sqrtf(r2);
+        const float inv_rho_j = vj.w;
+        if (TERMS & 1) {
+            const float pp = fmaf(A.pres, inv_rho_j, __ldg(pj_over_rho + 2 * j));
+            const float f = c.kp * pp * (diff * diff) * rsqrtf(r2);
+            A.pax = fmaf(f, djx, A.pax);
+            A.pay = fmaf(f, djy, A.pay);
+            A.paz = fmaf(f, djz, A.paz);
+        }
+        if (TERMS & 2) {
+            const float v = c.kv * inv_rho_j * diff;
+            A.vax = fmaf(v, vj.x - A.v.x, A.vax);
+            A.vay = fmaf(v, vj.y - A.v.y, A.vay);
+            A.vaz = fmaf(v, vj.z - A.v.z, A.vaz);
+        }
     }
+}
 
-    // a = (a_p + a_v) / rho_i (sph_fused.rs:633-638).
+// Candidates [b, e) for one particle: scan 32 at a time for r^2 < h^2, then
+// evaluate only the hits.
+template <int TERMS>
+__device__ __forceinline__ void force_one(const float4* __restrict__ pos4, const float4* __restrict__ vel4,
+                                          const float* __restrict__ pj, uint32_t b, uint32_t e, ForceAcc& A,
+                                          const SphConsts& c) {
+    for (uint32_t j0 = b; j0 < e; j0 += 32) {
+        const uint32_t cnt = min(32u, e - j0);
+        uint32_t hit = 0;
+#pragma unroll 4
+        for (uint32_t k = 0; k < cnt; ++k) hit |= in_range_bit(A.p, __ldg(pos4 + j0 + k), c, k);
+        force_hits<TERMS>(pos4, vel4, pj, j0, hit, A, c);
+    }
+}
+
+// Candidates [b, e) for two particles: one load per candidate in the scan.
+template <int TERMS>
+__device__ __forceinline__ void force_two(const float4* __restrict__ pos4, const float4* __restrict__ vel4,
+                                          const float* __restrict__ pj, uint32_t b, uint32_t e, ForceAcc& A,
+                                          ForceAcc& B, const SphConsts& c) {
+    for (uint32_t j0 = b; j0 < e; j0 += 32) {
+        const uint32_t cnt = min(32u, e - j0);
+        uint32_t ha = 0, hb = 0;
+#pragma unroll 2
+        for (uint32_t k = 0; k < cnt; ++k) {
+            const float4 q = __ldg(pos4 + j0 + k);
+            ha |= in_range_bit(A.p, q, c, k);
+            hb |= in_range_bit(B.p, q, c, k);
+        }
+        force_hits<TERMS>(pos4, vel4, pj, j0, ha, A, c);
+        force_hits<TERMS>(pos4, vel4, pj, j0, hb, B, c);
+    }
+}
+
+// a = (a_p + a_v) / rho_i (sph_fused.rs:633-638), then the velocity update
+// or the manifest step epilogue, written in original order.
+template <int EPI>
+__device__ __forceinline__ void force_finish(const ForceAcc& A, uint32_t i, const StepEpi& ep, const ForceOut& out) {
     float ax = 0.f, ay = 0.f, az = 0.f;
-    float vx = vi.x, vy = vi.y, vz = vi.z;
-    if (valid) {
-        const float inv_rho = vi.w;
-        ax = (pax + vax) * inv_rho;
-        ay = (pay + vay) * inv_rho;
-        az = (paz + vaz) * inv_rho;
+    float vx = A.v.x, vy = A.v.y, vz = A.v.z;
+    const float inv_rho = A.v.w;
+    if (inv_rho != 0.f) {  // rho_i >= 1e-6 (sph_fused.rs:550)
+        ax = (A.pax + A.vax) * inv_rho;
+        ay = (A.pay + A.vay) * inv_rho;
+        az = (A.paz + A.vaz) * inv_rho;
         vx += ax * ep.dt;
         vy += ay * ep.dt;
         vz += az * ep.dt;
     }
-    const uint32_t i = sorted_idx[s];
     if (EPI == 0) {
         out.vx[i] = vx;
         out.vy[i] = vy;
@@ -275,40 +402,129 @@ __global__ void __launch_bounds__(128)
             out.ay[i] = ay;
             out.az[i] = az;
         }
-    } else {
-        // GravityModule: gravity.rs:31-34.
-        if (ep.flags & 1u) {
-            vx += ep.gx * ep.dt;
-            vy += ep.gy * ep.dt;
-            vz += ep.gz * ep.dt;
-        }
-        float x = pi.x, y = pi.y, z = pi.z;
-        // IntegrateModule: integrate.rs:16-31.
-        if (ep.flags & 2u) {
-            if (!isfinite(vx)) vx = 0.f;
-            if (!isfinite(vy)) vy = 0.f;
-            if (!isfinite(vz)) vz = 0.f;
-            x += vx * ep.dt;
-            y += vy * ep.dt;
-            z += vz * ep.dt;
-        }
-        // BoxColliderModule: box_collider.rs:36-46.
-        if (ep.flags & 4u) {
-            const float e = ep.restitution;
-            if (x < ep.bmin[0]) { x = ep.bmin[0]; vx = fabsf(vx) * e; }
-            if (x > ep.bmax[0]) { x = ep.bmax[0]; vx = -fabsf(vx) * e; }
-            if (y < ep.bmin[1]) { y = ep.bmin[1]; vy = fabsf(vy) * e; }
-            if (y > ep.bmax[1]) { y = ep.bmax[1]; vy = -fabsf(vy) * e; }
-            if (z < ep.bmin[2]) { z = ep.bmin[2]; vz = fabsf(vz) * e; }
-            if (z > ep.bmax[2]) { z = ep.bmax[2]; vz = -fabsf(vz) * e; }
-        }
-        out.px[i] = x;
-        out.py[i] = y;
-        out.pz[i] = z;
-        out.vx[i] = vx;
-        out.vy[i] = vy;
-        out.vz[i] = vz;
+        return;
     }
+    // GravityModule: gravity.rs:31-34.
+    if (ep.flags & 1u) {
+        vx += ep.gx * ep.dt;
+        vy += ep.gy * ep.dt;
+        vz += ep.gz * ep.dt;
+    }
+    float x = A.p.x, y = A.p.y, z = A.p.z;
+    // IntegrateModule: integrate.rs:16-31.
+    if (ep.flags & 2u) {
+        if (!isfinite(vx)) vx = 0.f;
+        if (!isfinite(vy)) vy = 0.f;
+        if (!isfinite(vz)) vz = 0.f;
+        x += vx * ep.dt;
+        y += vy * ep.dt;
+        z += vz * ep.dt;
+    }
+    // BoxColliderModule: box_collider.rs:36-46.
+    if (ep.flags & 4u) {
+        const float e = ep.restitution;
+        if (x < ep.bmin[0]) { x = ep.bmin[0]; vx = fabsf(vx) * e; }
+        if (x > ep.bmax[0]) { x = ep.bmax[0]; vx = -fabsf(vx) * e; }
+        if (y < ep.bmin[1]) { y = ep.bmin[1]; vy = fabsf(vy) * e; }
+        if (y > ep.bmax[1]) { y = ep.bmax[1]; vy = -fabsf(vy) * e; }
+        if (z < ep.bmin[2]) { z = ep.bmin[2]; vz = fabsf(vz) * e; }
+        if (z > ep.bmax[2]) { z = ep.bmax[2]; vz = -fabsf(vz) * e; }
+    }
+    out.px[i] = x;
+    out.py[i] = y;
+    out.pz[i] = z;
+    out.vx[i] = vx;
+    out.vy[i] = vy;
+    out.vz[i] = vz;
+}
+
+// Force pass, one particle per thread (dense cells, where the hit loop
+// dominates and a second particle would only add divergence).
+template <int TERMS, int EPI>
+__global__ void __launch_bounds__(128)
+    force_single_kernel(const float4* __restrict__ pos4, const float4* __restrict__ vel4,
+                        const float2* __restrict__ aux, const uint32_t* __restrict__ cell_start,
+                        const uint32_t* __restrict__ sorted_idx, uint32_t n, Geom g, SphConsts c, StepEpi ep,
+                        ForceOut out) {
+    const uint32_t s = blockIdx.x * blockDim.x + threadIdx.x;
+    if (s >= n) return;
+    const float* __restrict__ pj = reinterpret_cast<const float*>(aux);
+    ForceAcc A = force_acc(pos4, vel4, aux, s, c);
+    if (A.v.w != 0.f) {
+        const Window w = make_window(A.p, g, c.h2_skip);
+#pragma unroll 1
+        for (int r = 0; r < 9; ++r) {
+            if (!w.on(r)) continue;
+            const uint32_t row = row_base(g, w.cy, w.cz, r);
+            force_one<TERMS>(pos4, vel4, pj, __ldg(cell_start + row + w.lo(r)), __ldg(cell_start + row + w.hi(r)),
+                             A, c);
+        }
+    }
+    force_finish<EPI>(A, sorted_idx[s], ep, out);
+}
+
+// Force pass, two consecutive cell-ordered particles per thread with the same
+// window logic as density_pair_kernel (union walk in one cell, three
+// segments for adjacent cells, two single walks otherwise). A particle with
+// rho < 1e-6 (1/rho stored as 0) walks nothing and keeps its velocity.
+template <int TERMS, int EPI>
+__global__ void __launch_bounds__(128)
+    force_kernel(const float4* __restrict__ pos4, const float4* __restrict__ vel4, const float2* __restrict__ aux,
+                 const uint32_t* __restrict__ cell_start, const uint32_t* __restrict__ sorted_idx, uint32_t n, Geom g,
+                 SphConsts c, StepEpi ep, ForceOut out) {
+    const uint32_t s0 = 2u * (blockIdx.x * blockDim.x + threadIdx.x);
+    if (s0 >= n) return;
+    const bool has1 = s0 + 1 < n;
+    const float* __restrict__ pj = reinterpret_cast<const float*>(aux);
+    ForceAcc A = force_acc(pos4, vel4, aux, s0, c);
+    ForceAcc B = force_acc(pos4, vel4, aux, has1 ? s0 + 1 : s0, c);
+    const bool va = A.v.w != 0.f, vb = has1 && B.v.w != 0.f;
+    const Window w0 = make_window(A.p, g, c.h2_skip);
+    const Window w1 = make_window(B.p, g, c.h2_skip);
+    if (va && vb && w0.cy == w1.cy && w0.cz == w1.cz) {
+        const bool same_cell = w0.cx == w1.cx;
+#pragma unroll 1
+        for (int r = 0; r < 9; ++r) {
+            const bool e0 = w0.on(r), e1 = w1.on(r);
+            if (!e0 && !e1) continue;
+            const uint32_t row = row_base(g, w0.cy, w0.cz, r);
+            if (same_cell) {
+                const int lo = e0 ? (e1 ? min(w0.lo(r), w1.lo(r)) : w0.lo(r)) : w1.lo(r);
+                const int hi = e0 ? (e1 ? max(w0.hi(r), w1.hi(r)) : w0.hi(r)) : w1.hi(r);
+                force_two<TERMS>(pos4, vel4, pj, __ldg(cell_start + row + lo), __ldg(cell_start + row + hi), A, B,
+                                 c);
+            } else {
+                uint32_t lb0 = e0 ? __ldg(cell_start + row + w0.lo(r)) : 0u;
+                uint32_t le0 = e0 ? __ldg(cell_start + row + w0.hi(r)) : 0u;
+                uint32_t lb1 = e1 ? __ldg(cell_start + row + w1.lo(r)) : 0u;
+                uint32_t le1 = e1 ? __ldg(cell_start + row + w1.hi(r)) : 0u;
+                if (!e0) lb0 = le0 = lb1;
+                if (!e1) lb1 = le1 = le0;
+                force_one<TERMS>(pos4, vel4, pj, lb0, min(lb1, le0), A, c);
+                if (lb1 < le0) force_two<TERMS>(pos4, vel4, pj, lb1, le0, A, B, c);
+                force_one<TERMS>(pos4, vel4, pj, max(le0, lb1), le1, B, c);
+            }
+        }
+    } else {
+#pragma unroll 1
+        for (int r = 0; r < 9; ++r) {
+            if (va && w0.on(r)) {
+                const uint32_t row = row_base(g, w0.cy, w0.cz, r);
+                force_one<TERMS>(pos4, vel4, pj, __ldg(cell_start + row + w0.lo(r)),
+                                 __ldg(cell_start + row + w0.hi(r)), A, c);
+            }
+        }
+#pragma unroll 1
+        for (int r = 0; r < 9; ++r) {
+            if (vb && w1.on(r)) {
+                const uint32_t row = row_base(g, w1.cy, w1.cz, r);
+                force_one<TERMS>(pos4, vel4, pj, __ldg(cell_start + row + w1.lo(r)),
+                                 __ldg(cell_start + row + w1.hi(r)), B, c);
+            }
+        }
+    }
+    force_finish<EPI>(A, sorted_idx[s0], ep, out);
+    if (has1) force_finish<EPI>(B, sorted_idx[s0 + 1], ep, out);
 }
 
 }  // namespace sph

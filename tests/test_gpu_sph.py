@@ -116,6 +116,20 @@ def test_force_dense_lattice_dambreak65k(cuda):
     assert_force_close(a_g, a, scale)
 
 
+@pytest.mark.parametrize("terms", [1, 2, 3])
+def test_force_dense_cells_single_particle_path(cuda, terms):
+    """>= 8 particles per cell on average selects the one-particle-per-thread
+    force kernel; it must agree with the oracle like the two-particle one."""
+    cfg = workloads.small("ref65k", 24_000, (10, 10, 10))
+    pos, vel = workloads.uniform_particles(cfg.n, seed=77, lo=-0.02, hi=1.02)
+    rho_g, _, a_g = run_force(cuda, cfg, pos, vel, terms)
+    rho, si, cst = check_density(cfg, pos, rho_g)
+    args = (*pos, *vel, rho, cfg.cell_size, cfg.dims, cst, si, 1e-4)
+    _, a = oracle.force(oparams(cfg), terms, *args, threads=oracle.max_threads())
+    _, scale = oracle.force(oparams(cfg), terms | 4, *args, threads=oracle.max_threads())
+    assert_force_close(a_g, a, scale)
+
+
 def make_step(cfg):
     sp = forge_sph.StepParams()
     sp.dt = cfg.dt
