@@ -682,10 +682,51 @@ extern "C" int forge_sph_force(forge_grid* g, const forge_sph_params* p, uint32_
     FORGE_LAUNCHED();
     sph::StepEpi ep{};
     ep.dt = dt;
-    sph::ForceOut o{vx_out, vy_out, vz_out, ax_out, ay_out, az_out, nullptr, nullptr, nullptr};
+    sph::ForceOut o{vx_out, vy_out, vz_out, ax_out, ay_out, az_out, nullptr, nullptr, nullptr, 0xffffffffu};
     if (terms == 3) launch_force_t<3, 0>(g, c, ep, o, st);
     else if (terms == 1) launch_force_t<1, 0>(g, c, ep, o, st);
     else launch_force_t<2, 0>(g, c, ep, o, st);
+    FORGE_LAUNCHED();
+    return FORGE_OK;
+}
+
+namespace {
+sph::StepEpi epi_of(const forge_step_params* sp) {
+    sph::StepEpi ep{};
+    ep.dt = sp->dt;
+    ep.gx = sp->gravity[0];
+    ep.gy = sp->gravity[1];
+    ep.gz = sp->gravity[2];
+    for (int a = 0; a < 3; ++a) {
+        ep.bmin[a] = sp->box_min[a];
+        ep.bmax[a] = sp->box_max[a];
+    }
+    ep.restitution = sp->restitution;
+    ep.flags = sp->flags;
+    return ep;
+}
+}  // namespace
+
+extern "C" int forge_sph_force_step(forge_grid* g, const forge_sph_params* p, const forge_step_params* sp,
+                                    float* px, float* py, float* pz, float* vx, float* vy, float* vz,
+                                    const float* density, uint64_t n, uint64_t n_update, void* stream) {
+    if (!g || !p || !sp) return set_error(FORGE_ERR_INVALID_ARG, "forge_sph_force_step: NULL grid or params");
+    if (!g->built || g->n != n)
+        return set_error(FORGE_ERR_INVALID_ARG,
+                         "forge_sph_force_step: the grid was not built for these %llu particles (last build: %llu)",
+                         (unsigned long long)n, (unsigned long long)g->n);
+    if (n_update > n) return set_error(FORGE_ERR_INVALID_ARG, "forge_sph_force_step: n_update > n");
+    if (n == 0) return FORGE_OK;
+    if (!px || !py || !pz || !vx || !vy || !vz || !density)
+        return set_error(FORGE_ERR_INVALID_ARG, "forge_sph_force_step: NULL array");
+    FORGE_DEVICE_SCOPE(g->device);
+    cudaStream_t st = as_stream(stream);
+    const sph::SphConsts c = make_consts(p);
+    sph::gather_vel_rho_kernel<<<grid_blocks(n, 256), 256, 0, st>>>(g->sorted_idx, (uint32_t)n, vx, vy, vz, density,
+                                                                    c, g->vel4, g->aux);
+    FORGE_LAUNCHED();
+    sph::ForceOut o{vx, vy, vz, nullptr, nullptr, nullptr, px, py, pz, (uint32_t)n_update};
+    launch_force_t<3, 1>(g, c, epi_of(sp), o, st);
     FORGE_LAUNCHED();
     return FORGE_OK;
 }
@@ -705,18 +746,8 @@ extern "C" int forge_sph_step(forge_grid* g, const forge_sph_params* p, const fo
     rc = launch_density(g, p, density, st);
     if (rc != FORGE_OK) return rc;
     prof_mark(g, 3, st);
-    sph::StepEpi ep{};
-    ep.dt = sp->dt;
-    ep.gx = sp->gravity[0];
-    ep.gy = sp->gravity[1];
-    ep.gz = sp->gravity[2];
-    for (int a = 0; a < 3; ++a) {
-        ep.bmin[a] = sp->box_min[a];
-        ep.bmax[a] = sp->box_max[a];
-    }
-    ep.restitution = sp->restitution;
-    ep.flags = sp->flags;
-    sph::ForceOut o{vx, vy, vz, nullptr, nullptr, nullptr, px, py, pz};
+    const sph::StepEpi ep = epi_of(sp);
+    sph::ForceOut o{vx, vy, vz, nullptr, nullptr, nullptr, px, py, pz, 0xffffffffu};
     launch_force_t<3, 1>(g, make_consts(p), ep, o, st);
     FORGE_LAUNCHED();
     prof_mark(g, 4, st);

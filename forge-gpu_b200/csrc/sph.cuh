@@ -280,6 +280,7 @@ struct ForceOut {
     float* px;  // EPI == 1
     float* py;
     float* pz;
+    uint32_t limit;  // only particles with original index < limit are written
 };
 
 struct StepEpi {
@@ -382,6 +383,7 @@ __device__ __forceinline__ void force_two(const float4* __restrict__ pos4, const
 // or the manifest step epilogue, written in original order.
 template <int EPI>
 __device__ __forceinline__ void force_finish(const ForceAcc& A, uint32_t i, const StepEpi& ep, const ForceOut& out) {
+    if (i >= out.limit) return;
     float ax = 0.f, ay = 0.f, az = 0.f;
     float vx = A.v.x, vy = A.v.y, vz = A.v.z;
     const float inv_rho = A.v.w;
@@ -448,6 +450,8 @@ __global__ void __launch_bounds__(128)
                         ForceOut out) {
     const uint32_t s = blockIdx.x * blockDim.x + threadIdx.x;
     if (s >= n) return;
+    const uint32_t i = sorted_idx[s];
+    if (i >= out.limit) return;  // not updated (a ghost of a sharded run)
     const float* __restrict__ pj = reinterpret_cast<const float*>(aux);
     ForceAcc A = force_acc(pos4, vel4, aux, s, c);
     if (A.v.w != 0.f) {
@@ -460,7 +464,7 @@ __global__ void __launch_bounds__(128)
                              A, c);
         }
     }
-    force_finish<EPI>(A, sorted_idx[s], ep, out);
+    force_finish<EPI>(A, i, ep, out);
 }
 
 // Force pass, two consecutive cell-ordered particles per thread with the same
@@ -478,7 +482,9 @@ __global__ void __launch_bounds__(128)
     const float* __restrict__ pj = reinterpret_cast<const float*>(aux);
     ForceAcc A = force_acc(pos4, vel4, aux, s0, c);
     ForceAcc B = force_acc(pos4, vel4, aux, has1 ? s0 + 1 : s0, c);
-    const bool va = A.v.w != 0.f, vb = has1 && B.v.w != 0.f;
+    const uint32_t i0 = sorted_idx[s0], i1 = has1 ? sorted_idx[s0 + 1] : 0xffffffffu;
+    // rho < 1e-6 (1/rho stored as 0) or not updated (ghost): no walk
+    const bool va = A.v.w != 0.f && i0 < out.limit, vb = has1 && B.v.w != 0.f && i1 < out.limit;
     const Window w0 = make_window(A.p, g, c.h2_skip);
     const Window w1 = make_window(B.p, g, c.h2_skip);
     if (va && vb && w0.cy == w1.cy && w0.cz == w1.cz) {
@@ -523,8 +529,8 @@ __global__ void __launch_bounds__(128)
             }
         }
     }
-    force_finish<EPI>(A, sorted_idx[s0], ep, out);
-    if (has1) force_finish<EPI>(B, sorted_idx[s0 + 1], ep, out);
+    force_finish<EPI>(A, i0, ep, out);
+    if (has1) force_finish<EPI>(B, i1, ep, out);
 }
 
 }  // namespace sph

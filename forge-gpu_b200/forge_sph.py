@@ -62,6 +62,7 @@ EXPORTED = (
     "forge_sph_density", "forge_sph_force", "forge_sph_step",
     "forge_grid_profile_enable", "forge_grid_profile_read",
     "forge_sort_pairs_static",
+    "forge_sph_force_step",
 )
 STATIC_SORT_MAX_N = 1 << 20
 
@@ -118,6 +119,8 @@ def lib() -> ctypes.CDLL:
                                  vp, vp, u64, vp]),
         "forge_grid_profile_enable": (i32, [vp, u32]),
         "forge_sort_pairs_static": (i32, [vp, vp, u64, u32, u32, vp]),
+        "forge_sph_force_step": (i32, [vp, ctypes.POINTER(SphParams), ctypes.POINTER(StepParams), vp, vp, vp, vp,
+                                       vp, vp, vp, u64, u64, vp]),
         "forge_grid_profile_read": (i32, [vp, ctypes.POINTER(f32), u32, ctypes.POINTER(u32)]),
     }
     for name, (res, args) in sig.items():

@@ -258,6 +258,20 @@ FORGE_API int forge_sph_step(forge_grid* g, const forge_sph_params* p,
                    float* pz, float* vx, float* vy, float* vz, float* density,
                    uint64_t n, void* stream);
 
+/* Force + step epilogue from a caller-supplied density, for a domain-
+ * decomposed run (the sharded form of forge_sph_step): the grid was built by
+ * forge_sph_density over n particles = owned particles first, then ghost
+ * copies of neighbouring slabs' boundary particles; density[n] holds the
+ * owners' exact densities (ghost entries overwritten after the exchange).
+ * Pressure + viscosity (Jacobi) + gravity / integrate / box as in
+ * forge_sph_step, but only particles i < n_update (the owned ones) are
+ * updated in place. Same math as SphFusedModule::execute's force pass
+ * (sph_fused.rs:518-639) followed by gravity.rs, integrate.rs,
+ * box_collider.rs. */
+FORGE_API int forge_sph_force_step(forge_grid* g, const forge_sph_params* p, const forge_step_params* sp,
+                                   float* px, float* py, float* pz, float* vx, float* vy, float* vz,
+                                   const float* density, uint64_t n, uint64_t n_update, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Benchmark aid (no reference counterpart; the reference only times the    */
 /* whole run with a wall clock, manifest_runner.rs:40-80).                  */
