@@ -308,7 +308,7 @@ def run_sharded(args, torch, dist, rank, world, local):
     cap = int(cfg.n / world * 1.3) + 4 * (cfg.n // cfg.dims[0]) + 1024
     dev = torch.device("cuda", local)
     be = slab.GpuBackend(forge_sph, cfg, cap, local)
-    run = slab.SlabRun(dist, rank, world, cfg, pos, vel, be, dev)
+    run = slab.SlabRun(dist, rank, world, cfg, pos, vel, be, dev, capacity=cap)
     del pos, vel
     for _ in range(args.warmup):
         run.step()
@@ -324,21 +324,37 @@ def run_sharded(args, torch, dist, rank, world, local):
     be.grid.check()
     ms_max = max_over_ranks(torch, dist, ms)
     halo = max_over_ranks(torch, dist, float(run.last_halo))
+    # phase breakdown on a few extra (untimed) steps
+    run.timing = []
+    for _ in range(3):
+        run.step()
+    torch.cuda.synchronize()
+    phase_ms = {}
+    ev = run.timing
+    for (a, ea), (b, eb) in zip(ev[:-1], ev[1:]):
+        if b != "start":
+            phase_ms[b] = phase_ms.get(b, 0.0) + ea.elapsed_time(eb) / 3
+    run.timing = None
+    phase_ms = {k: max_over_ranks(torch, dist, v) for k, v in sorted(phase_ms.items())}
 
     # e2e: the same sharded step with the rank's particle state read from and
     # written back to pinned host memory every step.
-    hbuf = torch.empty((cap, run.state.shape[1]), dtype=torch.float32).pin_memory()
-    cur = run.state.shape[0]
-    hbuf[:cur].copy_(run.state)
+    hbuf = torch.empty((run.cols.shape[0], cap), dtype=torch.float32).pin_memory()
+    cur = run.n
+    for k in range(hbuf.shape[0]):
+        hbuf[k, :cur].copy_(run.cols[k, :cur])
     moved = [0]
 
     def one():
         nonlocal cur
-        run.state = hbuf[:cur].to(dev, non_blocking=True)
+        for k in range(hbuf.shape[0]):
+            run.cols[k, :cur].copy_(hbuf[k, :cur], non_blocking=True)
+        run.n = cur
         run.step()
-        cur = run.state.shape[0]
-        hbuf[:cur].copy_(run.state, non_blocking=True)
-        moved[0] += cur * hbuf.shape[1] * 4
+        cur = run.n
+        for k in range(hbuf.shape[0]):
+            hbuf[k, :cur].copy_(run.cols[k, :cur], non_blocking=True)
+        moved[0] += cur * hbuf.shape[0] * 4
 
     for _ in range(3):
         one()
@@ -363,6 +379,7 @@ def run_sharded(args, torch, dist, rank, world, local):
                 "config": {"workload": cfg.name, "particles": cfg.n, "cells": cfg.cells, "h": cfg.h,
                            "inputs_exceed_l2": True, "parallelism": f"x-slab over {world} GPUs (NCCL send/recv)",
                            "max_halo_particles_per_rank": halo},
+                "phases_ms_max_over_ranks": phase_ms,
                 "e2e": {"value": cfg.n * e2e_steps / (e2e_ms / 1e3), "unit": "particle-steps/s",
                         "h2d_bytes_per_step": tot_bytes, "d2h_bytes_per_step": tot_bytes},
                 "gpu_launches": (kernels_per_step(cfg) + 1) * args.steps * world,

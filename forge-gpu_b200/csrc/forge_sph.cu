@@ -14,6 +14,7 @@
 #include "grid.cuh"
 #include "radix_sort.cuh"
 #include "sph.cuh"
+#include "slab.cuh"
 
 using namespace forge;
 
@@ -781,5 +782,71 @@ extern "C" int forge_grid_profile_read(forge_grid* g, float* out, uint32_t cap_s
     }
     *steps = cnt;
     g->prof_count = 0;
+    return FORGE_OK;
+}
+
+// ===========================================================================
+// Slab-exchange helpers
+// ===========================================================================
+struct forge_slab {
+    int device = 0;
+    uint64_t max_n = 0;
+    uint32_t* tile_counts = nullptr;
+};
+
+extern "C" int forge_slab_create(uint64_t max_n, int device, forge_slab** out) {
+    if (!out) return set_error(FORGE_ERR_INVALID_ARG, "forge_slab_create: out is NULL");
+    *out = nullptr;
+    if (max_n >= 0xffffffffull) return set_error(FORGE_ERR_INVALID_ARG, "forge_slab_create: max_n must be < 2^32-1");
+    FORGE_DEVICE_SCOPE(device);
+    forge_slab* h = new forge_slab;
+    h->device = device;
+    h->max_n = max_n;
+    const size_t tiles = (max_n + slab::kTile - 1) / slab::kTile + 1;
+    if (dalloc(&h->tile_counts, tiles * slab::kLists) != cudaSuccess) {
+        delete h;
+        return set_error(FORGE_ERR_CUDA, "forge_slab_create: cudaMalloc failed");
+    }
+    *out = h;
+    return FORGE_OK;
+}
+
+extern "C" void forge_slab_destroy(forge_slab* h) {
+    if (!h) return;
+    DeviceScope scope(h->device);
+    cudaFree(h->tile_counts);
+    delete h;
+}
+
+extern "C" int forge_slab_classify(forge_slab* h, const float* x, uint64_t n, float lo, float hi, float reach,
+                                   uint32_t flags, uint32_t* idx_out, uint32_t* counts, void* stream) {
+    if (!h || !counts) return set_error(FORGE_ERR_INVALID_ARG, "forge_slab_classify: NULL handle or counts");
+    if (n > h->max_n)
+        return set_error(FORGE_ERR_CAPACITY, "forge_slab_classify: n=%llu exceeds max_n=%llu", (unsigned long long)n,
+                         (unsigned long long)h->max_n);
+    if (n && (!x || !idx_out)) return set_error(FORGE_ERR_INVALID_ARG, "forge_slab_classify: NULL array");
+    FORGE_DEVICE_SCOPE(h->device);
+    cudaStream_t st = as_stream(stream);
+    if (n == 0) {
+        FORGE_CUDA(cudaMemsetAsync(counts, 0, slab::kLists * sizeof(uint32_t), st));
+        return FORGE_OK;
+    }
+    const slab::ClassifyArgs a{lo, hi, reach, flags};
+    const uint32_t tiles = grid_blocks(n, slab::kTile);
+    slab::classify_count_kernel<<<tiles, slab::kThreads, 0, st>>>(x, (uint32_t)n, a, h->tile_counts);
+    slab::classify_scan_kernel<<<1, 1024, 0, st>>>(h->tile_counts, tiles, counts);
+    slab::classify_write_kernel<<<tiles, slab::kThreads, 0, st>>>(x, (uint32_t)n, a, h->tile_counts, counts,
+                                                                  idx_out);
+    FORGE_LAUNCHED();
+    return FORGE_OK;
+}
+
+extern "C" int forge_slab_compact(float* cols, uint64_t ld, uint32_t rows, uint64_t n, const uint32_t* gone,
+                                  uint64_t k, void* stream) {
+    if (k == 0) return FORGE_OK;
+    if (!cols || !gone || k > n || n >= 0xffffffffull)
+        return set_error(FORGE_ERR_INVALID_ARG, "forge_slab_compact: bad arguments");
+    slab::compact_kernel<<<1, 1024, 0, as_stream(stream)>>>(cols, ld, rows, (uint32_t)n, gone, (uint32_t)k);
+    FORGE_LAUNCHED();
     return FORGE_OK;
 }

@@ -1,0 +1,145 @@
+// Slab-exchange helpers for the sharded SPH step (sm_100a): ordered
+// selection of the particles that leave a slab or lie within h of its faces,
+// and in-place removal of leaving particles from a column buffer. Integer /
+// byte work, HBM-bound; deterministic (every list comes out in ascending
+// particle order, no atomics on positions).
+#pragma once
+
+#include "common.cuh"
+
+namespace forge {
+namespace slab {
+
+constexpr int kThreads = 256;
+constexpr int kItems = 16;
+constexpr int kTile = kThreads * kItems;
+constexpr int kLists = 3;  // A (either side), L (left), R (right)
+
+struct ClassifyArgs {
+    float lo, hi, reach;
+    uint32_t flags;  // 1 has left neighbour, 2 has right neighbour, 4 halo mode (else migrate mode)
+};
+
+// Membership bits of element x in lists A, L, R.
+__device__ __forceinline__ uint32_t member_bits(float x, const ClassifyArgs& a) {
+    const bool halo = a.flags & 4u;
+    const bool l = (a.flags & 1u) && (halo ? x < a.lo + a.reach : x < a.lo);
+    const bool r = (a.flags & 2u) && (halo ? x >= a.hi - a.reach : x >= a.hi);
+    const bool all = !halo && (l || r);
+    return (all ? 1u : 0u) | (l ? 2u : 0u) | (r ? 4u : 0u);
+}
+
+// Pass 1: per-tile counts of each list.
+__global__ void __launch_bounds__(kThreads)
+    classify_count_kernel(const float* __restrict__ x, uint32_t n, ClassifyArgs a, uint32_t* __restrict__ tile_counts) {
+    __shared__ uint32_t s[kLists];
+    if (threadIdx.x < kLists) s[threadIdx.x] = 0;
+    __syncthreads();
+    uint32_t c[kLists] = {0, 0, 0};
+    const uint32_t base = blockIdx.x * kTile;
+#pragma unroll
+    for (int k = 0; k < kItems; ++k) {
+        const uint32_t i = base + k * kThreads + threadIdx.x;
+        if (i < n) {
+            const uint32_t b = member_bits(x[i], a);
+#pragma unroll
+            for (int l = 0; l < kLists; ++l) c[l] += (b >> l) & 1u;
+        }
+    }
+#pragma unroll
+    for (int l = 0; l < kLists; ++l) {
+        uint32_t v = c[l];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if ((threadIdx.x & 31) == 0 && v) atomicAdd(&s[l], v);
+    }
+    __syncthreads();
+    if (threadIdx.x < kLists) tile_counts[blockIdx.x * kLists + threadIdx.x] = s[threadIdx.x];
+}
+
+// Pass 2 (one block): exclusive scan of the tile counts per list, list totals
+// to counts[0..2], and each list's start in the packed output.
+__global__ void __launch_bounds__(1024)
+    classify_scan_kernel(uint32_t* __restrict__ tile_counts, uint32_t tiles, uint32_t* __restrict__ counts) {
+    __shared__ uint32_t s_scan[1024 / 32 + 1];
+    __shared__ uint32_t s_tot[kLists];
+    for (int l = 0; l < kLists; ++l) {
+        uint32_t carry = 0;
+        for (uint32_t b = 0; b < tiles; b += 1024) {
+            const uint32_t t = b + threadIdx.x;
+            const uint32_t v = t < tiles ? tile_counts[t * kLists + l] : 0u;
+            uint32_t total;
+            const uint32_t ex = block_exclusive_scan<1024>(v, s_scan, &total);
+            if (t < tiles) tile_counts[t * kLists + l] = carry + ex;
+            carry += total;
+        }
+        if (threadIdx.x == 0) s_tot[l] = carry;
+        __syncthreads();
+    }
+    if (threadIdx.x < kLists) counts[threadIdx.x] = s_tot[threadIdx.x];
+}
+
+// Pass 3: write each list's element indices in ascending order, packed as
+// [A | L | R].
+__global__ void __launch_bounds__(kThreads)
+    classify_write_kernel(const float* __restrict__ x, uint32_t n, ClassifyArgs a,
+                          const uint32_t* __restrict__ tile_offsets, const uint32_t* __restrict__ counts,
+                          uint32_t* __restrict__ out) {
+    __shared__ uint32_t s_scan[kThreads / 32 + 1];
+    const uint32_t base = blockIdx.x * kTile + threadIdx.x * kItems;  // blocked: thread owns 16 consecutive
+    uint32_t bits[kItems];
+    uint32_t c[kLists] = {0, 0, 0};
+#pragma unroll
+    for (int k = 0; k < kItems; ++k) {
+        const uint32_t i = base + k;
+        bits[k] = i < n ? member_bits(x[i], a) : 0u;
+#pragma unroll
+        for (int l = 0; l < kLists; ++l) c[l] += (bits[k] >> l) & 1u;
+    }
+    uint32_t start = 0;
+#pragma unroll
+    for (int l = 0; l < kLists; ++l) {
+        uint32_t total;
+        uint32_t pos = block_exclusive_scan<kThreads>(c[l], s_scan, &total) + tile_offsets[blockIdx.x * kLists + l] +
+                       start;
+        start += counts[l];
+#pragma unroll
+        for (int k = 0; k < kItems; ++k)
+            if ((bits[k] >> l) & 1u) out[pos++] = base + k;
+    }
+}
+
+// Remove columns `gone` (ascending, k of them, all < n) from a row-major
+// (rows x ld) buffer of n live columns: the surviving columns among the last k
+// move into the holes below n - k, in ascending order. One block.
+__global__ void __launch_bounds__(1024)
+    compact_kernel(float* __restrict__ cols, uint64_t ld, uint32_t rows, uint32_t n, const uint32_t* __restrict__ gone,
+                   uint32_t k) {
+    __shared__ uint32_t s_scan[1024 / 32 + 1];
+    const uint32_t keep = n - k;
+    uint32_t carry = 0;  // fillers ranked so far
+    for (uint32_t b = 0; b < k; b += 1024) {
+        const uint32_t t = keep + b + threadIdx.x;  // tail column
+        bool fill = false;
+        if (b + threadIdx.x < k) {
+            // t is a filler unless it is in `gone` (binary search)
+            uint32_t lo = 0, hi = k;
+            while (lo < hi) {
+                const uint32_t mid = (lo + hi) >> 1;
+                if (gone[mid] < t) lo = mid + 1;
+                else hi = mid;
+            }
+            fill = !(lo < k && gone[lo] == t);
+        }
+        uint32_t total;
+        const uint32_t r = carry + block_exclusive_scan<1024>(fill ? 1u : 0u, s_scan, &total);
+        if (fill) {
+            const uint32_t dst = gone[r];  // the r-th hole (holes are the smallest entries of gone)
+            for (uint32_t row = 0; row < rows; ++row) cols[row * ld + dst] = cols[row * ld + t];
+        }
+        carry += total;
+    }
+}
+
+}  // namespace slab
+}  // namespace forge

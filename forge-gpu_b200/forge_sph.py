@@ -63,6 +63,7 @@ EXPORTED = (
     "forge_grid_profile_enable", "forge_grid_profile_read",
     "forge_sort_pairs_static",
     "forge_sph_force_step",
+    "forge_slab_create", "forge_slab_destroy", "forge_slab_classify", "forge_slab_compact",
 )
 STATIC_SORT_MAX_N = 1 << 20
 
@@ -119,6 +120,10 @@ def lib() -> ctypes.CDLL:
                                  vp, vp, u64, vp]),
         "forge_grid_profile_enable": (i32, [vp, u32]),
         "forge_sort_pairs_static": (i32, [vp, vp, u64, u32, u32, vp]),
+        "forge_slab_create": (i32, [u64, i32, pvp]),
+        "forge_slab_destroy": (None, [vp]),
+        "forge_slab_classify": (i32, [vp, vp, u64, f32, f32, f32, u32, vp, vp, vp]),
+        "forge_slab_compact": (i32, [vp, u64, u32, u64, vp, u64, vp]),
         "forge_sph_force_step": (i32, [vp, ctypes.POINTER(SphParams), ctypes.POINTER(StepParams), vp, vp, vp, vp,
                                        vp, vp, vp, u64, u64, vp]),
         "forge_grid_profile_read": (i32, [vp, ctypes.POINTER(f32), u32, ctypes.POINTER(u32)]),

@@ -73,46 +73,69 @@ class Exchanger:
             for r in self.dist.batch_isend_irecv(ops):
                 r.wait()
 
-    def swap(self, to_left: torch.Tensor | None, to_right: torch.Tensor | None, ncol: int):
-        """Send row blocks to rank-1 / rank+1, receive theirs. Returns
-        (from_left, from_right), each (k, ncol) (empty where no neighbour)."""
+    def swap_counted(self, to_left, counts_left, to_right, counts_right, ncol: int):
+        """swap() that also carries a tuple of sub-block sizes per message.
+        Returns (from_left, from_right, counts_from_left, counts_from_right)."""
         left = self.rank - 1 if self.rank > 0 else None
         right = self.rank + 1 if self.rank < self.world - 1 else None
-        dt = torch.float32
-        cnt = {}
-        sends, recvs = {}, {}
-        if left is not None:
-            sends[left] = torch.tensor([to_left.shape[0]], dtype=torch.int64, device=self.device)
-            cnt[left] = torch.zeros(1, dtype=torch.int64, device=self.device)
-            recvs[left] = cnt[left]
-        if right is not None:
-            # distinct tensors per peer: a batch may not reuse one buffer
-            sends[right] = torch.tensor([to_right.shape[0]], dtype=torch.int64, device=self.device)
-            cnt[right] = torch.zeros(1, dtype=torch.int64, device=self.device)
-            recvs[right] = cnt[right]
-        self._p2p(sends, recvs)
-        sends, recvs, out = {}, {}, {}
-        for peer, blk in ((left, to_left), (right, to_right)):
+        k = len(counts_left)
+        sends, recvs, cnt = {}, {}, {}
+        for peer, c in ((left, counts_left), (right, counts_right)):
             if peer is None:
                 continue
-            blk = blk.to(self.device)
-            k = int(cnt[peer].item())
-            out[peer] = torch.empty((k, ncol), dtype=dt, device=self.device)
+            sends[peer] = torch.tensor(list(c), dtype=torch.int64, device=self.device)
+            cnt[peer] = torch.zeros(k, dtype=torch.int64, device=self.device)
+            recvs[peer] = cnt[peer]
+        self._p2p(sends, recvs)
+        host = {p: tuple(int(v) for v in t.tolist()) for p, t in cnt.items()}
+        zero = tuple([0] * k)
+        cl, cr = host.get(left, zero), host.get(right, zero)
+        a, b = self.swap_known(to_left, sum(cl), to_right, sum(cr), ncol)
+        return a, b, cl, cr
+
+    def swap_known(self, to_left, n_from_left: int, to_right, n_from_right: int, ncol: int):
+        """Exchange row blocks whose incoming sizes are already known."""
+        left = self.rank - 1 if self.rank > 0 else None
+        right = self.rank + 1 if self.rank < self.world - 1 else None
+        sends, recvs, out = {}, {}, {}
+        for peer, blk, k in ((left, to_left, n_from_left), (right, to_right, n_from_right)):
+            if peer is None:
+                continue
+            out[peer] = torch.empty((k, ncol), dtype=torch.float32, device=self.device)
             if k:
                 recvs[peer] = out[peer]
             if blk.shape[0]:
-                sends[peer] = blk.contiguous()
+                sends[peer] = blk.to(self.device).contiguous()
         self._p2p(sends, recvs)
-        empty = torch.empty((0, ncol), dtype=dt, device=self.device)
-        a, b = out.get(left, empty), out.get(right, empty)
-        return a.to(self.home), b.to(self.home)
+        empty = torch.empty((0, ncol), dtype=torch.float32, device=self.home)
+        a = out[left].to(self.home) if left is not None else empty
+        b = out[right].to(self.home) if right is not None else empty
+        return a, b
 
 
 class SlabRun:
-    """One rank's share of a sharded SPH run."""
+    """One rank's share of a sharded SPH run.
+
+    Particle state lives in one preallocated (7, capacity) float32 buffer,
+    rows x, y, z, vx, vy, vz, id-bits, so each row slice cols[k, :n] is a
+    contiguous SoA array the kernels take directly: owned particles in
+    columns [0, n), ghosts (copies of neighbours' particles within h of a
+    face) after them.
+
+    Two neighbour exchange rounds per step:
+      round 1 (after force, for the next step): migrants (owned particles that
+        left the slab) and halo rows (owned particles within h of a face) go
+        to that neighbour in one message; the receiver appends migrants to its
+        owned set and halo rows as ghosts. The sender keeps its migrants as
+        ghosts too -- they sit just across the face.
+      round 2 (after density): for every ghost the owner sends its exact
+        density (counts known from round 1, so no count exchange).
+    Leaving particles are removed by moving tail columns into their holes, so
+    per step only halo- and migrant-sized data moves.
+    """
 
     def __init__(self, dist, rank: int, world: int, cfg, pos, vel, backend, device: torch.device,
-                 x_range=(0.0, 1.0), order_by_id: bool = False, comm_device=None):
+                 x_range=(0.0, 1.0), order_by_id: bool = False, comm_device=None, capacity: int | None = None):
         self.cfg, self.backend, self.device = cfg, backend, device
         self.geo = SlabGeometry(rank, world, x_range[0], x_range[1], cfg.h)
         self.ex = Exchanger(dist, rank, world, device, comm_device)
@@ -120,79 +143,136 @@ class SlabRun:
         px = torch.as_tensor(pos[0])
         m = self.geo.owned_mask(px)
         ids = torch.arange(px.numel(), dtype=torch.int32)[m]
-        cols = [torch.as_tensor(a)[m] for a in list(pos) + list(vel)]
-        self.state = self._pack(cols, ids).to(device)  # (n_own, 7)
+        own = torch.stack([torch.as_tensor(a)[m] for a in list(pos) + list(vel)] + [ids.view(torch.float32)])
+        n_own = own.shape[1]
+        cap = capacity if capacity is not None else int(n_own * 1.5) + 4096
+        self.cols = torch.empty((_NCOL, cap), dtype=torch.float32, device=device)
+        self.cols[:, :n_own] = own.to(device)
+        self.n = n_own
+        self.ng = 0
         self.last_halo = 0
+        self.timing = None  # set to a list to record per-phase CUDA events
+        self._round1(migrate=False)  # initial halo
 
-    @staticmethod
-    def _pack(cols, ids):
-        return torch.stack(list(cols) + [ids.view(torch.float32)], dim=1).contiguous()
+    def _mark(self, name):
+        if self.timing is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            self.timing.append((name, ev))
+
+    @property
+    def capacity(self) -> int:
+        return self.cols.shape[1]
 
     @property
     def n_own(self) -> int:
-        return self.state.shape[0]
+        return self.n
+
+    @property
+    def state(self) -> torch.Tensor:
+        """(n_own, 7) view: x, y, z, vx, vy, vz, id bits."""
+        return self.cols[:, :self.n].t()
 
     def ids(self) -> torch.Tensor:
-        return self.state[:, 6].contiguous().view(torch.int32)
+        return self.cols[6, :self.n].view(torch.int32)
+
+    def _need(self, n: int) -> None:
+        if n > self.capacity:
+            raise RuntimeError(f"slab rank {self.geo.rank}: {n} particles exceed capacity {self.capacity}")
+
+    def _flags(self):
+        return (0 if self.geo.first else 1) | (0 if self.geo.last else 2)
+
+    def _round1(self, migrate: bool) -> None:
+        """Remove migrants from the owned set, send [migrants | halo] to each
+        neighbour, append arrivals and ghosts, and record the ghost-density
+        bookkeeping for round 2."""
+        g, C, be = self.geo, self.cols, self.backend
+        n_own = self.n
+        reach = self.cfg.h * (1.0 + 1e-5)
+        if migrate:
+            mig, mig_l, mig_r = be.classify(C[0], n_own, g.lo, g.hi, reach, self._flags())
+        else:
+            mig = mig_l = mig_r = torch.empty(0, dtype=torch.int64, device=C.device)
+        rows_ml, rows_mr = C[:, mig_l], C[:, mig_r]  # gathered before the compaction moves columns
+        be.compact(C, n_own, mig)
+        keep = n_own - mig.numel()
+        _, hl, hr = be.classify(C[0], keep, g.lo, g.hi, reach, self._flags() | 4)
+        send_l = torch.cat([rows_ml, C[:, hl]], dim=1).t()
+        send_r = torch.cat([rows_mr, C[:, hr]], dim=1).t()
+        got_l, got_r, cnt_l, cnt_r = self.ex.swap_counted(send_l, (mig_l.numel(), hl.numel()),
+                                                          send_r, (mig_r.numel(), hr.numel()), _NCOL)
+        am_l, ah_l = cnt_l
+        am_r, ah_r = cnt_r
+        n_new = keep + am_l + am_r
+        ng = ah_l + ah_r + mig_l.numel() + mig_r.numel()
+        self._need(n_new + ng + 1)
+        C[:, keep:keep + am_l] = got_l[:am_l].t()
+        C[:, keep + am_l:n_new] = got_r[:am_r].t()
+        o = n_new
+        blocks = {}
+        for name, blk in (("hl", got_l[am_l:].t()), ("hr", got_r[am_r:].t()), ("ml", rows_ml), ("mr", rows_mr)):
+            w = blk.shape[1]
+            C[:, o:o + w] = blk
+            blocks[name] = torch.arange(o, o + w, device=C.device)
+            o += w
+        arr_l = torch.arange(keep, keep + am_l, device=C.device)
+        arr_r = torch.arange(keep + am_l, n_new, device=C.device)
+        # round 2: rho of [halo sent to X, arrivals from X] goes to X; X's rho
+        # fills [halo from X, our migrants to X] in the same order.
+        self.rho_send = (torch.cat([hl, arr_l]), torch.cat([hr, arr_r]))
+        self.rho_slot = (torch.cat([blocks["hl"], blocks["ml"]]), torch.cat([blocks["hr"], blocks["mr"]]))
+        self.n, self.ng = n_new, ng
+        self.last_halo = ng
 
     def step(self) -> None:
-        g, h = self.geo, self.cfg.h
-        st = self.state
-        x = st[:, 0]
-        reach = h * (1.0 + 1e-5)
-        left_idx = torch.nonzero(x < g.lo + reach).flatten() if not g.first else None
-        right_idx = torch.nonzero(x >= g.hi - reach).flatten() if not g.last else None
-        empty = st[:0]
-        from_l, from_r = self.ex.swap(st[left_idx] if left_idx is not None else empty,
-                                      st[right_idx] if right_idx is not None else empty, _NCOL)
-        n_own, nl, nr = st.shape[0], from_l.shape[0], from_r.shape[0]
-        self.last_halo = nl + nr
-        local = torch.cat([st, from_l, from_r], dim=0)
+        g, C = self.geo, self.cols
+        self._mark("start")
+        n_own, n = self.n, self.n + self.ng
+        send_l, send_r = self.rho_send
+        slot_l, slot_r = self.rho_slot
         perm = None
-        if self.order_by_id:
-            perm = torch.argsort(local[:, 6].contiguous().view(torch.int32), stable=True)
-            local = local[perm]
-        cols = [local[:, k].contiguous() for k in range(6)]
-        n = local.shape[0]
-        rho = self.backend.density(cols[0:3], n)
-        # ghost densities from their owners
-        send_l = rho[_pos_after(perm, left_idx)].reshape(-1, 1) if left_idx is not None else rho[:0].reshape(0, 1)
-        send_r = rho[_pos_after(perm, right_idx)].reshape(-1, 1) if right_idx is not None else rho[:0].reshape(0, 1)
-        got_l, got_r = self.ex.swap(send_l, send_r, 1)
-        ghost_rho = torch.cat([got_l.flatten(), got_r.flatten()])
-        ghost_pos = torch.arange(n_own, n, device=rho.device)
-        if perm is not None:
+        if self.order_by_id:  # test mode: neighbour order identical to the unsharded run
+            perm = torch.argsort(C[6, :n].view(torch.int32), stable=True)
+            C[:, :n] = C[:, perm]
             inv = torch.empty_like(perm)
             inv[perm] = torch.arange(n, device=perm.device)
-            ghost_pos = inv[ghost_pos]
-        rho[ghost_pos] = ghost_rho
-        # force + epilogue for owned particles only
-        owned_flag = torch.zeros(n, dtype=torch.bool, device=rho.device)
-        if perm is None:
-            owned_flag[:n_own] = True
-        else:
-            owned_flag[perm < n_own] = True
-        # owned rows lead the local arrays unless they were id-ordered
-        self.backend.force_step(cols, rho, n, n_own if perm is None else n)
-        new = torch.stack(cols + [local[:, 6]], dim=1)[owned_flag]
-        # migration
-        x = new[:, 0]
-        go_l = (x < g.lo) if not g.first else torch.zeros_like(x, dtype=torch.bool)
-        go_r = (x >= g.hi) if not g.last else torch.zeros_like(x, dtype=torch.bool)
-        stay = ~(go_l | go_r)
-        in_l, in_r = self.ex.swap(new[go_l], new[go_r], _NCOL)
-        self.state = torch.cat([new[stay], in_l, in_r], dim=0).contiguous()
-        if self.order_by_id:
-            self.state = self.state[torch.argsort(self.ids(), stable=True)].contiguous()
+            send_l, send_r, slot_l, slot_r = inv[send_l], inv[send_r], inv[slot_l], inv[slot_r]
+        rho = self.backend.density([C[k, :n] for k in range(3)], n)
+        self._mark("density")
+        got_l, got_r = self.ex.swap_known(rho[send_l].reshape(-1, 1), slot_l.numel(),
+                                          rho[send_r].reshape(-1, 1), slot_r.numel(), 1)
+        rho[slot_l] = got_l.flatten()
+        rho[slot_r] = got_r.flatten()
+        self._mark("ghost_rho")
+        self.backend.force_step([C[k, :n] for k in range(6)], rho, n, n if perm is not None else n_own)
+        self._mark("force")
+        if perm is not None:  # restore the owned-then-ghost layout
+            C[:, perm] = C[:, :n].clone()
+        self._round1(migrate=True)
+        self._mark("exchange")
 
 
-def _pos_after(perm, idx):
-    """Positions, in the (possibly id-ordered) local arrays, of owned rows idx."""
-    if perm is None:
-        return idx
-    inv = torch.empty_like(perm)
-    inv[perm] = torch.arange(perm.numel(), device=perm.device)
-    return inv[idx]
+def torch_classify(x, n, lo, hi, reach, flags):
+    """forge_slab_classify with torch ops (CPU ranks in tests)."""
+    x = x[:n]
+    none = torch.zeros(n, dtype=torch.bool, device=x.device)
+    halo = bool(flags & 4)
+    left = (x < lo + reach if halo else x < lo) if flags & 1 else none
+    right = (x >= hi - reach if halo else x >= hi) if flags & 2 else none
+    both = none if halo else (left | right)
+    return tuple(torch.nonzero(m).flatten() for m in (both, left, right))
+
+
+def torch_compact(cols, n, gone):
+    """forge_slab_compact with torch ops (CPU ranks in tests)."""
+    k = gone.numel()
+    if k == 0:
+        return
+    keep = n - k
+    tail = torch.arange(keep, n, device=cols.device)
+    fillers = tail[~torch.isin(tail, gone)]
+    cols[:, gone[:fillers.numel()]] = cols[:, fillers]
 
 
 class GpuBackend:
@@ -212,6 +292,34 @@ class GpuBackend:
         self.stp = stp
         self.L = forge_sph.lib()
         self.capacity = capacity
+        h = ctypes.c_void_p()
+        forge_sph.check(self.L.forge_slab_create(capacity, device, ctypes.byref(h)))
+        self.slab = h
+        dev = torch.device("cuda", device)
+        self.idx = torch.empty(2 * max(capacity, 1), dtype=torch.int32, device=dev)  # [A | L | R] <= 2n
+        self.counts = torch.zeros(3, dtype=torch.int32, device=dev)
+
+    def __del__(self):
+        h = getattr(self, "slab", None)
+        if h and self.f._lib is not None:
+            self.f._lib.forge_slab_destroy(h)
+            self.slab = None
+
+    def classify(self, x, n, lo, hi, reach, flags):
+        """(A, L, R) ascending index lists from forge_slab_classify (one
+        device-to-host read of the three counts)."""
+        self.f.check(self.L.forge_slab_classify(self.slab, x.data_ptr(), n, lo, hi, reach, flags,
+                                                self.idx.data_ptr(), self.counts.data_ptr(), self._st()))
+        a, l, r = self.counts.tolist()
+        flat = self.idx[:a + l + r].long()
+        return flat[:a], flat[a:a + l], flat[a + l:]
+
+    def compact(self, cols, n, gone):
+        if gone.numel() == 0:
+            return
+        g32 = gone.to(torch.int32)
+        self.f.check(self.L.forge_slab_compact(cols.data_ptr(), cols.stride(0), cols.shape[0], n, g32.data_ptr(),
+                                               gone.numel(), self._st()))
 
     def _st(self):
         return torch.cuda.current_stream().cuda_stream

@@ -273,6 +273,33 @@ FORGE_API int forge_sph_force_step(forge_grid* g, const forge_sph_params* p, con
                                    const float* density, uint64_t n, uint64_t n_update, void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* Slab-exchange helpers for the sharded step. No counterpart in the        */
+/* reference: its multi-GPU API is a stub (forge-runtime/src/cuda.rs:134-178). */
+/* ------------------------------------------------------------------------ */
+
+typedef struct forge_slab forge_slab;
+
+/* Scratch for classifying up to max_n particles of one slab. */
+FORGE_API int forge_slab_create(uint64_t max_n, int device, forge_slab** out);
+FORGE_API void forge_slab_destroy(forge_slab* h);
+
+/* Ordered selection against the slab [lo, hi). flags: 1 = has a left
+ * neighbour, 2 = has a right neighbour, 4 = halo mode.
+ *   migrate mode: L = {i : x[i] < lo}, R = {i : x[i] >= hi}, A = L u R
+ *   halo mode:    L = {i : x[i] < lo + reach}, R = {i : x[i] >= hi - reach}, A = {}
+ * (L only with a left neighbour, R only with a right one). idx_out receives
+ * [A | L | R], each ascending -- at most 2n entries, so it must hold 2n;
+ * counts[3] (device) = |A|, |L|, |R|. */
+FORGE_API int forge_slab_classify(forge_slab* h, const float* x, uint64_t n, float lo, float hi, float reach,
+                                  uint32_t flags, uint32_t* idx_out, uint32_t* counts, void* stream);
+
+/* Remove the k columns gone[] (ascending, < n) from a row-major rows x ld
+ * float buffer holding n live columns: surviving columns among the last k
+ * move into the holes, so the live columns become [0, n - k). */
+FORGE_API int forge_slab_compact(float* cols, uint64_t ld, uint32_t rows, uint64_t n, const uint32_t* gone,
+                                 uint64_t k, void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* Benchmark aid (no reference counterpart; the reference only times the    */
 /* whole run with a wall clock, manifest_runner.rs:40-80).                  */
 /* ------------------------------------------------------------------------ */

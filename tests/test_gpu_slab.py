@@ -81,3 +81,24 @@ def test_two_rank_sharded_step_matches_single_gpu(cuda, tmp_path):
                                          *(x.data_ptr() for x in p + v), rho.data_ptr(), cfg.n, None))
     want = np.stack([x.cpu().numpy() for x in p + v], axis=1)
     assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("n", [0, 1, 4095, 4097, 300_000])
+def test_slab_classify_and_compact_match_torch(cuda, n):
+    torch_ = cuda
+    g = torch_.Generator().manual_seed(n)
+    x = (torch_.rand(n, generator=g) * 1.2 - 0.1).cuda()
+    cfg = _cfg()
+    be = slab.GpuBackend(forge_sph, cfg, max(n, 1), 0)
+    for flags in (1, 2, 3, 5, 6, 7):
+        got = be.classify(x, n, 0.25, 0.75, 0.05, flags)
+        want = slab.torch_classify(x, n, 0.25, 0.75, 0.05, flags)
+        for a, b in zip(got, want):
+            assert torch_.equal(a, b), flags
+    mig = slab.torch_classify(x, n, 0.25, 0.75, 0.05, 3)[0]
+    cols = torch_.rand((7, n + 5), generator=g).cuda()
+    ref = cols.clone()
+    be.compact(cols, n, mig)
+    slab.torch_compact(ref, n, mig)
+    keep = n - mig.numel()
+    assert torch_.equal(cols[:, :keep], ref[:, :keep])

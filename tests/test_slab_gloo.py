@@ -38,6 +38,9 @@ class OracleBackend:
         self.cfg = cfg
         self.p = oracle.SphParams(cfg.h, cfg.mass, cfg.gas_constant, cfg.rest_density, cfg.viscosity)
 
+    classify = staticmethod(slab.torch_classify)
+    compact = staticmethod(slab.torch_compact)
+
     def density(self, pos, n):
         c = self.cfg
         p = [x.numpy() for x in pos]
