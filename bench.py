@@ -308,7 +308,7 @@ def run_sharded(args, torch, dist, rank, world, local):
     cap = int(cfg.n / world * 1.3) + 4 * (cfg.n // cfg.dims[0]) + 1024
     dev = torch.device("cuda", local)
     be = slab.GpuBackend(forge_sph, cfg, cap, local)
-    run = slab.SlabRun(dist, rank, world, cfg, pos, vel, be, dev, capacity=cap)
+    run = slab.SlabRun(dist, rank, world, cfg, pos, vel, be, dev, capacity=cap, comm=args.comm, forge_sph=forge_sph)
     del pos, vel
     for _ in range(args.warmup):
         run.step()
@@ -377,7 +377,7 @@ def run_sharded(args, torch, dist, rank, world, local):
                 "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic",
                 "config": {"workload": cfg.name, "particles": cfg.n, "cells": cfg.cells, "h": cfg.h,
-                           "inputs_exceed_l2": True, "parallelism": f"x-slab over {world} GPUs (NCCL send/recv)",
+                           "inputs_exceed_l2": True, "parallelism": f"x-slab over {world} GPUs (NCCL send/recv, exchange={args.comm})",
                            "max_halo_particles_per_rank": halo},
                 "phases_ms_max_over_ranks": phase_ms,
                 "e2e": {"value": cfg.n * e2e_steps / (e2e_ms / 1e3), "unit": "particle-steps/s",
@@ -397,6 +397,8 @@ def main():
                     choices=["sharded16m", "dambreak1m", "dambreak65k", "blobs4m", "ref65k"])
     ap.add_argument("--no-extra", action="store_true", help="skip the 1M dam-break and 2^28 sort extras")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
+    ap.add_argument("--comm", choices=["nccl", "torch"], default="nccl",
+                    help="N>1 exchange: in the library over NCCL, or in Python over torch.distributed")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 

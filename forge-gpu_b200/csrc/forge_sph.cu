@@ -850,3 +850,5 @@ extern "C" int forge_slab_compact(float* cols, uint64_t ld, uint32_t rows, uint6
     FORGE_LAUNCHED();
     return FORGE_OK;
 }
+
+#include "slab_comm.cuh"

@@ -143,3 +143,39 @@ __global__ void __launch_bounds__(1024)
 
 }  // namespace slab
 }  // namespace forge
+
+namespace forge {
+namespace slab {
+
+// out[i*rows + r] = cols[r*ld + idx[i]]: columns listed in idx -> row-major
+// records of `rows` floats (the message layout of the slab exchange).
+__global__ void __launch_bounds__(256)
+    pack_kernel(const float* __restrict__ cols, uint64_t ld, uint32_t rows, const uint32_t* __restrict__ idx,
+                uint32_t k, float* __restrict__ out) {
+    const uint32_t t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= k * rows) return;
+    const uint32_t i = t / rows, r = t - i * rows;
+    out[t] = cols[r * ld + idx[i]];
+}
+
+// cols[r*ld + dst + i] = in[i*rows + r] for i < k.
+__global__ void __launch_bounds__(256)
+    unpack_kernel(const float* __restrict__ in, uint32_t k, uint32_t rows, float* __restrict__ cols, uint64_t ld,
+                  uint32_t dst) {
+    const uint32_t t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= k * rows) return;
+    const uint32_t i = t / rows, r = t - i * rows;
+    cols[r * ld + dst + i] = in[t];
+}
+
+// out[i] = rho[list[i]] for i < k1, rho[start + i - k1] for k1 <= i < k1 + k2.
+__global__ void __launch_bounds__(256)
+    rho_pack_kernel(const float* __restrict__ rho, const uint32_t* __restrict__ list, uint32_t k1, uint32_t start,
+                    uint32_t k2, float* __restrict__ out) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < k1) out[i] = rho[list[i]];
+    else if (i < k1 + k2) out[i] = rho[start + i - k1];
+}
+
+}  // namespace slab
+}  // namespace forge

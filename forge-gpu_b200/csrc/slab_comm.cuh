@@ -1,0 +1,354 @@
+// Host side of the sharded SPH step's neighbour exchange, over the library's
+// own NCCL communicator (NCCL 2.x, loaded at run time with dlopen so that
+// single-GPU users need no NCCL). Included at the end of forge_sph.cu.
+//
+// Per step and rank (x-slab [lo, hi), one neighbour on each side at most):
+//   forge_slab_exchange  (round 1, after the force pass of the previous step)
+//     classify migrants (x outside the slab)   -> pack their records
+//     remove them from the owned columns        (compact, tail into holes)
+//     classify halo rows (x within reach)      -> pack their records
+//     send [migrants | halo] to each neighbour, counts first, then payload
+//     append arrivals as owned, then ghosts: halo from L, halo from R,
+//     our migrants to L, our migrants to R (they sit just across the face)
+//   forge_slab_exchange_rho (round 2, after density; sizes known, no sync)
+//     send rho of [halo sent to X, arrivals from X] to X; X's values land in
+//     [halo from X, our migrants to X].
+// Three stream synchronisations per round 1 (two list sizes, one count
+// exchange); everything else is enqueued.
+#pragma once
+
+#include <dlfcn.h>
+#include <nccl.h>
+
+namespace {
+
+struct NcclApi {
+    bool loaded = false;
+    ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+    ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*GroupStart)() = nullptr;
+    ncclResult_t (*GroupEnd)() = nullptr;
+    ncclResult_t (*Send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*Recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    const char* (*GetErrorString)(ncclResult_t) = nullptr;
+};
+
+std::mutex g_nccl_mu;
+NcclApi g_nccl;
+
+int nccl_load() {
+    std::lock_guard<std::mutex> lock(g_nccl_mu);
+    if (g_nccl.loaded) return FORGE_OK;
+    // Prefer a libnccl already in the process (e.g. the one torch loaded).
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return set_error(FORGE_ERR_NCCL, "libnccl.so.2 not found: %s", dlerror());
+#define FORGE_NCCL_SYM(name)                                                                        \
+    *reinterpret_cast<void**>(&g_nccl.name) = dlsym(h, "nccl" #name);                               \
+    if (!g_nccl.name) return set_error(FORGE_ERR_NCCL, "libnccl.so.2 lacks nccl" #name);
+    FORGE_NCCL_SYM(GetUniqueId)
+    FORGE_NCCL_SYM(CommInitRank)
+    FORGE_NCCL_SYM(CommDestroy)
+    FORGE_NCCL_SYM(GroupStart)
+    FORGE_NCCL_SYM(GroupEnd)
+    FORGE_NCCL_SYM(Send)
+    FORGE_NCCL_SYM(Recv)
+    FORGE_NCCL_SYM(GetErrorString)
+#undef FORGE_NCCL_SYM
+    g_nccl.loaded = true;
+    return FORGE_OK;
+}
+
+#define FORGE_NCCL(call)                                                                            \
+    do {                                                                                            \
+        ncclResult_t r_ = (call);                                                                   \
+        if (r_ != ncclSuccess)                                                                      \
+            return set_error(FORGE_ERR_NCCL, "%s failed: %s", #call, g_nccl.GetErrorString(r_));    \
+    } while (0)
+
+constexpr uint32_t kSlabRows = 7;  // x, y, z, vx, vy, vz, id bits
+
+}  // namespace
+
+struct forge_slab_comm {
+    int device = 0, rank = 0, world = 1;
+    int left = -1, right = -1;
+    uint64_t cap = 0;
+    float lo = 0.f, hi = 0.f, reach = 0.f;
+    ncclComm_t comm = nullptr;
+    forge_slab* sel = nullptr;
+    uint32_t* idx = nullptr;       // classify output, 2 cap
+    uint32_t* counts = nullptr;    // 3 device words
+    uint32_t* hcounts = nullptr;   // 3 pinned host words
+    uint32_t* halo_l = nullptr;    // halo lists of the last round (cap each)
+    uint32_t* halo_r = nullptr;
+    float* send_l = nullptr;       // records, cap x 7 each
+    float* send_r = nullptr;
+    float* recv_l = nullptr;
+    float* recv_r = nullptr;
+    float* rho_send_l = nullptr;   // cap each
+    float* rho_send_r = nullptr;
+    float* rho_recv_l = nullptr;
+    float* rho_recv_r = nullptr;
+    uint64_t* dcount = nullptr;    // [send l(2) | send r(2) | recv l(2) | recv r(2)]
+    uint64_t* hcount = nullptr;    // pinned mirror
+    // bookkeeping of the last round 1
+    uint32_t n_hl = 0, n_hr = 0;          // halo rows sent left / right
+    uint32_t n_ml = 0, n_mr = 0;          // migrants sent left / right
+    uint32_t arr_l = 0, n_arr_l = 0;      // arrivals from left: columns [arr_l, arr_l + n_arr_l)
+    uint32_t arr_r = 0, n_arr_r = 0;
+    uint32_t g_hl = 0, n_ghl = 0;         // ghost blocks: halo from left
+    uint32_t g_hr = 0, n_ghr = 0;         // halo from right
+    uint32_t g_ml = 0, g_mr = 0;          // our migrants to left / right
+    bool have_round = false;
+};
+
+namespace {
+
+void slab_comm_free(forge_slab_comm* c) {
+    DeviceScope scope(c->device);
+    if (c->comm) g_nccl.CommDestroy(c->comm);
+    forge_slab_destroy(c->sel);
+    for (void* p : {(void*)c->idx, (void*)c->counts, (void*)c->halo_l, (void*)c->halo_r, (void*)c->send_l,
+                    (void*)c->send_r, (void*)c->recv_l, (void*)c->recv_r, (void*)c->rho_send_l,
+                    (void*)c->rho_send_r, (void*)c->rho_recv_l, (void*)c->rho_recv_r, (void*)c->dcount})
+        cudaFree(p);
+    cudaFreeHost(c->hcounts);
+    cudaFreeHost(c->hcount);
+    delete c;
+}
+
+int pack(float* cols, uint64_t ld, const uint32_t* idx, uint32_t k, float* out, cudaStream_t st) {
+    if (!k) return FORGE_OK;
+    slab::pack_kernel<<<grid_blocks((uint64_t)k * kSlabRows, 256), 256, 0, st>>>(cols, ld, kSlabRows, idx, k, out);
+    FORGE_LAUNCHED();
+    return FORGE_OK;
+}
+
+int unpack(const float* in, uint32_t k, float* cols, uint64_t ld, uint32_t dst, cudaStream_t st) {
+    if (!k) return FORGE_OK;
+    slab::unpack_kernel<<<grid_blocks((uint64_t)k * kSlabRows, 256), 256, 0, st>>>(in, k, kSlabRows, cols, ld, dst);
+    FORGE_LAUNCHED();
+    return FORGE_OK;
+}
+
+// Runs forge_slab_classify and reads the three list sizes back (one sync).
+int classify_sync(forge_slab_comm* c, const float* x, uint64_t n, uint32_t flags, uint32_t sizes[3], cudaStream_t st) {
+    int rc = forge_slab_classify(c->sel, x, n, c->lo, c->hi, c->reach, flags, c->idx, c->counts, st);
+    if (rc != FORGE_OK) return rc;
+    FORGE_CUDA(cudaMemcpyAsync(c->hcounts, c->counts, 3 * sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
+    FORGE_CUDA(cudaStreamSynchronize(st));
+    for (int i = 0; i < 3; ++i) sizes[i] = c->hcounts[i];
+    return FORGE_OK;
+}
+
+}  // namespace
+
+extern "C" int forge_nccl_unique_id(uint8_t* out) {
+    if (!out) return set_error(FORGE_ERR_INVALID_ARG, "forge_nccl_unique_id: out is NULL");
+    int rc = nccl_load();
+    if (rc != FORGE_OK) return rc;
+    ncclUniqueId id;
+    FORGE_NCCL(g_nccl.GetUniqueId(&id));
+    memcpy(out, id.internal, NCCL_UNIQUE_ID_BYTES);
+    return FORGE_OK;
+}
+
+extern "C" int forge_slab_comm_create(const uint8_t* id, int rank, int world, int device, uint64_t capacity,
+                                      float lo, float hi, float reach, forge_slab_comm** out) {
+    if (!out || !id) return set_error(FORGE_ERR_INVALID_ARG, "forge_slab_comm_create: NULL argument");
+    *out = nullptr;
+    if (world < 1 || rank < 0 || rank >= world || capacity == 0 || capacity >= 0x7fffffffull)
+        return set_error(FORGE_ERR_INVALID_ARG, "forge_slab_comm_create: bad rank/world/capacity");
+    int rc = nccl_load();
+    if (rc != FORGE_OK) return rc;
+    FORGE_DEVICE_SCOPE(device);
+    forge_slab_comm* c = new forge_slab_comm;
+    c->device = device;
+    c->rank = rank;
+    c->world = world;
+    c->left = rank > 0 ? rank - 1 : -1;
+    c->right = rank < world - 1 ? rank + 1 : -1;
+    c->cap = capacity;
+    c->lo = lo;
+    c->hi = hi;
+    c->reach = reach;
+    const size_t m = capacity;
+    bool ok = dalloc(&c->idx, 2 * m) == cudaSuccess && dalloc(&c->counts, 3) == cudaSuccess &&
+              dalloc(&c->halo_l, m) == cudaSuccess && dalloc(&c->halo_r, m) == cudaSuccess &&
+              dalloc(&c->send_l, m * kSlabRows) == cudaSuccess && dalloc(&c->send_r, m * kSlabRows) == cudaSuccess &&
+              dalloc(&c->recv_l, m * kSlabRows) == cudaSuccess && dalloc(&c->recv_r, m * kSlabRows) == cudaSuccess &&
+              dalloc(&c->rho_send_l, m) == cudaSuccess && dalloc(&c->rho_send_r, m) == cudaSuccess &&
+              dalloc(&c->rho_recv_l, m) == cudaSuccess && dalloc(&c->rho_recv_r, m) == cudaSuccess &&
+              dalloc(&c->dcount, 8) == cudaSuccess &&
+              cudaMallocHost(&c->hcounts, 3 * sizeof(uint32_t)) == cudaSuccess &&
+              cudaMallocHost(&c->hcount, 8 * sizeof(uint64_t)) == cudaSuccess;
+    if (!ok) {
+        slab_comm_free(c);
+        return set_error(FORGE_ERR_CUDA, "forge_slab_comm_create: allocation failed (capacity %llu)",
+                         (unsigned long long)capacity);
+    }
+    rc = forge_slab_create(capacity, device, &c->sel);
+    if (rc != FORGE_OK) {
+        slab_comm_free(c);
+        return rc;
+    }
+    ncclUniqueId uid;
+    memcpy(uid.internal, id, NCCL_UNIQUE_ID_BYTES);
+    ncclResult_t r = g_nccl.CommInitRank(&c->comm, world, uid, rank);
+    if (r != ncclSuccess) {
+        c->comm = nullptr;
+        slab_comm_free(c);
+        return set_error(FORGE_ERR_NCCL, "ncclCommInitRank failed: %s", g_nccl.GetErrorString(r));
+    }
+    *out = c;
+    return FORGE_OK;
+}
+
+extern "C" void forge_slab_comm_destroy(forge_slab_comm* c) {
+    if (c) slab_comm_free(c);
+}
+
+extern "C" int forge_slab_exchange(forge_slab_comm* c, float* cols, uint64_t ld, uint64_t n_own, int migrate,
+                                   uint64_t* n_own_out, uint64_t* n_ghost_out, void* stream) {
+    if (!c || !cols || !n_own_out || !n_ghost_out)
+        return set_error(FORGE_ERR_INVALID_ARG, "forge_slab_exchange: NULL argument");
+    if (n_own > c->cap || ld < c->cap)
+        return set_error(FORGE_ERR_CAPACITY, "forge_slab_exchange: n_own or ld does not fit the capacity");
+    FORGE_DEVICE_SCOPE(c->device);
+    cudaStream_t st = as_stream(stream);
+    const uint32_t sides = (c->left >= 0 ? 1u : 0u) | (c->right >= 0 ? 2u : 0u);
+    uint32_t sz[3] = {0, 0, 0};
+    int rc;
+    // 1. migrants: pack, then remove from the owned columns
+    uint32_t ml = 0, mr = 0, keep = (uint32_t)n_own;
+    if (migrate && n_own) {
+        rc = classify_sync(c, cols, n_own, sides, sz, st);
+        if (rc != FORGE_OK) return rc;
+        ml = sz[1];
+        mr = sz[2];
+        if ((rc = pack(cols, ld, c->idx + sz[0], ml, c->send_l, st)) != FORGE_OK) return rc;
+        if ((rc = pack(cols, ld, c->idx + sz[0] + ml, mr, c->send_r, st)) != FORGE_OK) return rc;
+        if ((rc = forge_slab_compact(cols, ld, kSlabRows, n_own, c->idx, sz[0], st)) != FORGE_OK) return rc;
+        keep = (uint32_t)n_own - sz[0];
+    }
+    // 2. halo rows of the remaining owned particles
+    uint32_t hl = 0, hr = 0;
+    if (keep) {
+        rc = classify_sync(c, cols, keep, sides | 4u, sz, st);
+        if (rc != FORGE_OK) return rc;
+        hl = sz[1];
+        hr = sz[2];
+    }
+    if ((uint64_t)ml + hl > c->cap || (uint64_t)mr + hr > c->cap)
+        return set_error(FORGE_ERR_CAPACITY, "forge_slab_exchange: message exceeds capacity");
+    if (hl) FORGE_CUDA(cudaMemcpyAsync(c->halo_l, c->idx + sz[0], hl * 4, cudaMemcpyDeviceToDevice, st));
+    if (hr) FORGE_CUDA(cudaMemcpyAsync(c->halo_r, c->idx + sz[0] + hl, hr * 4, cudaMemcpyDeviceToDevice, st));
+    if ((rc = pack(cols, ld, c->halo_l, hl, c->send_l + (size_t)ml * kSlabRows, st)) != FORGE_OK) return rc;
+    if ((rc = pack(cols, ld, c->halo_r, hr, c->send_r + (size_t)mr * kSlabRows, st)) != FORGE_OK) return rc;
+    // 3. counts
+    c->hcount[0] = ml;
+    c->hcount[1] = hl;
+    c->hcount[2] = mr;
+    c->hcount[3] = hr;
+    c->hcount[4] = c->hcount[5] = c->hcount[6] = c->hcount[7] = 0;
+    FORGE_CUDA(cudaMemcpyAsync(c->dcount, c->hcount, 8 * sizeof(uint64_t), cudaMemcpyHostToDevice, st));
+    FORGE_NCCL(g_nccl.GroupStart());
+    if (c->left >= 0) {
+        FORGE_NCCL(g_nccl.Send(c->dcount + 0, 2, ncclUint64, c->left, c->comm, st));
+        FORGE_NCCL(g_nccl.Recv(c->dcount + 4, 2, ncclUint64, c->left, c->comm, st));
+    }
+    if (c->right >= 0) {
+        FORGE_NCCL(g_nccl.Send(c->dcount + 2, 2, ncclUint64, c->right, c->comm, st));
+        FORGE_NCCL(g_nccl.Recv(c->dcount + 6, 2, ncclUint64, c->right, c->comm, st));
+    }
+    FORGE_NCCL(g_nccl.GroupEnd());
+    FORGE_CUDA(cudaMemcpyAsync(c->hcount + 4, c->dcount + 4, 4 * sizeof(uint64_t), cudaMemcpyDeviceToHost, st));
+    FORGE_CUDA(cudaStreamSynchronize(st));
+    const uint64_t aml = c->hcount[4], ahl = c->hcount[5], amr = c->hcount[6], ahr = c->hcount[7];
+    if (aml + ahl > c->cap || amr + ahr > c->cap)
+        return set_error(FORGE_ERR_CAPACITY, "forge_slab_exchange: incoming message exceeds capacity");
+    const uint64_t n_new = keep + aml + amr;
+    const uint64_t ng = ahl + ahr + ml + mr;
+    if (n_new + ng > ld) return set_error(FORGE_ERR_CAPACITY, "forge_slab_exchange: owned + ghosts exceed ld");
+    // 4. payload
+    FORGE_NCCL(g_nccl.GroupStart());
+    if (c->left >= 0) {
+        if (ml + hl) FORGE_NCCL(g_nccl.Send(c->send_l, (ml + hl) * kSlabRows, ncclFloat32, c->left, c->comm, st));
+        if (aml + ahl) FORGE_NCCL(g_nccl.Recv(c->recv_l, (aml + ahl) * kSlabRows, ncclFloat32, c->left, c->comm, st));
+    }
+    if (c->right >= 0) {
+        if (mr + hr) FORGE_NCCL(g_nccl.Send(c->send_r, (mr + hr) * kSlabRows, ncclFloat32, c->right, c->comm, st));
+        if (amr + ahr) FORGE_NCCL(g_nccl.Recv(c->recv_r, (amr + ahr) * kSlabRows, ncclFloat32, c->right, c->comm, st));
+    }
+    FORGE_NCCL(g_nccl.GroupEnd());
+    // 5. arrivals, then ghosts
+    uint32_t o = keep;
+    if ((rc = unpack(c->recv_l, (uint32_t)aml, cols, ld, o, st)) != FORGE_OK) return rc;
+    c->arr_l = o;
+    c->n_arr_l = (uint32_t)aml;
+    o += (uint32_t)aml;
+    if ((rc = unpack(c->recv_r, (uint32_t)amr, cols, ld, o, st)) != FORGE_OK) return rc;
+    c->arr_r = o;
+    c->n_arr_r = (uint32_t)amr;
+    o += (uint32_t)amr;
+    c->g_hl = o;
+    c->n_ghl = (uint32_t)ahl;
+    if ((rc = unpack(c->recv_l + aml * kSlabRows, (uint32_t)ahl, cols, ld, o, st)) != FORGE_OK) return rc;
+    o += (uint32_t)ahl;
+    c->g_hr = o;
+    c->n_ghr = (uint32_t)ahr;
+    if ((rc = unpack(c->recv_r + amr * kSlabRows, (uint32_t)ahr, cols, ld, o, st)) != FORGE_OK) return rc;
+    o += (uint32_t)ahr;
+    c->g_ml = o;
+    if ((rc = unpack(c->send_l, ml, cols, ld, o, st)) != FORGE_OK) return rc;
+    o += ml;
+    c->g_mr = o;
+    if ((rc = unpack(c->send_r, mr, cols, ld, o, st)) != FORGE_OK) return rc;
+    c->n_hl = hl;
+    c->n_hr = hr;
+    c->n_ml = ml;
+    c->n_mr = mr;
+    c->have_round = true;
+    *n_own_out = n_new;
+    *n_ghost_out = ng;
+    return FORGE_OK;
+}
+
+extern "C" int forge_slab_exchange_rho(forge_slab_comm* c, float* rho, void* stream) {
+    if (!c || !rho) return set_error(FORGE_ERR_INVALID_ARG, "forge_slab_exchange_rho: NULL argument");
+    if (!c->have_round) return set_error(FORGE_ERR_INVALID_ARG, "forge_slab_exchange_rho: no exchange round yet");
+    FORGE_DEVICE_SCOPE(c->device);
+    cudaStream_t st = as_stream(stream);
+    const uint32_t kl = c->n_hl + c->n_arr_l, kr = c->n_hr + c->n_arr_r;
+    if (kl)
+        slab::rho_pack_kernel<<<grid_blocks(kl, 256), 256, 0, st>>>(rho, c->halo_l, c->n_hl, c->arr_l, c->n_arr_l,
+                                                                     c->rho_send_l);
+    if (kr)
+        slab::rho_pack_kernel<<<grid_blocks(kr, 256), 256, 0, st>>>(rho, c->halo_r, c->n_hr, c->arr_r, c->n_arr_r,
+                                                                     c->rho_send_r);
+    FORGE_LAUNCHED();
+    // from X: [X's halo rows to us | our migrants to X]
+    const uint32_t il = c->n_ghl + c->n_ml, ir = c->n_ghr + c->n_mr;
+    FORGE_NCCL(g_nccl.GroupStart());
+    if (c->left >= 0) {
+        if (kl) FORGE_NCCL(g_nccl.Send(c->rho_send_l, kl, ncclFloat32, c->left, c->comm, st));
+        if (il) FORGE_NCCL(g_nccl.Recv(c->rho_recv_l, il, ncclFloat32, c->left, c->comm, st));
+    }
+    if (c->right >= 0) {
+        if (kr) FORGE_NCCL(g_nccl.Send(c->rho_send_r, kr, ncclFloat32, c->right, c->comm, st));
+        if (ir) FORGE_NCCL(g_nccl.Recv(c->rho_recv_r, ir, ncclFloat32, c->right, c->comm, st));
+    }
+    FORGE_NCCL(g_nccl.GroupEnd());
+    auto d2d = [&](float* dst, const float* src, uint32_t k) -> int {
+        if (k) FORGE_CUDA(cudaMemcpyAsync(dst, src, k * sizeof(float), cudaMemcpyDeviceToDevice, st));
+        return FORGE_OK;
+    };
+    int rc;
+    if ((rc = d2d(rho + c->g_hl, c->rho_recv_l, c->n_ghl)) != FORGE_OK) return rc;
+    if ((rc = d2d(rho + c->g_ml, c->rho_recv_l + c->n_ghl, c->n_ml)) != FORGE_OK) return rc;
+    if ((rc = d2d(rho + c->g_hr, c->rho_recv_r, c->n_ghr)) != FORGE_OK) return rc;
+    if ((rc = d2d(rho + c->g_mr, c->rho_recv_r + c->n_ghr, c->n_mr)) != FORGE_OK) return rc;
+    return FORGE_OK;
+}

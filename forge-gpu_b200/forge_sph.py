@@ -64,6 +64,8 @@ EXPORTED = (
     "forge_sort_pairs_static",
     "forge_sph_force_step",
     "forge_slab_create", "forge_slab_destroy", "forge_slab_classify", "forge_slab_compact",
+    "forge_nccl_unique_id", "forge_slab_comm_create", "forge_slab_comm_destroy", "forge_slab_exchange",
+    "forge_slab_exchange_rho",
 )
 STATIC_SORT_MAX_N = 1 << 20
 
@@ -120,6 +122,11 @@ def lib() -> ctypes.CDLL:
                                  vp, vp, u64, vp]),
         "forge_grid_profile_enable": (i32, [vp, u32]),
         "forge_sort_pairs_static": (i32, [vp, vp, u64, u32, u32, vp]),
+        "forge_nccl_unique_id": (i32, [ctypes.c_char_p]),
+        "forge_slab_comm_create": (i32, [ctypes.c_char_p, i32, i32, i32, u64, f32, f32, f32, pvp]),
+        "forge_slab_comm_destroy": (None, [vp]),
+        "forge_slab_exchange": (i32, [vp, vp, u64, u64, i32, ctypes.POINTER(u64), ctypes.POINTER(u64), vp]),
+        "forge_slab_exchange_rho": (i32, [vp, vp, vp]),
         "forge_slab_create": (i32, [u64, i32, pvp]),
         "forge_slab_destroy": (None, [vp]),
         "forge_slab_classify": (i32, [vp, vp, u64, f32, f32, f32, u32, vp, vp, vp]),

@@ -113,6 +113,103 @@ class Exchanger:
         return a, b
 
 
+class PyComm:
+    """The two exchange rounds in Python over torch.distributed (any backend;
+    gloo for CPU ranks and tests). Same protocol as the library's NCCL path."""
+
+    def __init__(self, run, dist, comm_device=None):
+        self.run = run
+        self.ex = Exchanger(dist, run.geo.rank, run.geo.world, run.device, comm_device)
+
+    def exchange(self, migrate: bool) -> None:
+        """Round 1: migrants leave, [migrants | halo] go to each neighbour,
+        arrivals and ghosts are appended."""
+        run = self.run
+        g, C, be = run.geo, run.cols, run.backend
+        n_own = run.n
+        flags = (0 if g.first else 1) | (0 if g.last else 2)
+        if migrate:
+            mig, mig_l, mig_r = be.classify(C[0], n_own, g.lo, g.hi, run.reach, flags)
+        else:
+            mig = mig_l = mig_r = torch.empty(0, dtype=torch.int64, device=C.device)
+        rows_ml, rows_mr = C[:, mig_l], C[:, mig_r]  # gathered before the compaction moves columns
+        be.compact(C, n_own, mig)
+        keep = n_own - mig.numel()
+        _, hl, hr = be.classify(C[0], keep, g.lo, g.hi, run.reach, flags | 4)
+        send_l = torch.cat([rows_ml, C[:, hl]], dim=1).t()
+        send_r = torch.cat([rows_mr, C[:, hr]], dim=1).t()
+        got_l, got_r, cnt_l, cnt_r = self.ex.swap_counted(send_l, (mig_l.numel(), hl.numel()),
+                                                          send_r, (mig_r.numel(), hr.numel()), _NCOL)
+        am_l, ah_l = cnt_l
+        am_r, ah_r = cnt_r
+        n_new = keep + am_l + am_r
+        ng = ah_l + ah_r + mig_l.numel() + mig_r.numel()
+        run._need(n_new + ng + 1)
+        C[:, keep:keep + am_l] = got_l[:am_l].t()
+        C[:, keep + am_l:n_new] = got_r[:am_r].t()
+        o = n_new
+        blocks = {}
+        for name, blk in (("hl", got_l[am_l:].t()), ("hr", got_r[am_r:].t()), ("ml", rows_ml), ("mr", rows_mr)):
+            w = blk.shape[1]
+            C[:, o:o + w] = blk
+            blocks[name] = torch.arange(o, o + w, device=C.device)
+            o += w
+        arr_l = torch.arange(keep, keep + am_l, device=C.device)
+        arr_r = torch.arange(keep + am_l, n_new, device=C.device)
+        # round 2: rho of [halo sent to X, arrivals from X] goes to X; X's rho
+        # fills [halo from X, our migrants to X] in the same order.
+        self.rho_send = (torch.cat([hl, arr_l]), torch.cat([hr, arr_r]))
+        self.rho_slot = (torch.cat([blocks["hl"], blocks["ml"]]), torch.cat([blocks["hr"], blocks["mr"]]))
+        run.n, run.ng = n_new, ng
+
+    def exchange_rho(self, rho: torch.Tensor) -> None:
+        """Round 2: ghosts receive their owners' densities."""
+        send_l, send_r = self.rho_send
+        slot_l, slot_r = self.rho_slot
+        got_l, got_r = self.ex.swap_known(rho[send_l].reshape(-1, 1), slot_l.numel(),
+                                          rho[send_r].reshape(-1, 1), slot_r.numel(), 1)
+        rho[slot_l] = got_l.flatten()
+        rho[slot_r] = got_r.flatten()
+
+
+class NcclComm:
+    """The two exchange rounds inside libforge_sph (forge_slab_exchange,
+    forge_slab_exchange_rho) over the library's own NCCL communicator: no
+    Python between the kernels and the NCCL calls of a round."""
+
+    def __init__(self, run, dist, forge_sph):
+        self.run, self.f = run, forge_sph
+        self.L = forge_sph.lib()
+        uid = ctypes.create_string_buffer(128)
+        if run.geo.rank == 0:
+            forge_sph.check(self.L.forge_nccl_unique_id(uid))
+        obj = [uid.raw if run.geo.rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        uid = ctypes.create_string_buffer(obj[0], 128)
+        h = ctypes.c_void_p()
+        forge_sph.check(self.L.forge_slab_comm_create(uid, run.geo.rank, run.geo.world, run.device.index,
+                                                      run.capacity, run.geo.lo, run.geo.hi, run.reach,
+                                                      ctypes.byref(h)))
+        self.h = h
+
+    def __del__(self):
+        h = getattr(self, "h", None)
+        if h and self.f._lib is not None:
+            self.f._lib.forge_slab_comm_destroy(h)
+            self.h = None
+
+    def exchange(self, migrate: bool) -> None:
+        run = self.run
+        n_own, ng = ctypes.c_uint64(), ctypes.c_uint64()
+        self.f.check(self.L.forge_slab_exchange(self.h, run.cols.data_ptr(), run.cols.stride(0), run.n,
+                                                1 if migrate else 0, ctypes.byref(n_own), ctypes.byref(ng),
+                                                torch.cuda.current_stream().cuda_stream))
+        run.n, run.ng = n_own.value, ng.value
+
+    def exchange_rho(self, rho: torch.Tensor) -> None:
+        self.f.check(self.L.forge_slab_exchange_rho(self.h, rho.data_ptr(), torch.cuda.current_stream().cuda_stream))
+
+
 class SlabRun:
     """One rank's share of a sharded SPH run.
 
@@ -131,14 +228,17 @@ class SlabRun:
       round 2 (after density): for every ghost the owner sends its exact
         density (counts known from round 1, so no count exchange).
     Leaving particles are removed by moving tail columns into their holes, so
-    per step only halo- and migrant-sized data moves.
+    per step only halo- and migrant-sized data moves. comm="nccl" runs both
+    rounds in the library (GPU ranks, NCCL); comm="torch" runs them in Python
+    over torch.distributed (gloo / CPU ranks).
     """
 
     def __init__(self, dist, rank: int, world: int, cfg, pos, vel, backend, device: torch.device,
-                 x_range=(0.0, 1.0), order_by_id: bool = False, comm_device=None, capacity: int | None = None):
+                 x_range=(0.0, 1.0), order_by_id: bool = False, comm_device=None, capacity: int | None = None,
+                 comm: str = "torch", forge_sph=None):
         self.cfg, self.backend, self.device = cfg, backend, device
         self.geo = SlabGeometry(rank, world, x_range[0], x_range[1], cfg.h)
-        self.ex = Exchanger(dist, rank, world, device, comm_device)
+        self.reach = cfg.h * (1.0 + 1e-5)
         self.order_by_id = order_by_id
         px = torch.as_tensor(pos[0])
         m = self.geo.owned_mask(px)
@@ -150,9 +250,9 @@ class SlabRun:
         self.cols[:, :n_own] = own.to(device)
         self.n = n_own
         self.ng = 0
-        self.last_halo = 0
         self.timing = None  # set to a list to record per-phase CUDA events
-        self._round1(migrate=False)  # initial halo
+        self.comm = NcclComm(self, dist, forge_sph) if comm == "nccl" else PyComm(self, dist, comm_device)
+        self.comm.exchange(migrate=False)  # initial halo
 
     def _mark(self, name):
         if self.timing is not None:
@@ -169,6 +269,10 @@ class SlabRun:
         return self.n
 
     @property
+    def last_halo(self) -> int:
+        return self.ng
+
+    @property
     def state(self) -> torch.Tensor:
         """(n_own, 7) view: x, y, z, vx, vy, vz, id bits."""
         return self.cols[:, :self.n].t()
@@ -180,76 +284,31 @@ class SlabRun:
         if n > self.capacity:
             raise RuntimeError(f"slab rank {self.geo.rank}: {n} particles exceed capacity {self.capacity}")
 
-    def _flags(self):
-        return (0 if self.geo.first else 1) | (0 if self.geo.last else 2)
-
-    def _round1(self, migrate: bool) -> None:
-        """Remove migrants from the owned set, send [migrants | halo] to each
-        neighbour, append arrivals and ghosts, and record the ghost-density
-        bookkeeping for round 2."""
-        g, C, be = self.geo, self.cols, self.backend
-        n_own = self.n
-        reach = self.cfg.h * (1.0 + 1e-5)
-        if migrate:
-            mig, mig_l, mig_r = be.classify(C[0], n_own, g.lo, g.hi, reach, self._flags())
-        else:
-            mig = mig_l = mig_r = torch.empty(0, dtype=torch.int64, device=C.device)
-        rows_ml, rows_mr = C[:, mig_l], C[:, mig_r]  # gathered before the compaction moves columns
-        be.compact(C, n_own, mig)
-        keep = n_own - mig.numel()
-        _, hl, hr = be.classify(C[0], keep, g.lo, g.hi, reach, self._flags() | 4)
-        send_l = torch.cat([rows_ml, C[:, hl]], dim=1).t()
-        send_r = torch.cat([rows_mr, C[:, hr]], dim=1).t()
-        got_l, got_r, cnt_l, cnt_r = self.ex.swap_counted(send_l, (mig_l.numel(), hl.numel()),
-                                                          send_r, (mig_r.numel(), hr.numel()), _NCOL)
-        am_l, ah_l = cnt_l
-        am_r, ah_r = cnt_r
-        n_new = keep + am_l + am_r
-        ng = ah_l + ah_r + mig_l.numel() + mig_r.numel()
-        self._need(n_new + ng + 1)
-        C[:, keep:keep + am_l] = got_l[:am_l].t()
-        C[:, keep + am_l:n_new] = got_r[:am_r].t()
-        o = n_new
-        blocks = {}
-        for name, blk in (("hl", got_l[am_l:].t()), ("hr", got_r[am_r:].t()), ("ml", rows_ml), ("mr", rows_mr)):
-            w = blk.shape[1]
-            C[:, o:o + w] = blk
-            blocks[name] = torch.arange(o, o + w, device=C.device)
-            o += w
-        arr_l = torch.arange(keep, keep + am_l, device=C.device)
-        arr_r = torch.arange(keep + am_l, n_new, device=C.device)
-        # round 2: rho of [halo sent to X, arrivals from X] goes to X; X's rho
-        # fills [halo from X, our migrants to X] in the same order.
-        self.rho_send = (torch.cat([hl, arr_l]), torch.cat([hr, arr_r]))
-        self.rho_slot = (torch.cat([blocks["hl"], blocks["ml"]]), torch.cat([blocks["hr"], blocks["mr"]]))
-        self.n, self.ng = n_new, ng
-        self.last_halo = ng
-
     def step(self) -> None:
-        g, C = self.geo, self.cols
+        C = self.cols
         self._mark("start")
         n_own, n = self.n, self.n + self.ng
-        send_l, send_r = self.rho_send
-        slot_l, slot_r = self.rho_slot
         perm = None
         if self.order_by_id:  # test mode: neighbour order identical to the unsharded run
             perm = torch.argsort(C[6, :n].view(torch.int32), stable=True)
             C[:, :n] = C[:, perm]
-            inv = torch.empty_like(perm)
-            inv[perm] = torch.arange(n, device=perm.device)
-            send_l, send_r, slot_l, slot_r = inv[send_l], inv[send_r], inv[slot_l], inv[slot_r]
         rho = self.backend.density([C[k, :n] for k in range(3)], n)
-        self._mark("density")
-        got_l, got_r = self.ex.swap_known(rho[send_l].reshape(-1, 1), slot_l.numel(),
-                                          rho[send_r].reshape(-1, 1), slot_r.numel(), 1)
-        rho[slot_l] = got_l.flatten()
-        rho[slot_r] = got_r.flatten()
-        self._mark("ghost_rho")
-        self.backend.force_step([C[k, :n] for k in range(6)], rho, n, n if perm is not None else n_own)
-        self._mark("force")
-        if perm is not None:  # restore the owned-then-ghost layout
+        if perm is not None:  # the exchange works in the owned-then-ghost layout
+            r = torch.empty_like(rho)
+            r[perm] = rho
+            rho = r
             C[:, perm] = C[:, :n].clone()
-        self._round1(migrate=True)
+        self._mark("density")
+        self.comm.exchange_rho(rho)
+        self._mark("ghost_rho")
+        if perm is not None:
+            rho = rho[perm]
+            C[:, :n] = C[:, perm]
+        self.backend.force_step([C[k, :n] for k in range(6)], rho, n, n if perm is not None else n_own)
+        if perm is not None:
+            C[:, perm] = C[:, :n].clone()
+        self._mark("force")
+        self.comm.exchange(migrate=True)
         self._mark("exchange")
 
 

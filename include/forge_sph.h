@@ -299,6 +299,35 @@ FORGE_API int forge_slab_classify(forge_slab* h, const float* x, uint64_t n, flo
 FORGE_API int forge_slab_compact(float* cols, uint64_t ld, uint32_t rows, uint64_t n, const uint32_t* gone,
                                  uint64_t k, void* stream);
 
+/* Neighbour exchange of the sharded SPH step over the library's own NCCL
+ * communicator (libnccl.so.2 is loaded at run time; single-GPU use needs no
+ * NCCL). One rank per GPU owns the x-slab [lo, hi); particle state is a
+ * row-major 7 x ld float buffer (rows x, y, z, vx, vy, vz, id bits), owned
+ * columns first, ghosts after them. No counterpart in the reference. */
+typedef struct forge_slab_comm forge_slab_comm;
+
+/* NCCL unique id (128 bytes) made on one rank and shared by the caller. */
+FORGE_API int forge_nccl_unique_id(uint8_t* out);
+
+/* Creates the communicator (collective over all ranks) and buffers for up
+ * to `capacity` particles per message / per classification. reach = halo
+ * width (h, with a small margin). */
+FORGE_API int forge_slab_comm_create(const uint8_t* id, int rank, int world, int device, uint64_t capacity,
+                                     float lo, float hi, float reach, forge_slab_comm** out);
+FORGE_API void forge_slab_comm_destroy(forge_slab_comm* c);
+
+/* Round 1 (after a step's force pass, or once at start with migrate = 0):
+ * migrants (x outside the slab) leave the owned columns and go to the
+ * neighbour, together with the halo rows (owned particles within reach of a
+ * face); arrivals are appended to the owned columns, then the ghosts.
+ * Synchronises `stream` three times (list sizes and counts). */
+FORGE_API int forge_slab_exchange(forge_slab_comm* c, float* cols, uint64_t ld, uint64_t n_own, int migrate,
+                                  uint64_t* n_own_out, uint64_t* n_ghost_out, void* stream);
+
+/* Round 2 (after density): every ghost receives its owner's density in
+ * rho[] (indexed like the columns). No host synchronisation. */
+FORGE_API int forge_slab_exchange_rho(forge_slab_comm* c, float* rho, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Benchmark aid (no reference counterpart; the reference only times the    */
 /* whole run with a wall clock, manifest_runner.rs:40-80).                  */
