@@ -32,8 +32,9 @@ import numpy as np  # noqa: E402
 import workloads  # noqa: E402
 
 # DRAM bytes (read + write) per force+epilogue launch per particle, from the
-# ncu capture summarised in profiles/ (None until captured).
-FORCE_TRAFFIC_B_PER_PARTICLE = None
+# ncu capture in profiles/sph_step_sharded16m_ncu.md (1,099 MB for 16,384,000
+# particles, cfg3); applied to cfg3-like workloads only.
+FORCE_TRAFFIC_B_PER_PARTICLE = 1099.0e6 / 16384000
 
 
 def peaks():
@@ -429,7 +430,7 @@ def main():
     dom = max(PHASES, key=lambda k: phase_ms[k])
     achieved = ab[dom] * cfg.n / (phase_ms[dom] / 1e3) / 1e9
     traffic = None
-    if dom == "force" and FORCE_TRAFFIC_B_PER_PARTICLE is not None:
+    if dom == "force" and cfg.name == "sharded16m":
         traffic = FORCE_TRAFFIC_B_PER_PARTICLE * cfg.n
     phases = {k: {"ms": phase_ms[k], "alg_bytes_per_particle": ab[k],
                   "achieved_gbs": ab[k] * cfg.n / (phase_ms[k] / 1e3) / 1e9,
