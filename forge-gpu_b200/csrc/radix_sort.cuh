@@ -29,6 +29,7 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kItems = 16;
 constexpr int kTile = kThreads * kItems;  // 4096 keys per tile
 constexpr int kMaxPasses = 4;
+constexpr int kLookBatch = 8;  // look-back status words loaded per round trip
 
 // Look-back status word: [31] pass parity | [30:29] flag | [28:0] count.
 constexpr uint32_t kFlagAgg = 1u << 29;
@@ -39,6 +40,24 @@ constexpr uint32_t kCountMask = (1u << 29) - 1;
 constexpr uint64_t kMaxN = (1ull << 29) - 1;
 
 constexpr int kHistThreads = 256;
+
+#ifdef FORGE_SORT_PHASES
+// Probe-only instrumentation: per-tile %globaltimer stamps at phase
+// boundaries (never compiled into the library).
+__device__ unsigned long long* g_phase_buf;
+#define FORGE_PHASE_MARK(tile, k)                                                          \
+    do {                                                                                   \
+        if (threadIdx.x == 0) {                                                            \
+            unsigned long long t_;                                                         \
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                         \
+            g_phase_buf[(size_t)(tile) * 8 + (k)] = t_;                                    \
+        }                                                                                  \
+    } while (0)
+#else
+#define FORGE_PHASE_MARK(tile, k) \
+    do {                          \
+    } while (0)
+#endif
 constexpr int kHistItems = 8;
 
 __host__ __device__ constexpr uint32_t num_tiles(uint64_t n) {
@@ -138,7 +157,7 @@ __global__ void __launch_bounds__(kHistThreads)
 // pass of the grid build), vals_in is not read.
 // ---------------------------------------------------------------------------
 template <bool IOTA>
-__global__ void __launch_bounds__(kThreads, 3)
+__global__ void __launch_bounds__(kThreads, 4)
     onesweep_pass_kernel(const uint32_t* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
                          uint32_t* __restrict__ keys_out, uint32_t* __restrict__ vals_out,
                          uint32_t n, uint32_t shift, uint32_t bits,
@@ -159,6 +178,7 @@ __global__ void __launch_bounds__(kThreads, 3)
     __syncthreads();
 
     const uint32_t tile = s_tile;
+    FORGE_PHASE_MARK(tile, 0);
     const uint32_t tile_start = tile * kTile;
     const uint32_t mask = (1u << bits) - 1u;
     const uint32_t warp_start = tile_start + warp * 32 * kItems;
@@ -175,9 +195,55 @@ __global__ void __launch_bounds__(kThreads, 3)
         else val[k] = ok ? vals_in[idx] : 0u;
     }
 
-    // Stable warp-level ranking.
+    FORGE_PHASE_MARK(tile, 1);  // loads issued
+    // Early counts: per-warp digit histograms from shared atomics (a warp
+    // whose keys share one digit adds 32 once), so the tile aggregate is
+    // published before the ranking and successors' look-backs do not wait
+    // for it.
+#pragma unroll
+    for (int k = 0; k < kItems; ++k) {
+        const uint32_t idx = warp_start + k * 32 + lane;
+        const bool ok = idx < n;
+        const uint32_t d = digit_of(key[k], shift, mask);
+        const uint32_t d0 = __shfl_sync(0xffffffffu, d, 0);
+        if (__all_sync(0xffffffffu, ok && d == d0)) {
+            if (lane == 0) s_whist[warp][d0] += 32u;
+        } else if (ok) {
+            atomicAdd(&s_whist[warp][d], 1u);
+        }
+        __syncwarp();
+    }
+    __syncthreads();
+
+    // Per digit (thread tid == digit): tile count, published at once, then
+    // each warp's starting position of the digit inside the sorted tile.
+    uint32_t cnt = 0;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) cnt += s_whist[w][tid];
+    FORGE_PHASE_MARK(tile, 2);  // counted
+    uint32_t* my_status = status + (size_t)tile * kRadix + tid;
+    const uint32_t par = parity ? kParityBit : 0u;
+    st_relaxed_u32(my_status, par | (tile == 0 ? kFlagPre : kFlagAgg) | cnt);
+
+    uint32_t total;
+    const uint32_t tile_off = block_exclusive_scan<kThreads>(cnt, s_scan, &total);
+    s_tile_off[tid] = tile_off;
+    {
+        uint32_t run = tile_off;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) {
+            const uint32_t c = s_whist[w][tid];
+            s_whist[w][tid] = run;
+            run += c;
+        }
+    }
+    // (the scan's barriers also publish s_whist / s_tile_off)
+    const uint32_t hist_off = block_exclusive_scan<kThreads>(pass_hist[tid], s_scan, &total);
+
+    // Stable warp-level ranking straight to tile positions: item-major,
+    // lane-minor order is the input order.
     const uint32_t lt = lanemask_lt();
-    uint32_t rank[kItems];
+    uint32_t pos[kItems];
 #pragma unroll
     for (int k = 0; k < kItems; ++k) {
         const uint32_t idx = warp_start + k * 32 + lane;
@@ -189,67 +255,59 @@ __global__ void __launch_bounds__(kThreads, 3)
         __syncwarp();
         if (ok && (peers & lt) == 0) s_whist[warp][d] = before + __popc(peers);
         __syncwarp();
-        rank[k] = before + __popc(peers & lt);
+        pos[k] = ok ? before + __popc(peers & lt) : 0xffffffffu;
+        if (ok) s_exchange[pos[k]] = key[k];
     }
-    __syncthreads();
 
-    // Per digit (thread tid == digit): exclusive offsets across warps and the
-    // tile count; publish the tile aggregate as early as possible.
-    uint32_t cnt = 0;
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) {
-        const uint32_t c = s_whist[w][tid];
-        s_whist[w][tid] = cnt;
-        cnt += c;
-    }
-    uint32_t* my_status = status + (size_t)tile * kRadix + tid;
-    const uint32_t par = parity ? kParityBit : 0u;
-    st_relaxed_u32(my_status, par | (tile == 0 ? kFlagPre : kFlagAgg) | cnt);
-
-    uint32_t total;
-    const uint32_t tile_off = block_exclusive_scan<kThreads>(cnt, s_scan, &total);
-    s_tile_off[tid] = tile_off;
-    const uint32_t hist_off = block_exclusive_scan<kThreads>(pass_hist[tid], s_scan, &total);
-
-    // Decoupled look-back for digit tid.
+    FORGE_PHASE_MARK(tile, 3);  // aggregate published, scans done
+    // Decoupled look-back for digit tid. The nearest inclusive prefix is
+    // typically ~20 tiles back with every aggregate already published, so
+    // kLookBatch status words are loaded per round trip and consumed in order
+    // until a prefix (a word not yet published is re-polled).
     uint32_t excl = 0;
     if (tile > 0) {
         int t = (int)tile - 1;
         uint32_t spins = 0;
-        while (true) {
-            const uint32_t v = ld_relaxed_u32(status + (size_t)t * kRadix + tid);
-            const bool ready = ((v & kParityBit) == par) && (v & kFlagMask) != 0;
-            if (!ready) {
+        bool done = false;
+        while (!done) {
+            uint32_t v[kLookBatch];
+#pragma unroll
+            for (int q = 0; q < kLookBatch; ++q)
+                v[q] = (t - q >= 0) ? ld_relaxed_u32(status + (size_t)(t - q) * kRadix + tid) : (par | kFlagPre);
+            bool go = true;
+            int used = 0;
+#pragma unroll
+            for (int q = 0; q < kLookBatch; ++q) {
+                if (!go) continue;
+                const bool ready = ((v[q] & kParityBit) == par) && (v[q] & kFlagMask) != 0;
+                if (!ready) {
+                    go = false;
+                    continue;
+                }
+                excl += v[q] & kCountMask;
+                ++used;
+                if ((v[q] & kFlagMask) == kFlagPre) {
+                    done = true;
+                    go = false;
+                }
+            }
+            t -= used;
+            if (!done && used == 0) {
                 if (++spins > kSpinLimit) {
                     atomicOr(err, kDevTimeout);
                     break;
                 }
                 if (spins > 64) __nanosleep(64);
-                continue;
             }
-            excl += v & kCountMask;
-            if ((v & kFlagMask) == kFlagPre || t == 0) break;
-            --t;
         }
         st_relaxed_u32(my_status, par | kFlagPre | ((excl + cnt) & kCountMask));
+#ifdef FORGE_SORT_PHASES
+        if (tid == 0) g_phase_buf[(size_t)tile * 8 + 6] = ((unsigned long long)spins << 32) | (uint32_t)((int)tile - 1 - t);
+#endif
     }
     s_base[tid] = hist_off + excl - tile_off;
     __syncthreads();
-
-    // Stage the digit-sorted tile in shared memory (keys), write out.
-    uint32_t pos[kItems];
-#pragma unroll
-    for (int k = 0; k < kItems; ++k) {
-        const uint32_t idx = warp_start + k * 32 + lane;
-        if (idx < n) {
-            const uint32_t d = digit_of(key[k], shift, mask);
-            pos[k] = s_tile_off[d] + s_whist[warp][d] + rank[k];
-            s_exchange[pos[k]] = key[k];
-        } else {
-            pos[k] = 0xffffffffu;
-        }
-    }
-    __syncthreads();
+    FORGE_PHASE_MARK(tile, 4);  // look-back done
 
     const uint32_t tile_n = min((uint32_t)kTile, n - tile_start);
     uint32_t dst[kItems];
@@ -273,6 +331,8 @@ __global__ void __launch_bounds__(kThreads, 3)
         const uint32_t j = tid + k * kThreads;
         if (j < tile_n) vals_out[dst[k]] = s_exchange[j];
     }
+    __syncthreads();
+    FORGE_PHASE_MARK(tile, 5);  // written
 }
 
 }  // namespace radix
