@@ -84,6 +84,9 @@ int num_sms(int device) {
 
 // Radix-sort scratch shared by the standalone sorter and the grid build:
 // meta = [kMaxPasses x 256 digit histograms][kMaxPasses tile counters][status word].
+// x-slices per cell (as bits) of the SPH passes' internal ordering.
+constexpr uint32_t kSphSubBits = 2;
+
 constexpr size_t kMetaHist = radix::kMaxPasses * radix::kRadix;
 constexpr size_t kMetaCounters = kMetaHist;
 constexpr size_t kMetaErr = kMetaHist + radix::kMaxPasses;
@@ -377,7 +380,8 @@ struct forge_grid {
     uint32_t* vb = nullptr;
     uint32_t* kc = nullptr;
     uint32_t* vc = nullptr;
-    uint32_t* cell_start = nullptr;  // C + 1
+    uint32_t* cell_start = nullptr;  // (C << kSphSubBits) + 1
+    uint32_t sub_bits = 0;           // x-slices of the last build (0: plain cells)
     float4* pos4 = nullptr;          // cell-ordered (x, y, z, key)
     float4* vel4 = nullptr;          // cell-ordered (vx, vy, vz, 1/rho)
     float2* aux = nullptr;           // cell-ordered (p/rho, rho)
@@ -416,8 +420,8 @@ extern "C" int forge_grid_create(float cell_size, uint32_t nx, uint32_t ny, uint
     *out = nullptr;
     if (!(cell_size > 0.f)) return set_error(FORGE_ERR_INVALID_ARG, "forge_grid_create: cell_size must be > 0");
     const uint64_t C = (uint64_t)nx * ny * nz;
-    if (nx == 0 || ny == 0 || nz == 0 || C >= (1ull << 31))
-        return set_error(FORGE_ERR_INVALID_ARG, "forge_grid_create: grid %ux%ux%u must be non-empty and < 2^31 cells",
+    if (nx == 0 || ny == 0 || nz == 0 || C >= (1ull << (31 - kSphSubBits)))
+        return set_error(FORGE_ERR_INVALID_ARG, "forge_grid_create: grid %ux%ux%u must be non-empty and < 2^29 cells",
                          nx, ny, nz);
     if (max_n > radix::kMaxN)
         return set_error(FORGE_ERR_INVALID_ARG, "forge_grid_create: max_n exceeds %llu",
@@ -441,7 +445,7 @@ extern "C" int forge_grid_create(float cell_size, uint32_t nx, uint32_t ny, uint
     int rc = FORGE_OK;
     bool ok = dalloc(&g->cell_idx, m) == cudaSuccess && dalloc(&g->kb, m) == cudaSuccess &&
               dalloc(&g->vb, m) == cudaSuccess && dalloc(&g->kc, m) == cudaSuccess &&
-              dalloc(&g->vc, m) == cudaSuccess && dalloc(&g->cell_start, C + 1) == cudaSuccess &&
+              dalloc(&g->vc, m) == cudaSuccess && dalloc(&g->cell_start, (C << kSphSubBits) + 1) == cudaSuccess &&
               dalloc(&g->pos4, m) == cudaSuccess && dalloc(&g->vel4, m) == cudaSuccess &&
               dalloc(&g->aux, m) == cudaSuccess &&
               dalloc(&g->scan_sums, m / grid::kScanTile + 1) == cudaSuccess &&
@@ -479,9 +483,12 @@ extern "C" void forge_grid_destroy(forge_grid* g) {
 namespace {
 
 // Hash + sort + cell-start table (+ optional cell-ordered gather).
+// sub_bits > 0 (the SPH passes): keys are cell << sub_bits | x-slice, so the
+// cell-ordered arrays are also ordered by x-slice inside each cell and the
+// table has (C << sub_bits) + 1 entries.
 int grid_build_impl(forge_grid* g, const float* px, const float* py, const float* pz, uint32_t stride, uint64_t n,
                     uint32_t* cell_idx_out, bool gather_pos, const float* vx, const float* vy, const float* vz,
-                    cudaStream_t st) {
+                    cudaStream_t st, uint32_t sub_bits = 0) {
     if (n > g->max_n)
         return set_error(FORGE_ERR_CAPACITY, "grid build: n=%llu exceeds max_n=%llu", (unsigned long long)n,
                          (unsigned long long)g->max_n);
@@ -489,10 +496,10 @@ int grid_build_impl(forge_grid* g, const float* px, const float* py, const float
     uint32_t* keys = cell_idx_out ? cell_idx_out : g->cell_idx;
     const uint32_t nn = (uint32_t)n;
     if (n > 0) {
-        grid::HashKeys src{px, py, pz, stride, g->geom, keys};
+        grid::HashKeys src{px, py, pz, stride, g->geom, keys, sub_bits};
         int where = 0;
-        int rc = run_onesweep(g->scratch, src, keys, nullptr, g->kb, g->vb, g->kc, g->vc, nn, 0, g->key_bits, st,
-                              &where);
+        int rc = run_onesweep(g->scratch, src, keys, nullptr, g->kb, g->vb, g->kc, g->vc, nn, 0,
+                              g->key_bits + sub_bits, st, &where);
         if (rc != FORGE_OK) return rc;
         g->sorted_keys = where == 0 ? g->kb : g->kc;
         g->sorted_idx = where == 0 ? g->vb : g->vc;
@@ -503,12 +510,13 @@ int grid_build_impl(forge_grid* g, const float* px, const float* py, const float
     prof_mark(g, 1, st);
     grid::GatherSrc gs{px, py, pz, stride, vx, vy, vz};
     grid::cell_start_gather_kernel<<<grid_blocks(n + 1, 256), 256, 0, st>>>(
-        g->sorted_keys, g->sorted_idx, nn, g->C, g->cell_start, gs, gather_pos ? g->pos4 : nullptr,
+        g->sorted_keys, g->sorted_idx, nn, g->C << sub_bits, g->cell_start, gs, gather_pos ? g->pos4 : nullptr,
         (gather_pos && vx) ? g->vel4 : nullptr);
     FORGE_LAUNCHED();
     prof_mark(g, 2, st);
     g->n = n;
     g->built = true;
+    g->sub_bits = sub_bits;
     return FORGE_OK;
 }
 
@@ -544,8 +552,9 @@ sph::SphConsts make_consts(const forge_sph_params* p) {
     return c;
 }
 
-sph::Geom geom_of(const forge_grid* g) {
-    return sph::Geom{g->geom.ox, g->geom.oy, g->geom.oz, g->geom.cs, g->geom.nx, g->geom.ny, g->geom.nz};
+sph::Geom geom_of(const forge_grid* g, float h) {
+    return sph::Geom{g->geom.ox, g->geom.oy, g->geom.oz, g->geom.cs, g->geom.nx, g->geom.ny, g->geom.nz,
+                     (int)g->sub_bits, g->geom.cs >= h ? 1 : 0};
 }
 
 constexpr uint32_t kSphThreads = 128;
@@ -553,7 +562,7 @@ constexpr uint32_t kSphThreads = 128;
 int launch_density(forge_grid* g, const forge_sph_params* p, float* density, cudaStream_t st) {
     if (g->n == 0) return FORGE_OK;
     sph::density_pair_kernel<<<grid_blocks((g->n + 1) / 2, kSphThreads), kSphThreads, 0, st>>>(
-        g->pos4, g->cell_start, g->sorted_idx, (uint32_t)g->n, geom_of(g), make_consts(p), g->vel4, g->aux, density);
+        g->pos4, g->cell_start, g->sorted_idx, (uint32_t)g->n, geom_of(g, p->h), make_consts(p), g->vel4, g->aux, density);
     FORGE_LAUNCHED();
     return FORGE_OK;
 }
@@ -568,10 +577,10 @@ void launch_force_t(forge_grid* g, const sph::SphConsts& c, const sph::StepEpi& 
                     cudaStream_t st) {
     if ((double)g->n / (double)g->C < kPairMaxOccupancy)
         sph::force_kernel<TERMS, EPI><<<grid_blocks((g->n + 1) / 2, kSphThreads), kSphThreads, 0, st>>>(
-            g->pos4, g->vel4, g->aux, g->cell_start, g->sorted_idx, (uint32_t)g->n, geom_of(g), c, ep, o);
+            g->pos4, g->vel4, g->aux, g->cell_start, g->sorted_idx, (uint32_t)g->n, geom_of(g, c.h), c, ep, o);
     else
         sph::force_single_kernel<TERMS, EPI><<<grid_blocks(g->n, kSphThreads), kSphThreads, 0, st>>>(
-            g->pos4, g->vel4, g->aux, g->cell_start, g->sorted_idx, (uint32_t)g->n, geom_of(g), c, ep, o);
+            g->pos4, g->vel4, g->aux, g->cell_start, g->sorted_idx, (uint32_t)g->n, geom_of(g, c.h), c, ep, o);
 }
 
 }  // namespace
@@ -602,7 +611,8 @@ extern "C" int forge_grid_query(forge_grid* g, const float* px, const float* py,
                                 const float* qy, const float* qz, uint64_t nq, float radius, uint32_t* counts,
                                 uint32_t* offsets, uint32_t* hits, uint64_t max_hits, void* stream) {
     if (!g) return set_error(FORGE_ERR_INVALID_ARG, "forge_grid_query: grid is NULL");
-    if (!g->built) return set_error(FORGE_ERR_INVALID_ARG, "forge_grid_query: grid has not been built");
+    if (!g->built || g->sub_bits != 0)
+        return set_error(FORGE_ERR_INVALID_ARG, "forge_grid_query: build the grid with forge_grid_build first");
     if (nq > g->max_n)
         return set_error(FORGE_ERR_CAPACITY, "forge_grid_query: nq=%llu exceeds max_n=%llu",
                          (unsigned long long)nq, (unsigned long long)g->max_n);
@@ -651,7 +661,7 @@ extern "C" int forge_sph_density(forge_grid* g, const forge_sph_params* p, const
     if (n && !density) return set_error(FORGE_ERR_INVALID_ARG, "forge_sph_density: density is NULL");
     FORGE_DEVICE_SCOPE(g->device);
     cudaStream_t st = as_stream(stream);
-    int rc = grid_build_impl(g, px, py, pz, 1, n, nullptr, true, nullptr, nullptr, nullptr, st);
+    int rc = grid_build_impl(g, px, py, pz, 1, n, nullptr, true, nullptr, nullptr, nullptr, st, kSphSubBits);
     if (rc != FORGE_OK) return rc;
     return launch_density(g, p, density, st);
 }
@@ -741,7 +751,7 @@ extern "C" int forge_sph_step(forge_grid* g, const forge_sph_params* p, const fo
     FORGE_DEVICE_SCOPE(g->device);
     cudaStream_t st = as_stream(stream);
     prof_mark(g, 0, st);
-    int rc = grid_build_impl(g, px, py, pz, 1, n, nullptr, true, vx, vy, vz, st);
+    int rc = grid_build_impl(g, px, py, pz, 1, n, nullptr, true, vx, vy, vz, st, kSphSubBits);
     if (rc != FORGE_OK) return rc;
     if (n == 0) return FORGE_OK;
     rc = launch_density(g, p, density, st);

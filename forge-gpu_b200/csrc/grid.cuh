@@ -32,7 +32,21 @@ __device__ __forceinline__ uint32_t cell_of(float x, float y, float z, const Gri
     return (uint32_t)cx + (uint32_t)cy * (uint32_t)g.nx + (uint32_t)cz * (uint32_t)g.nx * (uint32_t)g.ny;
 }
 
-// Histogram key source that hashes positions and stores the cell index.
+// Sub-slice of a position inside its (clamped) cell along x: the cell is cut
+// into 2^sub_bits slabs. fx - cx is exact (the fractional part of a float is
+// representable), so slice = floor(2^sub_bits * fx) - 2^sub_bits * cx for
+// positions inside the grid; clamped positions land in the edge slice.
+__device__ __forceinline__ uint32_t slice_of(float x, const GridGeom& g, uint32_t sub_bits) {
+    const float fx = (x - g.ox) / g.cs;
+    int cx = floor_to_int(fx);
+    cx = cx < 0 ? 0 : (cx >= g.nx ? g.nx - 1 : cx);
+    const int S = 1 << sub_bits;
+    int s = floor_to_int((fx - (float)cx) * (float)S);
+    return (uint32_t)(s < 0 ? 0 : (s >= S ? S - 1 : s));
+}
+
+// Histogram key source that hashes positions and stores the key:
+// cell << sub_bits | x-slice (sub_bits = 0: the plain cell index).
 // stride 1: SoA (px, py, pz separate); stride 3: Vec3f AoS (px = xyz).
 struct HashKeys {
     const float* __restrict__ px;
@@ -41,9 +55,12 @@ struct HashKeys {
     uint32_t stride;
     GridGeom g;
     uint32_t* __restrict__ keys_out;
+    uint32_t sub_bits;
     __device__ __forceinline__ uint32_t operator()(uint32_t i) const {
         const size_t o = (size_t)i * stride;
-        const uint32_t c = cell_of(px[o], py[o], pz[o], g);
+        const float x = px[o];
+        uint32_t c = cell_of(x, py[o], pz[o], g);
+        if (sub_bits) c = (c << sub_bits) | slice_of(x, g, sub_bits);
         keys_out[i] = c;
         return c;
     }

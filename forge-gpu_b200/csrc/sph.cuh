@@ -2,39 +2,43 @@
 // + viscosity-Laplacian force with the manifest step epilogue.
 //
 // Data layout (HBM): particles live in the caller's SoA arrays in ORIGINAL
-// order. After the grid build the library holds cell-ordered copies
-//   pos4[s] = (x, y, z, bits(cell key))
+// order. The SPH grid build sorts them by key = cell << sub_bits | x-slice
+// (each cell cut into 2^sub_bits slabs along x; ties in ascending particle
+// index) and the library holds cell-ordered copies
+//   pos4[s] = (x, y, z, bits(key))
 //   vel4[s] = (vx, vy, vz, 1/rho)       (1/rho := 0 when rho < 1e-6)
 //   aux[s]  = (p/rho, rho)              p = k (rho - rho0)
-// so for each (dz, dy) the three cells dx = -1..1 are ONE contiguous range
-// [cell_start[row+cx-1], cell_start[row+cx+2]). Walking the rows dz-major,
-// dy-minor visits neighbours in exactly the reference order (dz, dy, dx, then
-// ascending particle index inside a cell), sph_density.rs:429-458.
+// so for each row (dz, dy) of the 3x3x3 cell block the candidates are ONE
+// contiguous range of slices [lo, hi] along x. Rows are walked in the
+// reference order (dz, dy); inside a row the candidates come in slice order
+// instead of the reference's (dx, index) order, so sums agree with the
+// reference to rounding, not bit for bit.
 //
-// Per particle the walk is trimmed to the cells whose box can hold a point
-// closer than h: a cell (or a whole row) is skipped only when the squared
-// distance from the particle to the cell's box, shrunk by a rounding slack,
-// exceeds h^2 (1 + 1e-4). Every pair with r^2 < h^2 is still visited, in the
-// same order, so the sums are unchanged; at cell size h this removes ~24% of
-// the candidates, at the reference's default cell size 2h far more.
+// Per particle and row the slice range is trimmed to the x-extent that can
+// hold a point with r^2 < h^2: w = sqrt(h^2 (1 + 1e-4) - gap_y^2 - gap_z^2)
+// around the particle, gaps shrunk by a rounding slack, clipped to the
+// reference's 3-cell window; a row whose (y, z) gap alone exceeds h is
+// skipped. Every pair with r^2 < h^2 is still visited.
 //
-// One thread per particle in cell order: consecutive lanes sit in the same or
-// adjacent cells, so a warp walks (almost) the same ranges and neighbour
-// loads are warp-broadcasts served by L1. Results are scattered back to the
-// original order through sorted_idx.
+// Two consecutive particles per thread share neighbour loads: same row ->
+// one walk over the union of their windows (a candidate outside one particle's
+// window is > h from it when cell size >= h, and adds nothing); otherwise two
+// walks. Results are scattered back to the original order through sorted_idx.
 //
-// Both passes are bound by instruction issue, not HBM (a few % of DRAM
-// bandwidth at these densities), so the kernels minimise instructions per
-// candidate pair: the density sum is branchless, and the force pass first
-// scans a chunk of 32 candidates for r^2 < h^2 (cheap) and then evaluates the
-// expensive pair term only for the hits, with per-particle reciprocals
-// instead of per-pair divides.
+// Both passes are bound by instruction issue and L1 wavefronts, not HBM, so
+// the kernels minimise instructions per candidate: the density sum is
+// branchless, and the force pass first scans a chunk of 32 candidates for
+// r^2 < h^2 (cheap) and then evaluates the expensive pair term only for the
+// hits, with per-particle reciprocals instead of per-pair divides.
 #pragma once
 
 #include "common.cuh"
 
 namespace forge {
 namespace sph {
+
+// floorf + saturating convert (NaN -> 0), as the cell hash does.
+__device__ __forceinline__ int floor_to_int_dev(float v) { return (int)floorf(v); }
 
 struct SphConsts {
     float h, h2;
@@ -49,14 +53,9 @@ struct SphConsts {
 struct Geom {
     float ox, oy, oz, cs;
     int nx, ny, nz;
+    int sub_bits;   // x-slices per cell = 2^sub_bits (keys are cell << sub_bits | slice)
+    int pairable;   // cs >= h: a walk over a same-row neighbour's window adds only r >= h pairs
 };
-
-__device__ __forceinline__ void key_to_cell(uint32_t key, const Geom& d, int& cx, int& cy, int& cz) {
-    const uint32_t t = key / (uint32_t)d.nx;
-    cx = (int)(key - t * (uint32_t)d.nx);
-    cy = (int)(t % (uint32_t)d.ny);
-    cz = (int)(t / (uint32_t)d.ny);
-}
 
 // Squared conservative gap: distance shrunk by a slack covering the rounding
 // of the cell assignment and of r^2, clamped at 0 (clamped out-of-grid
@@ -66,62 +65,84 @@ __device__ __forceinline__ float gap2(float raw, float slack) {
     return g * g;
 }
 
-// A particle's cell and its trimmed search window, packed: for row
-// r = (dz+1)*3 + (dy+1), bit 3r = row visited, bit 3r+1 = window starts at
-// cx-1 (else cx), bit 3r+2 = window ends after cx+1 (else after cx).
-struct Window {
-    int cx, cy, cz;
-    uint32_t bits;
-    __device__ __forceinline__ bool on(int r) const { return (bits >> (3 * r)) & 1u; }
-    __device__ __forceinline__ int lo(int r) const { return cx - (int)((bits >> (3 * r + 1)) & 1u); }
-    __device__ __forceinline__ int hi(int r) const { return cx + 1 + (int)((bits >> (3 * r + 2)) & 1u); }
+// A particle's place in the grid and what its row windows are built from.
+struct Frame {
+    int cy, cz;
+    int fx_lo, fx_hi;   // x-slice range of the reference window: cells cx-1..cx+1, clamped to the grid
+    int f_own;          // own x-slice index in the row
+    float fxs;          // (x - ox) / cs * 2^sub_bits   (slice coordinate)
+    float slack;        // slice-units rounding slack
+    float gyl, gyr, gzl, gzr;  // squared gaps to the neighbouring rows
 };
 
-__device__ __forceinline__ Window make_window(const float4& p, const Geom& g, float H) {
-    Window w;
-    key_to_cell(__float_as_uint(p.w), g, w.cx, w.cy, w.cz);
-    const int cx = w.cx, cy = w.cy, cz = w.cz;
-    const float bx = g.ox + (float)cx * g.cs, by = g.oy + (float)cy * g.cs, bz = g.oz + (float)cz * g.cs;
-    const float sx = 4e-7f * (fabsf(p.x) + fabsf(bx) + g.cs);
+__device__ __forceinline__ Frame make_frame(const float4& p, const Geom& g) {
+    Frame f;
+    const uint32_t key = __float_as_uint(p.w);
+    const uint32_t S = 1u << g.sub_bits;
+    const uint32_t rowlen = (uint32_t)g.nx * S;
+    const uint32_t t = key / rowlen;
+    f.f_own = (int)(key - t * rowlen);
+    f.cy = (int)(t % (uint32_t)g.ny);
+    f.cz = (int)(t / (uint32_t)g.ny);
+    const int cx = f.f_own >> g.sub_bits;
+    f.fx_lo = max(cx - 1, 0) * (int)S;
+    f.fx_hi = (min(cx + 1, g.nx - 1) + 1) * (int)S - 1;
+    const float fx = (p.x - g.ox) / g.cs;
+    f.fxs = fx * (float)S;
+    f.slack = (4e-7f * (fabsf(fx) + 2.f)) * (float)S;
+    const float by = g.oy + (float)f.cy * g.cs, bz = g.oz + (float)f.cz * g.cs;
     const float sy = 4e-7f * (fabsf(p.y) + fabsf(by) + g.cs);
     const float sz = 4e-7f * (fabsf(p.z) + fabsf(bz) + g.cs);
-    const float gxl = gap2(p.x - bx, sx), gxr = gap2(bx + g.cs - p.x, sx);
-    const float gyl = gap2(p.y - by, sy), gyr = gap2(by + g.cs - p.y, sy);
-    const float gzl = gap2(p.z - bz, sz), gzr = gap2(bz + g.cs - p.z, sz);
-    uint32_t bits = 0;
-#pragma unroll
-    for (int r = 0; r < 9; ++r) {
-        const int dz = r / 3 - 1, dy = r % 3 - 1;
-        const int z = cz + dz, y = cy + dy;
-        const float base = (dz < 0 ? gzl : (dz > 0 ? gzr : 0.f)) + (dy < 0 ? gyl : (dy > 0 ? gyr : 0.f));
-        const bool on = z >= 0 && z < g.nz && y >= 0 && y < g.ny && base <= H;
-        const bool l = cx > 0 && base + gxl <= H;
-        const bool rr = cx < g.nx - 1 && base + gxr <= H;
-        bits |= (on ? 1u : 0u) << (3 * r);
-        bits |= (l ? 1u : 0u) << (3 * r + 1);
-        bits |= (rr ? 1u : 0u) << (3 * r + 2);
-    }
-    w.bits = bits;
-    return w;
+    f.gyl = gap2(p.y - by, sy);
+    f.gyr = gap2(by + g.cs - p.y, sy);
+    f.gzl = gap2(p.z - bz, sz);
+    f.gzr = gap2(bz + g.cs - p.z, sz);
+    return f;
 }
 
-__device__ __forceinline__ uint32_t row_base(const Geom& g, int cy, int cz, int r) {
+// Window of row r = (dz+1)*3 + (dy+1) as an inclusive x-slice range
+// [lo, hi]: the slices that can hold a point with r^2 < h^2, i.e. whose x
+// lies within w = sqrt(H - gap_y^2 - gap_z^2) of the particle, clipped to the
+// reference's 3-cell window and always containing the particle's own slice
+// (clamped out-of-grid particles). false: the row is skipped.
+__device__ __forceinline__ bool row_window(const Frame& f, int r, const Geom& g, float H, int& lo, int& hi) {
     const int dz = r / 3 - 1, dy = r % 3 - 1;
-    return ((uint32_t)(cz + dz) * (uint32_t)g.ny + (uint32_t)(cy + dy)) * (uint32_t)g.nx;
+    const int z = f.cz + dz, y = f.cy + dy;
+    if (z < 0 || z >= g.nz || y < 0 || y >= g.ny) return false;
+    const float base = (dz < 0 ? f.gzl : (dz > 0 ? f.gzr : 0.f)) + (dy < 0 ? f.gyl : (dy > 0 ? f.gyr : 0.f));
+    if (base > H) return false;
+    const float w = sqrtf(H - base) / g.cs * (float)(1 << g.sub_bits) + f.slack;
+    lo = max(min(floor_to_int_dev(f.fxs - w), f.f_own), f.fx_lo);
+    hi = min(max(floor_to_int_dev(f.fxs + w), f.f_own), f.fx_hi);
+    return true;
+}
+
+__device__ __forceinline__ uint32_t row_base(const Geom& g, const Frame& f, int r) {
+    const int dz = r / 3 - 1, dy = r % 3 - 1;
+    return ((uint32_t)(f.cz + dz) * (uint32_t)g.ny + (uint32_t)(f.cy + dy)) * ((uint32_t)g.nx << g.sub_bits);
 }
 
 // Calls f(b, e) for each trimmed contiguous candidate range of particle p
-// (cell-ordered indices), in reference order.
+// (cell-ordered indices), rows in the reference order (dz, dy).
 template <class F>
 __device__ __forceinline__ void for_each_range(const float4& p, const Geom& g, const uint32_t* __restrict__ cell_start,
-                                               float H, F&& f) {
-    const Window w = make_window(p, g, H);
-#pragma unroll
+                                               float H, F&& fn) {
+    const Frame f = make_frame(p, g);
+#pragma unroll 1
     for (int r = 0; r < 9; ++r) {
-        if (!w.on(r)) continue;
-        const uint32_t row = row_base(g, w.cy, w.cz, r);
-        f(__ldg(cell_start + row + w.lo(r)), __ldg(cell_start + row + w.hi(r)));
+        int lo, hi;
+        if (!row_window(f, r, g, H, lo, hi)) continue;
+        const uint32_t row = row_base(g, f, r);
+        fn(__ldg(cell_start + row + lo), __ldg(cell_start + row + hi + 1));
     }
+}
+
+// Union of two windows of the same row (either may be absent).
+__device__ __forceinline__ bool union_window(bool a, int alo, int ahi, bool b, int blo, int bhi, int& lo, int& hi) {
+    if (!a && !b) return false;
+    lo = a ? (b ? min(alo, blo) : alo) : blo;
+    hi = a ? (b ? max(ahi, bhi) : ahi) : bhi;
+    return true;
 }
 
 // Per-particle data the force pass reads for a neighbour, from its density.
@@ -182,32 +203,18 @@ __global__ void __launch_bounds__(128)
     const bool has1 = s0 + 1 < n;
     const float4 p0 = pos4[s0];
     const float4 p1 = has1 ? pos4[s0 + 1] : p0;
-    const Window w0 = make_window(p0, g, c.h2_skip);
-    const Window w1 = make_window(p1, g, c.h2_skip);
+    const Frame f0 = make_frame(p0, g);
+    const Frame f1 = make_frame(p1, g);
     float rho0 = 0.f, rho1 = 0.f;
-    if (has1 && w0.cy == w1.cy && w0.cz == w1.cz) {
-        const bool same_cell = w0.cx == w1.cx;
-#pragma unroll
+    if (has1 && g.pairable && f0.cy == f1.cy && f0.cz == f1.cz) {
+#pragma unroll 1
         for (int r = 0; r < 9; ++r) {
-            const bool e0 = w0.on(r), e1 = w1.on(r);
-            if (!e0 && !e1) continue;
-            const uint32_t row = row_base(g, w0.cy, w0.cz, r);
-            if (same_cell) {
-                const int lo = e0 ? (e1 ? min(w0.lo(r), w1.lo(r)) : w0.lo(r)) : w1.lo(r);
-                const int hi = e0 ? (e1 ? max(w0.hi(r), w1.hi(r)) : w0.hi(r)) : w1.hi(r);
-                poly6_two(pos4, __ldg(cell_start + row + lo), __ldg(cell_start + row + hi), p0, p1, c, rho0, rho1);
-            } else {
-                // cx0 < cx1, so lb0 <= lb1 and le0 <= le1 for the trimmed ranges.
-                uint32_t lb0 = e0 ? __ldg(cell_start + row + w0.lo(r)) : 0u;
-                uint32_t le0 = e0 ? __ldg(cell_start + row + w0.hi(r)) : 0u;
-                uint32_t lb1 = e1 ? __ldg(cell_start + row + w1.lo(r)) : 0u;
-                uint32_t le1 = e1 ? __ldg(cell_start + row + w1.hi(r)) : 0u;
-                if (!e0) lb0 = le0 = lb1;
-                if (!e1) lb1 = le1 = le0;
-                poly6_one(pos4, lb0, min(lb1, le0), p0, c, rho0);
-                if (lb1 < le0) poly6_two(pos4, lb1, le0, p0, p1, c, rho0, rho1);
-                poly6_one(pos4, max(le0, lb1), le1, p1, c, rho1);
-            }
+            int l0, h0, l1, h1, lo, hi;
+            const bool a = row_window(f0, r, g, c.h2_skip, l0, h0);
+            const bool b = row_window(f1, r, g, c.h2_skip, l1, h1);
+            if (!union_window(a, l0, h0, b, l1, h1, lo, hi)) continue;
+            const uint32_t row = row_base(g, f0, r);
+            poly6_two(pos4, __ldg(cell_start + row + lo), __ldg(cell_start + row + hi + 1), p0, p1, c, rho0, rho1);
         }
     } else {
         for_each_range(p0, g, cell_start, c.h2_skip,
@@ -455,13 +462,13 @@ __global__ void __launch_bounds__(128)
     const float* __restrict__ pj = reinterpret_cast<const float*>(aux);
     ForceAcc A = force_acc(pos4, vel4, aux, s, c);
     if (A.v.w != 0.f) {
-        const Window w = make_window(A.p, g, c.h2_skip);
+        const Frame f = make_frame(A.p, g);
 #pragma unroll 1
         for (int r = 0; r < 9; ++r) {
-            if (!w.on(r)) continue;
-            const uint32_t row = row_base(g, w.cy, w.cz, r);
-            force_one<TERMS>(pos4, vel4, pj, __ldg(cell_start + row + w.lo(r)), __ldg(cell_start + row + w.hi(r)),
-                             A, c);
+            int lo, hi;
+            if (!row_window(f, r, g, c.h2_skip, lo, hi)) continue;
+            const uint32_t row = row_base(g, f, r);
+            force_one<TERMS>(pos4, vel4, pj, __ldg(cell_start + row + lo), __ldg(cell_start + row + hi + 1), A, c);
         }
     }
     force_finish<EPI>(A, i, ep, out);
@@ -485,47 +492,35 @@ __global__ void __launch_bounds__(128)
     const uint32_t i0 = sorted_idx[s0], i1 = has1 ? sorted_idx[s0 + 1] : 0xffffffffu;
     // rho < 1e-6 (1/rho stored as 0) or not updated (ghost): no walk
     const bool va = A.v.w != 0.f && i0 < out.limit, vb = has1 && B.v.w != 0.f && i1 < out.limit;
-    const Window w0 = make_window(A.p, g, c.h2_skip);
-    const Window w1 = make_window(B.p, g, c.h2_skip);
-    if (va && vb && w0.cy == w1.cy && w0.cz == w1.cz) {
-        const bool same_cell = w0.cx == w1.cx;
+    const Frame f0 = make_frame(A.p, g);
+    const Frame f1 = make_frame(B.p, g);
+    if (va && vb && g.pairable && f0.cy == f1.cy && f0.cz == f1.cz) {
 #pragma unroll 1
         for (int r = 0; r < 9; ++r) {
-            const bool e0 = w0.on(r), e1 = w1.on(r);
-            if (!e0 && !e1) continue;
-            const uint32_t row = row_base(g, w0.cy, w0.cz, r);
-            if (same_cell) {
-                const int lo = e0 ? (e1 ? min(w0.lo(r), w1.lo(r)) : w0.lo(r)) : w1.lo(r);
-                const int hi = e0 ? (e1 ? max(w0.hi(r), w1.hi(r)) : w0.hi(r)) : w1.hi(r);
-                force_two<TERMS>(pos4, vel4, pj, __ldg(cell_start + row + lo), __ldg(cell_start + row + hi), A, B,
-                                 c);
-            } else {
-                uint32_t lb0 = e0 ? __ldg(cell_start + row + w0.lo(r)) : 0u;
-                uint32_t le0 = e0 ? __ldg(cell_start + row + w0.hi(r)) : 0u;
-                uint32_t lb1 = e1 ? __ldg(cell_start + row + w1.lo(r)) : 0u;
-                uint32_t le1 = e1 ? __ldg(cell_start + row + w1.hi(r)) : 0u;
-                if (!e0) lb0 = le0 = lb1;
-                if (!e1) lb1 = le1 = le0;
-                force_one<TERMS>(pos4, vel4, pj, lb0, min(lb1, le0), A, c);
-                if (lb1 < le0) force_two<TERMS>(pos4, vel4, pj, lb1, le0, A, B, c);
-                force_one<TERMS>(pos4, vel4, pj, max(le0, lb1), le1, B, c);
-            }
+            int l0, h0, l1, h1, lo, hi;
+            const bool a = row_window(f0, r, g, c.h2_skip, l0, h0);
+            const bool b = row_window(f1, r, g, c.h2_skip, l1, h1);
+            if (!union_window(a, l0, h0, b, l1, h1, lo, hi)) continue;
+            const uint32_t row = row_base(g, f0, r);
+            force_two<TERMS>(pos4, vel4, pj, __ldg(cell_start + row + lo), __ldg(cell_start + row + hi + 1), A, B, c);
         }
     } else {
 #pragma unroll 1
         for (int r = 0; r < 9; ++r) {
-            if (va && w0.on(r)) {
-                const uint32_t row = row_base(g, w0.cy, w0.cz, r);
-                force_one<TERMS>(pos4, vel4, pj, __ldg(cell_start + row + w0.lo(r)),
-                                 __ldg(cell_start + row + w0.hi(r)), A, c);
+            int lo, hi;
+            if (va && row_window(f0, r, g, c.h2_skip, lo, hi)) {
+                const uint32_t row = row_base(g, f0, r);
+                force_one<TERMS>(pos4, vel4, pj, __ldg(cell_start + row + lo), __ldg(cell_start + row + hi + 1), A,
+                                 c);
             }
         }
 #pragma unroll 1
         for (int r = 0; r < 9; ++r) {
-            if (vb && w1.on(r)) {
-                const uint32_t row = row_base(g, w1.cy, w1.cz, r);
-                force_one<TERMS>(pos4, vel4, pj, __ldg(cell_start + row + w1.lo(r)),
-                                 __ldg(cell_start + row + w1.hi(r)), B, c);
+            int lo, hi;
+            if (vb && row_window(f1, r, g, c.h2_skip, lo, hi)) {
+                const uint32_t row = row_base(g, f1, r);
+                force_one<TERMS>(pos4, vel4, pj, __ldg(cell_start + row + lo), __ldg(cell_start + row + hi + 1), B,
+                                 c);
             }
         }
     }
