@@ -10,9 +10,10 @@ publishes no dataset for them, so every input is generated here from a seed
                    gravity (0,-9.81,0), box [0,1]^3, restitution 1.0.
 * cfg2 "dambreak1m": the config asks for 1M particles on a 0.5h lattice in
                    [0,0.4]x[0,0.8]x[0,0.4], which only holds 65,536; we keep
-                   N = 1,048,576 as a 64x128x64 lattice at spacing h/4 in the
-                   same region (~64 particles per cell), h 0.025, grid 40^3,
-                   dt 1e-4. The literal 0.5h lattice is "dambreak65k".
+                   the "1M" as N = 1,024,000: an 80x160x80 lattice at spacing
+                   h/5 = 0.005 filling the same region (125 particles per
+                   cell), h 0.025, grid 40^3, dt 1e-4. The literal 0.5h
+                   lattice is "dambreak65k".
 * cfg3 "sharded16m": 320x160x320 lattice at spacing h/2 in [0,1]x[0,0.5]x[0,1],
                    h = 0.00625, grid 160^3, dt 2.5e-5.
 * cfg4 "blobs4m":  4,194,304 points from 64 Gaussian blobs (centres uniform
@@ -71,8 +72,8 @@ def config(name: str) -> SphConfig:
     if name == "ref65k":
         return SphConfig(name, 65536, 0.025, 0.025, (40, 40, 40), 1.0, steps=100)
     if name == "dambreak1m":
-        s = 0.025 / 4
-        return SphConfig(name, 64 * 128 * 64, 0.025, 0.025, (40, 40, 40), 1000.0 * s ** 3, steps=1000)
+        s = 0.025 / 5
+        return SphConfig(name, 80 * 160 * 80, 0.025, 0.025, (40, 40, 40), 1000.0 * s ** 3, steps=1000)
     if name == "dambreak65k":
         s = 0.025 / 2
         return SphConfig(name, 32 * 64 * 32, 0.025, 0.025, (40, 40, 40), 1000.0 * s ** 3, steps=1000)
@@ -103,7 +104,7 @@ def particles(cfg: SphConfig, seed: int = SEED):
         vel = [rng.normal(0.0, 0.01, n).astype(np.float32) for _ in range(3)]
         return pos, vel
     if cfg.name == "dambreak1m":
-        pos = list(_lattice(64, 128, 64, 0.025 / 4))
+        pos = list(_lattice(80, 160, 80, 0.025 / 5))
     elif cfg.name == "dambreak65k":
         pos = list(_lattice(32, 64, 32, 0.025 / 2))
     elif cfg.name == "sharded16m":

@@ -250,3 +250,30 @@ def test_unfused_modules_sequence(cuda):
     v2, _ = oracle.force(p, 2, *pos, *v1, rho, cfg.cell_size, cfg.dims, cst, si, cfg.dt, threads=th)
     for k, a in enumerate("xyz"):
         np.testing.assert_allclose(host_f32(f.f32_fields["vel_" + a]), v2[k], rtol=1e-4, atol=1e-6)
+
+
+def test_step_is_capture_safe_in_a_cuda_graph(cuda):
+    """forge_sph_step only enqueues work (no allocation, no host sync), so a
+    captured step replayed K times equals K eager steps bit for bit -- the way
+    run_manifest drives the step (manifest_runner.rs:53-77)."""
+    torch = cuda
+    cfg = workloads.config("ref65k")
+    pos, vel = workloads.particles(cfg)
+    eager = gpu_steps(torch, cfg, pos, vel, 4)
+    g = forge_sph.HashGrid(cfg.cell_size, cfg.dims, (0, 0, 0), cfg.n, 0)
+    p, v = [dev(torch, x) for x in pos], [dev(torch, x) for x in vel]
+    rho = torch.empty(cfg.n, dtype=torch.float32, device="cuda")
+    sp, _ = make_step(cfg)
+    L = forge_sph.lib()
+    args = [x.data_ptr() for x in p + v] + [rho.data_ptr()]
+    side = torch.cuda.Stream()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        forge_sph.check(L.forge_sph_step(g.handle, ctypes.byref(gparams(cfg)), ctypes.byref(sp), *args, cfg.n,
+                                         side.cuda_stream))
+    for _ in range(4):
+        graph.replay()
+    torch.cuda.synchronize()
+    g.check()
+    for x, y in zip([host_f32(t) for t in p + v], eager[0] + eager[1]):
+        assert np.array_equal(x, y)
