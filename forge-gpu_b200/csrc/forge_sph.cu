@@ -843,10 +843,10 @@ extern "C" int forge_slab_classify(forge_slab* h, const float* x, uint64_t n, fl
     }
     const slab::ClassifyArgs a{lo, hi, reach, flags};
     const uint32_t tiles = grid_blocks(n, slab::kTile);
-    slab::classify_count_kernel<<<tiles, slab::kThreads, 0, st>>>(x, (uint32_t)n, a, h->tile_counts);
+    slab::classify_count_kernel<<<tiles, slab::kThreads, 0, st>>>(x, (uint32_t)n, nullptr, a, h->tile_counts);
     slab::classify_scan_kernel<<<1, 1024, 0, st>>>(h->tile_counts, tiles, counts);
-    slab::classify_write_kernel<<<tiles, slab::kThreads, 0, st>>>(x, (uint32_t)n, a, h->tile_counts, counts,
-                                                                  idx_out);
+    slab::classify_write_kernel<<<tiles, slab::kThreads, 0, st>>>(x, (uint32_t)n, nullptr, a, h->tile_counts,
+                                                                  counts, idx_out);
     FORGE_LAUNCHED();
     return FORGE_OK;
 }
@@ -856,7 +856,7 @@ extern "C" int forge_slab_compact(float* cols, uint64_t ld, uint32_t rows, uint6
     if (k == 0) return FORGE_OK;
     if (!cols || !gone || k > n || n >= 0xffffffffull)
         return set_error(FORGE_ERR_INVALID_ARG, "forge_slab_compact: bad arguments");
-    slab::compact_kernel<<<1, 1024, 0, as_stream(stream)>>>(cols, ld, rows, (uint32_t)n, gone, (uint32_t)k);
+    slab::compact_kernel<<<1, 1024, 0, as_stream(stream)>>>(cols, ld, rows, (uint32_t)n, gone, (uint32_t)k, nullptr);
     FORGE_LAUNCHED();
     return FORGE_OK;
 }

@@ -31,8 +31,10 @@ __device__ __forceinline__ uint32_t member_bits(float x, const ClassifyArgs& a) 
 
 // Pass 1: per-tile counts of each list.
 __global__ void __launch_bounds__(kThreads)
-    classify_count_kernel(const float* __restrict__ x, uint32_t n, ClassifyArgs a, uint32_t* __restrict__ tile_counts) {
+    classify_count_kernel(const float* __restrict__ x, uint32_t n, const uint32_t* __restrict__ n_sub, ClassifyArgs a,
+                          uint32_t* __restrict__ tile_counts) {
     __shared__ uint32_t s[kLists];
+    if (n_sub) n -= *n_sub;  // live length known only on the device
     if (threadIdx.x < kLists) s[threadIdx.x] = 0;
     __syncthreads();
     uint32_t c[kLists] = {0, 0, 0};
@@ -82,10 +84,11 @@ __global__ void __launch_bounds__(1024)
 // Pass 3: write each list's element indices in ascending order, packed as
 // [A | L | R].
 __global__ void __launch_bounds__(kThreads)
-    classify_write_kernel(const float* __restrict__ x, uint32_t n, ClassifyArgs a,
+    classify_write_kernel(const float* __restrict__ x, uint32_t n, const uint32_t* __restrict__ n_sub, ClassifyArgs a,
                           const uint32_t* __restrict__ tile_offsets, const uint32_t* __restrict__ counts,
                           uint32_t* __restrict__ out) {
     __shared__ uint32_t s_scan[kThreads / 32 + 1];
+    if (n_sub) n -= *n_sub;
     const uint32_t base = blockIdx.x * kTile + threadIdx.x * kItems;  // blocked: thread owns 16 consecutive
     uint32_t bits[kItems];
     uint32_t c[kLists] = {0, 0, 0};
@@ -114,8 +117,9 @@ __global__ void __launch_bounds__(kThreads)
 // move into the holes below n - k, in ascending order. One block.
 __global__ void __launch_bounds__(1024)
     compact_kernel(float* __restrict__ cols, uint64_t ld, uint32_t rows, uint32_t n, const uint32_t* __restrict__ gone,
-                   uint32_t k) {
+                   uint32_t k, const uint32_t* __restrict__ k_dev) {
     __shared__ uint32_t s_scan[1024 / 32 + 1];
+    if (k_dev) k = *k_dev;
     const uint32_t keep = n - k;
     uint32_t carry = 0;  // fillers ranked so far
     for (uint32_t b = 0; b < k; b += 1024) {
@@ -175,6 +179,41 @@ __global__ void __launch_bounds__(256)
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < k1) out[i] = rho[list[i]];
     else if (i < k1 + k2) out[i] = rho[start + i - k1];
+}
+
+}  // namespace slab
+}  // namespace forge
+
+namespace forge {
+namespace slab {
+
+// Packs list `list` (1 = L, 2 = R) of a classification [A | L | R] with
+// device-side sizes counts[3] into records at out + *rec0_dev (0 if null),
+// optionally copying the column indices to idx_copy. Grid-stride: the sizes
+// are not known on the host.
+__global__ void __launch_bounds__(256)
+    pack_dev_kernel(const float* __restrict__ cols, uint64_t ld, uint32_t rows, const uint32_t* __restrict__ idx,
+                    const uint32_t* __restrict__ counts, int list, const uint32_t* __restrict__ rec0_dev,
+                    float* __restrict__ out, uint32_t* __restrict__ idx_copy) {
+    const uint32_t off = counts[0] + (list == 2 ? counts[1] : 0u);
+    const uint32_t cnt = counts[list], rec0 = rec0_dev ? *rec0_dev : 0u;
+    for (uint32_t t = blockIdx.x * blockDim.x + threadIdx.x; t < cnt * rows; t += gridDim.x * blockDim.x) {
+        const uint32_t i = t / rows, r = t - i * rows;
+        const uint32_t col = idx[off + i];
+        out[(size_t)(rec0 + i) * rows + r] = cols[r * ld + col];
+        if (idx_copy && r == 0) idx_copy[i] = col;
+    }
+}
+
+// The counts message and bookkeeping from the two classifications:
+// mig = [A, L, R], halo = [0, L, R] -> msg[0..3] = mL, hL, mR, hR; msg[8] = A.
+__global__ void counts_msg_kernel(const uint32_t* __restrict__ mig, const uint32_t* __restrict__ halo,
+                                  uint64_t* __restrict__ msg) {
+    msg[0] = mig[1];
+    msg[1] = halo[1];
+    msg[2] = mig[2];
+    msg[3] = halo[2];
+    msg[8] = mig[0];
 }
 
 }  // namespace slab

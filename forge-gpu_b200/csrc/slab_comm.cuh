@@ -13,8 +13,9 @@
 //   forge_slab_exchange_rho (round 2, after density; sizes known, no sync)
 //     send rho of [halo sent to X, arrivals from X] to X; X's values land in
 //     [halo from X, our migrants to X].
-// Three stream synchronisations per round 1 (two list sizes, one count
-// exchange); everything else is enqueued.
+// One stream synchronisation per round 1 (after the count exchange: NCCL
+// needs the payload sizes on the host); every list size before it stays on
+// the device.
 #pragma once
 
 #include <dlfcn.h>
@@ -73,13 +74,15 @@ constexpr uint32_t kSlabRows = 7;  // x, y, z, vx, vy, vz, id bits
 
 struct forge_slab_comm {
     int device = 0, rank = 0, world = 1;
+    int sms = 148;
     int left = -1, right = -1;
     uint64_t cap = 0;
     float lo = 0.f, hi = 0.f, reach = 0.f;
     ncclComm_t comm = nullptr;
     forge_slab* sel = nullptr;
-    uint32_t* idx = nullptr;       // classify output, 2 cap
-    uint32_t* counts = nullptr;    // 3 device words
+    uint32_t* idx = nullptr;       // migrant classification [A | L | R], 2 cap
+    uint32_t* idx_h = nullptr;     // halo classification [L | R], 2 cap
+    uint32_t* counts = nullptr;    // 6 device words: migrant sizes A, L, R; halo sizes 0, L, R
     uint32_t* hcounts = nullptr;   // 3 pinned host words
     uint32_t* halo_l = nullptr;    // halo lists of the last round (cap each)
     uint32_t* halo_r = nullptr;
@@ -91,7 +94,7 @@ struct forge_slab_comm {
     float* rho_send_r = nullptr;
     float* rho_recv_l = nullptr;
     float* rho_recv_r = nullptr;
-    uint64_t* dcount = nullptr;    // [send l(2) | send r(2) | recv l(2) | recv r(2)]
+    uint64_t* dcount = nullptr;    // [send l(2) | send r(2) | recv l(2) | recv r(2) | migrants A]
     uint64_t* hcount = nullptr;    // pinned mirror
     // bookkeeping of the last round 1
     uint32_t n_hl = 0, n_hr = 0;          // halo rows sent left / right
@@ -110,20 +113,13 @@ void slab_comm_free(forge_slab_comm* c) {
     DeviceScope scope(c->device);
     if (c->comm) g_nccl.CommDestroy(c->comm);
     forge_slab_destroy(c->sel);
-    for (void* p : {(void*)c->idx, (void*)c->counts, (void*)c->halo_l, (void*)c->halo_r, (void*)c->send_l,
+    for (void* p : {(void*)c->idx, (void*)c->idx_h, (void*)c->counts, (void*)c->halo_l, (void*)c->halo_r, (void*)c->send_l,
                     (void*)c->send_r, (void*)c->recv_l, (void*)c->recv_r, (void*)c->rho_send_l,
                     (void*)c->rho_send_r, (void*)c->rho_recv_l, (void*)c->rho_recv_r, (void*)c->dcount})
         cudaFree(p);
     cudaFreeHost(c->hcounts);
     cudaFreeHost(c->hcount);
     delete c;
-}
-
-int pack(float* cols, uint64_t ld, const uint32_t* idx, uint32_t k, float* out, cudaStream_t st) {
-    if (!k) return FORGE_OK;
-    slab::pack_kernel<<<grid_blocks((uint64_t)k * kSlabRows, 256), 256, 0, st>>>(cols, ld, kSlabRows, idx, k, out);
-    FORGE_LAUNCHED();
-    return FORGE_OK;
 }
 
 int unpack(const float* in, uint32_t k, float* cols, uint64_t ld, uint32_t dst, cudaStream_t st) {
@@ -133,13 +129,28 @@ int unpack(const float* in, uint32_t k, float* cols, uint64_t ld, uint32_t dst, 
     return FORGE_OK;
 }
 
-// Runs forge_slab_classify and reads the three list sizes back (one sync).
-int classify_sync(forge_slab_comm* c, const float* x, uint64_t n, uint32_t flags, uint32_t sizes[3], cudaStream_t st) {
-    int rc = forge_slab_classify(c->sel, x, n, c->lo, c->hi, c->reach, flags, c->idx, c->counts, st);
-    if (rc != FORGE_OK) return rc;
-    FORGE_CUDA(cudaMemcpyAsync(c->hcounts, c->counts, 3 * sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
-    FORGE_CUDA(cudaStreamSynchronize(st));
-    for (int i = 0; i < 3; ++i) sizes[i] = c->hcounts[i];
+// Enqueues a classification of x[0, n - *n_sub) into idx/counts (no sync).
+int classify_async(forge_slab_comm* c, const float* x, uint64_t n, const uint32_t* n_sub, uint32_t flags,
+                   uint32_t* idx, uint32_t* counts, cudaStream_t st) {
+    if (n == 0) {
+        FORGE_CUDA(cudaMemsetAsync(counts, 0, 3 * sizeof(uint32_t), st));
+        return FORGE_OK;
+    }
+    const slab::ClassifyArgs a{c->lo, c->hi, c->reach, flags};
+    const uint32_t tiles = grid_blocks(n, slab::kTile);
+    slab::classify_count_kernel<<<tiles, slab::kThreads, 0, st>>>(x, (uint32_t)n, n_sub, a, c->sel->tile_counts);
+    slab::classify_scan_kernel<<<1, 1024, 0, st>>>(c->sel->tile_counts, tiles, counts);
+    slab::classify_write_kernel<<<tiles, slab::kThreads, 0, st>>>(x, (uint32_t)n, n_sub, a, c->sel->tile_counts,
+                                                                  counts, idx);
+    FORGE_LAUNCHED();
+    return FORGE_OK;
+}
+
+int pack_list(forge_slab_comm* c, const float* cols, uint64_t ld, const uint32_t* idx, const uint32_t* counts,
+              int list, const uint32_t* rec0, float* out, uint32_t* idx_copy, cudaStream_t st) {
+    slab::pack_dev_kernel<<<(uint32_t)c->sms * 4, 256, 0, st>>>(cols, ld, kSlabRows, idx, counts, list,
+                                                                             rec0, out, idx_copy);
+    FORGE_LAUNCHED();
     return FORGE_OK;
 }
 
@@ -166,6 +177,7 @@ extern "C" int forge_slab_comm_create(const uint8_t* id, int rank, int world, in
     FORGE_DEVICE_SCOPE(device);
     forge_slab_comm* c = new forge_slab_comm;
     c->device = device;
+    c->sms = num_sms(device);
     c->rank = rank;
     c->world = world;
     c->left = rank > 0 ? rank - 1 : -1;
@@ -175,15 +187,16 @@ extern "C" int forge_slab_comm_create(const uint8_t* id, int rank, int world, in
     c->hi = hi;
     c->reach = reach;
     const size_t m = capacity;
-    bool ok = dalloc(&c->idx, 2 * m) == cudaSuccess && dalloc(&c->counts, 3) == cudaSuccess &&
+    bool ok = dalloc(&c->idx, 2 * m) == cudaSuccess && dalloc(&c->idx_h, 2 * m) == cudaSuccess &&
+              dalloc(&c->counts, 6) == cudaSuccess &&
               dalloc(&c->halo_l, m) == cudaSuccess && dalloc(&c->halo_r, m) == cudaSuccess &&
               dalloc(&c->send_l, m * kSlabRows) == cudaSuccess && dalloc(&c->send_r, m * kSlabRows) == cudaSuccess &&
               dalloc(&c->recv_l, m * kSlabRows) == cudaSuccess && dalloc(&c->recv_r, m * kSlabRows) == cudaSuccess &&
               dalloc(&c->rho_send_l, m) == cudaSuccess && dalloc(&c->rho_send_r, m) == cudaSuccess &&
               dalloc(&c->rho_recv_l, m) == cudaSuccess && dalloc(&c->rho_recv_r, m) == cudaSuccess &&
-              dalloc(&c->dcount, 8) == cudaSuccess &&
+              dalloc(&c->dcount, 9) == cudaSuccess &&
               cudaMallocHost(&c->hcounts, 3 * sizeof(uint32_t)) == cudaSuccess &&
-              cudaMallocHost(&c->hcount, 8 * sizeof(uint64_t)) == cudaSuccess;
+              cudaMallocHost(&c->hcount, 9 * sizeof(uint64_t)) == cudaSuccess;
     if (!ok) {
         slab_comm_free(c);
         return set_error(FORGE_ERR_CUDA, "forge_slab_comm_create: allocation failed (capacity %llu)",
@@ -219,41 +232,31 @@ extern "C" int forge_slab_exchange(forge_slab_comm* c, float* cols, uint64_t ld,
     FORGE_DEVICE_SCOPE(c->device);
     cudaStream_t st = as_stream(stream);
     const uint32_t sides = (c->left >= 0 ? 1u : 0u) | (c->right >= 0 ? 2u : 0u);
-    uint32_t sz[3] = {0, 0, 0};
+    uint32_t* cm = c->counts;      // migrant list sizes A, L, R
+    uint32_t* ch = c->counts + 3;  // halo list sizes 0, L, R
     int rc;
-    // 1. migrants: pack, then remove from the owned columns
-    uint32_t ml = 0, mr = 0, keep = (uint32_t)n_own;
-    if (migrate && n_own) {
-        rc = classify_sync(c, cols, n_own, sides, sz, st);
-        if (rc != FORGE_OK) return rc;
-        ml = sz[1];
-        mr = sz[2];
-        if ((rc = pack(cols, ld, c->idx + sz[0], ml, c->send_l, st)) != FORGE_OK) return rc;
-        if ((rc = pack(cols, ld, c->idx + sz[0] + ml, mr, c->send_r, st)) != FORGE_OK) return rc;
-        if ((rc = forge_slab_compact(cols, ld, kSlabRows, n_own, c->idx, sz[0], st)) != FORGE_OK) return rc;
-        keep = (uint32_t)n_own - sz[0];
+    // All list sizes stay on the device until the count exchange below: one
+    // host synchronisation per round.
+    // 1. migrants: classify, pack (before the compaction moves columns), remove
+    if (migrate) {
+        if ((rc = classify_async(c, cols, n_own, nullptr, sides, c->idx, cm, st)) != FORGE_OK) return rc;
+        if ((rc = pack_list(c, cols, ld, c->idx, cm, 1, nullptr, c->send_l, nullptr, st)) != FORGE_OK) return rc;
+        if ((rc = pack_list(c, cols, ld, c->idx, cm, 2, nullptr, c->send_r, nullptr, st)) != FORGE_OK) return rc;
+        if (n_own) {
+            slab::compact_kernel<<<1, 1024, 0, st>>>(cols, ld, kSlabRows, (uint32_t)n_own, c->idx, 0u, cm);
+            FORGE_LAUNCHED();
+        }
+    } else {
+        FORGE_CUDA(cudaMemsetAsync(cm, 0, 3 * sizeof(uint32_t), st));
     }
-    // 2. halo rows of the remaining owned particles
-    uint32_t hl = 0, hr = 0;
-    if (keep) {
-        rc = classify_sync(c, cols, keep, sides | 4u, sz, st);
-        if (rc != FORGE_OK) return rc;
-        hl = sz[1];
-        hr = sz[2];
-    }
-    if ((uint64_t)ml + hl > c->cap || (uint64_t)mr + hr > c->cap)
-        return set_error(FORGE_ERR_CAPACITY, "forge_slab_exchange: message exceeds capacity");
-    if (hl) FORGE_CUDA(cudaMemcpyAsync(c->halo_l, c->idx + sz[0], hl * 4, cudaMemcpyDeviceToDevice, st));
-    if (hr) FORGE_CUDA(cudaMemcpyAsync(c->halo_r, c->idx + sz[0] + hl, hr * 4, cudaMemcpyDeviceToDevice, st));
-    if ((rc = pack(cols, ld, c->halo_l, hl, c->send_l + (size_t)ml * kSlabRows, st)) != FORGE_OK) return rc;
-    if ((rc = pack(cols, ld, c->halo_r, hr, c->send_r + (size_t)mr * kSlabRows, st)) != FORGE_OK) return rc;
-    // 3. counts
-    c->hcount[0] = ml;
-    c->hcount[1] = hl;
-    c->hcount[2] = mr;
-    c->hcount[3] = hr;
-    c->hcount[4] = c->hcount[5] = c->hcount[6] = c->hcount[7] = 0;
-    FORGE_CUDA(cudaMemcpyAsync(c->dcount, c->hcount, 8 * sizeof(uint64_t), cudaMemcpyHostToDevice, st));
+    // 2. halo rows of the remaining owned particles, after the migrants
+    if ((rc = classify_async(c, cols, n_own, cm, sides | 4u, c->idx_h, ch, st)) != FORGE_OK) return rc;
+    if ((rc = pack_list(c, cols, ld, c->idx_h, ch, 1, cm + 1, c->send_l, c->halo_l, st)) != FORGE_OK) return rc;
+    if ((rc = pack_list(c, cols, ld, c->idx_h, ch, 2, cm + 2, c->send_r, c->halo_r, st)) != FORGE_OK) return rc;
+    // 3. counts: ours to the neighbours, theirs back, everything to the host
+    slab::counts_msg_kernel<<<1, 1, 0, st>>>(cm, ch, c->dcount);
+    FORGE_LAUNCHED();
+    FORGE_CUDA(cudaMemsetAsync(c->dcount + 4, 0, 4 * sizeof(uint64_t), st));
     FORGE_NCCL(g_nccl.GroupStart());
     if (c->left >= 0) {
         FORGE_NCCL(g_nccl.Send(c->dcount + 0, 2, ncclUint64, c->left, c->comm, st));
@@ -264,11 +267,14 @@ extern "C" int forge_slab_exchange(forge_slab_comm* c, float* cols, uint64_t ld,
         FORGE_NCCL(g_nccl.Recv(c->dcount + 6, 2, ncclUint64, c->right, c->comm, st));
     }
     FORGE_NCCL(g_nccl.GroupEnd());
-    FORGE_CUDA(cudaMemcpyAsync(c->hcount + 4, c->dcount + 4, 4 * sizeof(uint64_t), cudaMemcpyDeviceToHost, st));
+    FORGE_CUDA(cudaMemcpyAsync(c->hcount, c->dcount, 9 * sizeof(uint64_t), cudaMemcpyDeviceToHost, st));
     FORGE_CUDA(cudaStreamSynchronize(st));
+    const uint32_t ml = (uint32_t)c->hcount[0], hl = (uint32_t)c->hcount[1];
+    const uint32_t mr = (uint32_t)c->hcount[2], hr = (uint32_t)c->hcount[3];
     const uint64_t aml = c->hcount[4], ahl = c->hcount[5], amr = c->hcount[6], ahr = c->hcount[7];
-    if (aml + ahl > c->cap || amr + ahr > c->cap)
-        return set_error(FORGE_ERR_CAPACITY, "forge_slab_exchange: incoming message exceeds capacity");
+    const uint32_t keep = (uint32_t)(n_own - c->hcount[8]);
+    if ((uint64_t)ml + hl > c->cap || (uint64_t)mr + hr > c->cap || aml + ahl > c->cap || amr + ahr > c->cap)
+        return set_error(FORGE_ERR_CAPACITY, "forge_slab_exchange: message exceeds capacity");
     const uint64_t n_new = keep + aml + amr;
     const uint64_t ng = ahl + ahr + ml + mr;
     if (n_new + ng > ld) return set_error(FORGE_ERR_CAPACITY, "forge_slab_exchange: owned + ghosts exceed ld");
