@@ -714,6 +714,11 @@ sph::StepEpi epi_of(const forge_step_params* sp) {
     }
     ep.restitution = sp->restitution;
     ep.flags = sp->flags;
+    ep.n_ops = sp->n_ops;
+    for (uint32_t k = 0; k < ep.n_ops; ++k) {
+        ep.ops[k].kind = sp->ops[k].kind;
+        for (int q = 0; q < 7; ++q) ep.ops[k].p[q] = sp->ops[k].p[q];
+    }
     return ep;
 }
 }  // namespace
@@ -722,6 +727,7 @@ extern "C" int forge_sph_force_step(forge_grid* g, const forge_sph_params* p, co
                                     float* px, float* py, float* pz, float* vx, float* vy, float* vz,
                                     const float* density, uint64_t n, uint64_t n_update, void* stream) {
     if (!g || !p || !sp) return set_error(FORGE_ERR_INVALID_ARG, "forge_sph_force_step: NULL grid or params");
+    if (sp->n_ops > FORGE_STEP_MAX_OPS) return set_error(FORGE_ERR_INVALID_ARG, "forge_sph_force_step: n_ops > 8");
     if (!g->built || g->n != n)
         return set_error(FORGE_ERR_INVALID_ARG,
                          "forge_sph_force_step: the grid was not built for these %llu particles (last build: %llu)",
@@ -746,6 +752,7 @@ extern "C" int forge_sph_step(forge_grid* g, const forge_sph_params* p, const fo
                               float* py, float* pz, float* vx, float* vy, float* vz, float* density, uint64_t n,
                               void* stream) {
     if (!g || !p || !sp) return set_error(FORGE_ERR_INVALID_ARG, "forge_sph_step: NULL grid or params");
+    if (sp->n_ops > FORGE_STEP_MAX_OPS) return set_error(FORGE_ERR_INVALID_ARG, "forge_sph_step: n_ops > 8");
     if (n && (!px || !py || !pz || !vx || !vy || !vz))
         return set_error(FORGE_ERR_INVALID_ARG, "forge_sph_step: NULL position/velocity pointer");
     FORGE_DEVICE_SCOPE(g->device);

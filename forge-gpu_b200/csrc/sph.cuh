@@ -290,13 +290,92 @@ struct ForceOut {
     uint32_t limit;  // only particles with original index < limit are written
 };
 
+struct StepOp {
+    uint32_t kind;  // FORGE_OP_*
+    float p[7];
+};
+
 struct StepEpi {
     float dt;
     float gx, gy, gz;
     float bmin[3], bmax[3];
     float restitution;
-    uint32_t flags;  // FORGE_STEP_* bits
+    uint32_t flags;  // FORGE_STEP_* bits (used when n_ops == 0)
+    uint32_t n_ops;
+    StepOp ops[8];
 };
+
+// BoxColliderModule: box_collider.rs:36-46.
+__device__ __forceinline__ void box_op(float& x, float& y, float& z, float& vx, float& vy, float& vz, const float* mn,
+                                       const float* mx, float e) {
+    if (x < mn[0]) { x = mn[0]; vx = fabsf(vx) * e; }
+    if (x > mx[0]) { x = mx[0]; vx = -fabsf(vx) * e; }
+    if (y < mn[1]) { y = mn[1]; vy = fabsf(vy) * e; }
+    if (y > mx[1]) { y = mx[1]; vy = -fabsf(vy) * e; }
+    if (z < mn[2]) { z = mn[2]; vz = fabsf(vz) * e; }
+    if (z > mx[2]) { z = mx[2]; vz = -fabsf(vz) * e; }
+}
+
+// The manifest modules after the SPH module, in list order.
+__device__ __forceinline__ void apply_ops(const StepEpi& ep, float& x, float& y, float& z, float& vx, float& vy,
+                                          float& vz) {
+    const float dt = ep.dt;
+    for (uint32_t k = 0; k < ep.n_ops; ++k) {
+        const StepOp& o = ep.ops[k];
+        switch (o.kind) {
+            case 1u:  // gravity.rs:31-34
+                vx += o.p[0] * dt;
+                vy += o.p[1] * dt;
+                vz += o.p[2] * dt;
+                break;
+            case 2u: {  // drag.rs:18-20
+                const float d = 1.0f - o.p[0] * dt;
+                vx *= d;
+                vy *= d;
+                vz *= d;
+                break;
+            }
+            case 3u:  // integrate.rs:16-31
+                if (!isfinite(vx)) vx = 0.f;
+                if (!isfinite(vy)) vy = 0.f;
+                if (!isfinite(vz)) vz = 0.f;
+                x += vx * dt;
+                y += vy * dt;
+                z += vz * dt;
+                break;
+            case 4u:  // ground_plane.rs:19-21
+                if (y < o.p[0]) {
+                    y = o.p[0];
+                    vy = -vy * o.p[1];
+                }
+                break;
+            case 5u: {  // sphere_collider.rs:22-41
+                const float dx = x - o.p[0], dy = y - o.p[1], dz = z - o.p[2];
+                const float dist = sqrtf(dx * dx + dy * dy + dz * dz);
+                const float r = o.p[3];
+                if (dist < r && dist > 1e-8f) {
+                    const float inv = 1.0f / dist;
+                    const float nx = dx * inv, ny = dy * inv, nz = dz * inv;
+                    x = o.p[0] + nx * r;
+                    y = o.p[1] + ny * r;
+                    z = o.p[2] + nz * r;
+                    const float vn = vx * nx + vy * ny + vz * nz;
+                    if (vn < 0) {
+                        vx -= (1 + o.p[4]) * vn * nx;
+                        vy -= (1 + o.p[4]) * vn * ny;
+                        vz -= (1 + o.p[4]) * vn * nz;
+                    }
+                }
+                break;
+            }
+            case 6u:  // box_collider.rs:36-46
+                box_op(x, y, z, vx, vy, vz, &o.p[0], &o.p[3], o.p[6]);
+                break;
+            default:
+                break;
+        }
+    }
+}
 
 // One particle's state in the force pass.
 struct ForceAcc {
@@ -413,31 +492,26 @@ __device__ __forceinline__ void force_finish(const ForceAcc& A, uint32_t i, cons
         }
         return;
     }
-    // GravityModule: gravity.rs:31-34.
-    if (ep.flags & 1u) {
-        vx += ep.gx * ep.dt;
-        vy += ep.gy * ep.dt;
-        vz += ep.gz * ep.dt;
-    }
     float x = A.p.x, y = A.p.y, z = A.p.z;
-    // IntegrateModule: integrate.rs:16-31.
-    if (ep.flags & 2u) {
-        if (!isfinite(vx)) vx = 0.f;
-        if (!isfinite(vy)) vy = 0.f;
-        if (!isfinite(vz)) vz = 0.f;
-        x += vx * ep.dt;
-        y += vy * ep.dt;
-        z += vz * ep.dt;
-    }
-    // BoxColliderModule: box_collider.rs:36-46.
-    if (ep.flags & 4u) {
-        const float e = ep.restitution;
-        if (x < ep.bmin[0]) { x = ep.bmin[0]; vx = fabsf(vx) * e; }
-        if (x > ep.bmax[0]) { x = ep.bmax[0]; vx = -fabsf(vx) * e; }
-        if (y < ep.bmin[1]) { y = ep.bmin[1]; vy = fabsf(vy) * e; }
-        if (y > ep.bmax[1]) { y = ep.bmax[1]; vy = -fabsf(vy) * e; }
-        if (z < ep.bmin[2]) { z = ep.bmin[2]; vz = fabsf(vz) * e; }
-        if (z > ep.bmax[2]) { z = ep.bmax[2]; vz = -fabsf(vz) * e; }
+    if (ep.n_ops) {
+        apply_ops(ep, x, y, z, vx, vy, vz);
+    } else {
+        // GravityModule: gravity.rs:31-34.
+        if (ep.flags & 1u) {
+            vx += ep.gx * ep.dt;
+            vy += ep.gy * ep.dt;
+            vz += ep.gz * ep.dt;
+        }
+        // IntegrateModule: integrate.rs:16-31.
+        if (ep.flags & 2u) {
+            if (!isfinite(vx)) vx = 0.f;
+            if (!isfinite(vy)) vy = 0.f;
+            if (!isfinite(vz)) vz = 0.f;
+            x += vx * ep.dt;
+            y += vy * ep.dt;
+            z += vz * ep.dt;
+        }
+        if (ep.flags & 4u) box_op(x, y, z, vx, vy, vz, ep.bmin, ep.bmax, ep.restitution);
     }
     out.px[i] = x;
     out.py[i] = y;

@@ -37,6 +37,9 @@ FORGE_ERR_TIMEOUT = -4
 FORGE_ERR_NCCL = -5
 FORGE_ERR_DEVICE = -6
 
+OP_GRAVITY, OP_DRAG, OP_INTEGRATE, OP_GROUND, OP_SPHERE, OP_BOX = 1, 2, 3, 4, 5, 6
+STEP_MAX_OPS = 8
+
 TERM_PRESSURE = 1
 TERM_VISCOSITY = 2
 STEP_GRAVITY = 1
@@ -83,9 +86,14 @@ class SphParams(ctypes.Structure):
                 ("rest_density", ctypes.c_float), ("viscosity", ctypes.c_float)]
 
 
+class StepOp(ctypes.Structure):
+    _fields_ = [("kind", ctypes.c_uint32), ("p", ctypes.c_float * 7)]
+
+
 class StepParams(ctypes.Structure):
     _fields_ = [("dt", ctypes.c_float), ("gravity", ctypes.c_float * 3), ("box_min", ctypes.c_float * 3),
-                ("box_max", ctypes.c_float * 3), ("restitution", ctypes.c_float), ("flags", ctypes.c_uint32)]
+                ("box_max", ctypes.c_float * 3), ("restitution", ctypes.c_float), ("flags", ctypes.c_uint32),
+                ("n_ops", ctypes.c_uint32), ("ops", StepOp * 8)]
 
 
 _lib = None
@@ -493,6 +501,9 @@ class GravityModule(SimModule):
     def name(self) -> str:
         return "gravity"
 
+    def op(self):
+        return OP_GRAVITY, [self.gx, self.gy, self.gz]
+
     def execute(self, fields: FieldSet, dt: float, stream=None) -> None:
         f = fields.f32_fields
         f["vel_x"].add_(self.gx * dt)
@@ -506,6 +517,9 @@ class IntegrateModule(SimModule):
 
     def name(self) -> str:
         return "integrate"
+
+    def op(self):
+        return OP_INTEGRATE, []
 
     def execute(self, fields: FieldSet, dt: float, stream=None) -> None:
         torch = _torch()
@@ -530,6 +544,9 @@ class BoxColliderModule(SimModule):
     def name(self) -> str:
         return "box_collider"
 
+    def op(self):
+        return OP_BOX, [self.min_x, self.min_y, self.min_z, self.max_x, self.max_y, self.max_z, self.restitution]
+
     def execute(self, fields: FieldSet, dt: float, stream=None) -> None:
         torch = _torch()
         f = fields.f32_fields
@@ -543,11 +560,86 @@ class BoxColliderModule(SimModule):
             p.clamp_(max=hi)
 
 
+@dataclass
+class DragModule(SimModule):
+    """DragModule (drag.rs:5-20): v *= 1 - coefficient * dt."""
+    coefficient: float = 0.0
+
+    def name(self) -> str:
+        return "drag"
+
+    def op(self):
+        return OP_DRAG, [self.coefficient]
+
+    def execute(self, fields: FieldSet, dt: float, stream=None) -> None:
+        torch = _torch()
+        d = torch.tensor(1.0, dtype=torch.float32) - torch.tensor(self.coefficient, dtype=torch.float32) * \
+            torch.tensor(dt, dtype=torch.float32)
+        for a in "xyz":
+            fields.f32_fields["vel_" + a].mul_(d.item())
+
+
+@dataclass
+class GroundPlaneModule(SimModule):
+    """GroundPlaneModule (ground_plane.rs:5-21): y < ground -> y = ground, vy = -vy * e."""
+    y: float = 0.0
+    restitution: float = 0.5
+
+    def name(self) -> str:
+        return "ground_plane"
+
+    def op(self):
+        return OP_GROUND, [self.y, self.restitution]
+
+    def execute(self, fields: FieldSet, dt: float, stream=None) -> None:
+        torch = _torch()
+        py, vy = fields.f32_fields["pos_y"], fields.f32_fields["vel_y"]
+        below = py < self.y
+        vy.copy_(torch.where(below, -vy * self.restitution, vy))
+        py.clamp_(min=self.y)
+
+
+@dataclass
+class SphereColliderModule(SimModule):
+    """SphereColliderModule (sphere_collider.rs:5-41): push particles inside the
+    sphere to its surface and reflect the inward normal velocity."""
+    cx: float = 0.0
+    cy: float = 0.0
+    cz: float = 0.0
+    radius: float = 1.0
+    restitution: float = 0.5
+
+    def name(self) -> str:
+        return "sphere_collider"
+
+    def op(self):
+        return OP_SPHERE, [self.cx, self.cy, self.cz, self.radius, self.restitution]
+
+    def execute(self, fields: FieldSet, dt: float, stream=None) -> None:
+        torch = _torch()
+        f = fields.f32_fields
+        p = [f["pos_" + a] for a in "xyz"]
+        v = [f["vel_" + a] for a in "xyz"]
+        c = (self.cx, self.cy, self.cz)
+        d = [p[k] - c[k] for k in range(3)]
+        dist = torch.sqrt(d[0] * d[0] + d[1] * d[1] + d[2] * d[2])
+        hit = (dist < self.radius) & (dist > 1e-8)
+        inv = 1.0 / torch.where(hit, dist, torch.ones_like(dist))
+        nrm = [d[k] * inv for k in range(3)]
+        vn = v[0] * nrm[0] + v[1] * nrm[1] + v[2] * nrm[2]
+        refl = hit & (vn < 0)
+        for k in range(3):
+            p[k].copy_(torch.where(hit, c[k] + nrm[k] * self.radius, p[k]))
+            v[k].copy_(torch.where(refl, v[k] - (1 + self.restitution) * vn * nrm[k], v[k]))
+
+
 class Pipeline:
     """Pipeline (modules/mod.rs:74-117). `step_async` recognises the manifest
-    SPH pattern (SphFused [+ Gravity] [+ Integrate] [+ BoxCollider]) and runs
-    it as ONE forge_sph_step call (grid build, density, force and epilogue);
-    anything else runs module by module."""
+    SPH pattern -- SphFusedModule followed only by per-particle modules
+    (gravity, drag, integrate, ground plane, sphere and box colliders, in any
+    order, at most 8) -- and runs it as ONE forge_sph_step call whose force
+    kernel applies those modules in order; anything else runs module by
+    module."""
 
     def __init__(self):
         self.modules: list = []
@@ -561,23 +653,16 @@ class Pipeline:
     def _fused_plan(self):
         if not self.modules or not isinstance(self.modules[0], SphFusedModule):
             return None
+        rest = self.modules[1:]
+        if len(rest) > STEP_MAX_OPS or not all(hasattr(m, "op") for m in rest):
+            return None
         sp = StepParams()
-        order = [GravityModule, IntegrateModule, BoxColliderModule]
-        flags = {GravityModule: STEP_GRAVITY, IntegrateModule: STEP_INTEGRATE, BoxColliderModule: STEP_BOX}
-        k = 0
-        for m in self.modules[1:]:
-            while k < len(order) and not isinstance(m, order[k]):
-                k += 1
-            if k == len(order):
-                return None
-            sp.flags |= flags[order[k]]
-            if isinstance(m, GravityModule):
-                sp.gravity[:] = [m.gx, m.gy, m.gz]
-            elif isinstance(m, BoxColliderModule):
-                sp.box_min[:] = [m.min_x, m.min_y, m.min_z]
-                sp.box_max[:] = [m.max_x, m.max_y, m.max_z]
-                sp.restitution = m.restitution
-            k += 1
+        sp.n_ops = len(rest)
+        for k, m in enumerate(rest):
+            kind, params = m.op()
+            sp.ops[k].kind = kind
+            for q, v in enumerate(params):
+                sp.ops[k].p[q] = v
         return sp
 
     def step_async(self, fields: FieldSet, dt: float, stream=None) -> None:

@@ -206,9 +206,29 @@ typedef struct forge_sph_params {
 #define FORGE_TERM_PRESSURE 0x1u  /* sph_pressure.rs:28-112   */
 #define FORGE_TERM_VISCOSITY 0x2u /* sph_viscosity.rs:27-106  */
 
-/* Per-step epilogue of the manifest pipeline after the SPH module
- * (manifest_runner.rs:371-541): GravityModule (gravity.rs:31-34),
- * IntegrateModule (integrate.rs:16-31), BoxColliderModule (box_collider.rs:26-47). */
+/* One per-particle module of the manifest pipeline after the SPH module,
+ * applied in list order in the force kernel's epilogue (forge-manifest/src/
+ * manifest_runner.rs:371-541 adds forces, then IntegrateModule, then the
+ * constraints in TOML order). */
+typedef struct forge_step_op {
+    uint32_t kind; /* FORGE_OP_* */
+    float p[7];
+} forge_step_op;
+
+#define FORGE_OP_GRAVITY 1u   /* v += g dt, p[0..2] = g            (gravity.rs:31-34)          */
+#define FORGE_OP_DRAG 2u      /* v *= 1 - c dt, p[0] = c            (drag.rs:18-20)             */
+#define FORGE_OP_INTEGRATE 3u /* NaN/Inf v -> 0, x += v dt          (integrate.rs:16-31)        */
+#define FORGE_OP_GROUND 4u    /* y < p[0]: y = p[0], vy = -vy p[1]  (ground_plane.rs:19-21)     */
+#define FORGE_OP_SPHERE 5u    /* centre p[0..2], radius p[3], restitution p[4]
+                                                                    (sphere_collider.rs:22-41)  */
+#define FORGE_OP_BOX 6u       /* min p[0..2], max p[3..5], restitution p[6]
+                                                                    (box_collider.rs:26-47)     */
+#define FORGE_STEP_MAX_OPS 8
+
+/* Per-step epilogue after the SPH module. With n_ops == 0 the flags select
+ * the common GravityModule -> IntegrateModule -> BoxColliderModule chain
+ * (manifest_runner.rs:371-541); with n_ops > 0 the op list is applied
+ * instead, in order. */
 typedef struct forge_step_params {
     float dt;
     float gravity[3];    /* v += g dt                     (flags & FORGE_STEP_GRAVITY)   */
@@ -216,6 +236,8 @@ typedef struct forge_step_params {
     float box_max[3];
     float restitution;
     uint32_t flags;
+    uint32_t n_ops;
+    forge_step_op ops[FORGE_STEP_MAX_OPS];
 } forge_step_params;
 
 #define FORGE_STEP_GRAVITY 0x1u

@@ -452,6 +452,72 @@ void orc_force(const orc_sph_params* p, uint32_t terms, const float* px, const f
     (void)threads;
 }
 
+/* One per-particle module after the SPH module:
+ * 1 gravity.rs:31-34, 2 drag.rs:18-20, 3 integrate.rs:16-31,
+ * 4 ground_plane.rs:19-21, 5 sphere_collider.rs:22-41, 6 box_collider.rs:36-46. */
+static void orc_apply_op(const orc_step_op* o, float dt, float* x, float* y, float* z, float* vx, float* vy,
+                         float* vz) {
+    switch (o->kind) {
+        case 1:
+            *vx += o->p[0] * dt;
+            *vy += o->p[1] * dt;
+            *vz += o->p[2] * dt;
+            break;
+        case 2: {
+            const float d = 1.0f - o->p[0] * dt;
+            *vx *= d;
+            *vy *= d;
+            *vz *= d;
+            break;
+        }
+        case 3:
+            if (!isfinite(*vx)) *vx = 0.0f;
+            if (!isfinite(*vy)) *vy = 0.0f;
+            if (!isfinite(*vz)) *vz = 0.0f;
+            *x += *vx * dt;
+            *y += *vy * dt;
+            *z += *vz * dt;
+            break;
+        case 4:
+            if (*y < o->p[0]) {
+                *y = o->p[0];
+                *vy = -*vy * o->p[1];
+            }
+            break;
+        case 5: {
+            const float dx = *x - o->p[0], dy = *y - o->p[1], dz = *z - o->p[2];
+            const float dist = sqrtf(dx * dx + dy * dy + dz * dz);
+            const float r = o->p[3];
+            if (dist < r && dist > 1e-8f) {
+                const float inv = 1.0f / dist;
+                const float nx = dx * inv, ny = dy * inv, nz = dz * inv;
+                *x = o->p[0] + nx * r;
+                *y = o->p[1] + ny * r;
+                *z = o->p[2] + nz * r;
+                const float vn = *vx * nx + *vy * ny + *vz * nz;
+                if (vn < 0) {
+                    *vx -= (1 + o->p[4]) * vn * nx;
+                    *vy -= (1 + o->p[4]) * vn * ny;
+                    *vz -= (1 + o->p[4]) * vn * nz;
+                }
+            }
+            break;
+        }
+        case 6: {
+            const float e = o->p[6];
+            if (*x < o->p[0]) { *x = o->p[0]; *vx = fabsf(*vx) * e; }
+            if (*x > o->p[3]) { *x = o->p[3]; *vx = -fabsf(*vx) * e; }
+            if (*y < o->p[1]) { *y = o->p[1]; *vy = fabsf(*vy) * e; }
+            if (*y > o->p[4]) { *y = o->p[4]; *vy = -fabsf(*vy) * e; }
+            if (*z < o->p[2]) { *z = o->p[2]; *vz = fabsf(*vz) * e; }
+            if (*z > o->p[5]) { *z = o->p[5]; *vz = -fabsf(*vz) * e; }
+            break;
+        }
+        default:
+            break;
+    }
+}
+
 /* manifest_runner.rs:371-541: SphFused -> Gravity (gravity.rs:31-34) ->
  * Integrate (integrate.rs:16-31) -> BoxCollider (box_collider.rs:26-47). */
 void orc_step(const orc_sph_params* p, const orc_step_params* sp, float* px, float* py, float* pz, float* vx,
@@ -472,6 +538,9 @@ void orc_step(const orc_sph_params* p, const orc_step_params* sp, float* px, flo
     for (uint64_t i = 0; i < n; ++i) {
         float x = px[i], y = py[i], z = pz[i];
         float u = nvx[i], v = nvy[i], w = nvz[i];
+        if (sp->n_ops) {
+            for (uint32_t k = 0; k < sp->n_ops; ++k) orc_apply_op(&sp->ops[k], dt, &x, &y, &z, &u, &v, &w);
+        } else {
         if (sp->flags & 1u) {
             u += sp->gravity[0] * dt;
             v += sp->gravity[1] * dt;
@@ -492,6 +561,7 @@ void orc_step(const orc_sph_params* p, const orc_step_params* sp, float* px, flo
             if (y > sp->box_max[1]) { y = sp->box_max[1]; v = -fabsf(v) * e; }
             if (z < sp->box_min[2]) { z = sp->box_min[2]; w = fabsf(w) * e; }
             if (z > sp->box_max[2]) { z = sp->box_max[2]; w = -fabsf(w) * e; }
+        }
         }
         px[i] = x; py[i] = y; pz[i] = z;
         vx[i] = u; vy[i] = v; vz[i] = w;

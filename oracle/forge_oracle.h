@@ -68,12 +68,19 @@ typedef struct orc_sph_params {
     float h, mass, gas_constant, rest_density, viscosity;
 } orc_sph_params;
 
+typedef struct orc_step_op {
+    uint32_t kind; /* 1 gravity, 2 drag, 3 integrate, 4 ground, 5 sphere, 6 box */
+    float p[7];
+} orc_step_op;
+
 typedef struct orc_step_params {
     float dt;
     float gravity[3];
     float box_min[3], box_max[3];
     float restitution;
-    uint32_t flags; /* 1 gravity, 2 integrate, 4 box */
+    uint32_t flags; /* 1 gravity, 2 integrate, 4 box (when n_ops == 0) */
+    uint32_t n_ops; /* > 0: apply ops[] in order instead */
+    orc_step_op ops[8];
 } orc_step_params;
 
 /* sph_density kernel, sph_density.rs:401-461. threads > 1 uses OpenMP over

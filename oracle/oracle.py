@@ -24,9 +24,14 @@ class SphParams(ctypes.Structure):
                 ("rest_density", ctypes.c_float), ("viscosity", ctypes.c_float)]
 
 
+class StepOp(ctypes.Structure):
+    _fields_ = [("kind", ctypes.c_uint32), ("p", ctypes.c_float * 7)]
+
+
 class StepParams(ctypes.Structure):
     _fields_ = [("dt", ctypes.c_float), ("gravity", ctypes.c_float * 3), ("box_min", ctypes.c_float * 3),
-                ("box_max", ctypes.c_float * 3), ("restitution", ctypes.c_float), ("flags", ctypes.c_uint32)]
+                ("box_max", ctypes.c_float * 3), ("restitution", ctypes.c_float), ("flags", ctypes.c_uint32),
+                ("n_ops", ctypes.c_uint32), ("ops", StepOp * 8)]
 
 
 def build() -> None:

@@ -42,20 +42,29 @@ def test_pipeline_fused_plan():
     p = forge_sph.Pipeline()
     p.add(forge_sph.SphFusedModule(0.025, 0.025, (40, 40, 40), 1.0, 3.0, 1000.0, 0.1))
     p.add(forge_sph.GravityModule(0.0, -9.81, 0.0))
+    p.add(forge_sph.DragModule(0.5))
     p.add(forge_sph.IntegrateModule())
+    p.add(forge_sph.GroundPlaneModule(0.1, 0.3))
+    p.add(forge_sph.SphereColliderModule(0.5, 0.5, 0.5, 0.2, 0.4))
     p.add(forge_sph.BoxColliderModule(0, 0, 0, 1, 1, 1, 0.5))
     sp = p._fused_plan()
-    assert sp is not None and sp.flags == 7
-    assert list(sp.gravity) == pytest.approx([0.0, -9.81, 0.0])
-    assert sp.restitution == pytest.approx(0.5)
+    assert sp is not None and sp.n_ops == 6
+    assert [sp.ops[k].kind for k in range(6)] == [forge_sph.OP_GRAVITY, forge_sph.OP_DRAG, forge_sph.OP_INTEGRATE,
+                                                  forge_sph.OP_GROUND, forge_sph.OP_SPHERE, forge_sph.OP_BOX]
+    assert list(sp.ops[0].p)[:3] == pytest.approx([0.0, -9.81, 0.0])
+    assert sp.ops[5].p[6] == pytest.approx(0.5)
     q = forge_sph.Pipeline()
     q.add(forge_sph.GravityModule())
-    assert q._fused_plan() is None
+    assert q._fused_plan() is None  # no SPH module first
     r = forge_sph.Pipeline()
     r.add(forge_sph.SphFusedModule(0.025, 0.025, (40, 40, 40), 1.0, 3.0, 1000.0, 0.1))
-    r.add(forge_sph.IntegrateModule())
-    r.add(forge_sph.GravityModule())  # gravity after integrate: not the fusable order
-    assert r._fused_plan() is None
+    r.add(forge_sph.SphDensityModule(0.025, 0.025, (40, 40, 40), 1.0))
+    assert r._fused_plan() is None  # a neighbour pass after it is not an epilogue op
+
+
+def test_step_params_layout_matches_header():
+    # dt, g[3], box min/max, restitution, flags, n_ops, 8 x (kind + 7 floats)
+    assert ctypes.sizeof(forge_sph.StepParams) == 4 * (1 + 3 + 3 + 3 + 1 + 1 + 1 + 8 * 8)
 
 
 def test_no_gpu_fails_loudly():

@@ -277,3 +277,48 @@ def test_step_is_capture_safe_in_a_cuda_graph(cuda):
     g.check()
     for x, y in zip([host_f32(t) for t in p + v], eager[0] + eager[1]):
         assert np.array_equal(x, y)
+
+
+def _all_ops_modules(cfg):
+    return [forge_sph.SphFusedModule(cfg.h, cfg.cell_size, cfg.dims, cfg.mass, cfg.gas_constant, cfg.rest_density,
+                                     cfg.viscosity),
+            forge_sph.GravityModule(0.0, -9.81, 0.0), forge_sph.DragModule(2.0), forge_sph.IntegrateModule(),
+            forge_sph.GroundPlaneModule(0.05, 0.3), forge_sph.SphereColliderModule(0.5, 0.4, 0.5, 0.15, 0.6),
+            forge_sph.BoxColliderModule(0, 0, 0, 1, 1, 1, 0.8)]
+
+
+def test_fused_epilogue_ops_vs_oracle(cuda):
+    """SphFused + gravity, drag, integrate, ground plane, sphere and box
+    colliders (the waterfall / tsunami module mix) as one fused step, against
+    the oracle applying the same modules in order."""
+    cfg = workloads.config("ref65k")
+    cfg.dt = 2e-3  # large enough that the ground and the sphere are hit
+    pos, vel = workloads.uniform_particles(cfg.n, seed=91, vsigma=0.5)
+    pipe = forge_sph.Pipeline()
+    for m in _all_ops_modules(cfg):
+        pipe.add(m)
+    sp = pipe._fused_plan()
+    assert sp is not None and sp.n_ops == 6
+    f = forge_sph.FieldSet(cfg.n, 0)
+    for a, x in zip("xyz", pos):
+        f.add_f32("pos_" + a, x)
+    for a, x in zip("xyz", vel):
+        f.add_f32("vel_" + a, x)
+    pipe.step(f, cfg.dt)
+    osp = oracle.StepParams()
+    osp.dt = cfg.dt
+    osp.n_ops = sp.n_ops
+    for k in range(sp.n_ops):
+        osp.ops[k].kind = sp.ops[k].kind
+        for q in range(7):
+            osp.ops[k].p[q] = sp.ops[k].p[q]
+    po, vo = [x.copy() for x in pos], [x.copy() for x in vel]
+    oracle.step(oparams(cfg), osp, po, vo, cfg.cell_size, cfg.dims, threads=oracle.max_threads())
+    inside = 0
+    for k, a in enumerate("xyz"):
+        gp, gv = host_f32(f.f32_fields["pos_" + a]), host_f32(f.f32_fields["vel_" + a])
+        np.testing.assert_allclose(gp, po[k], rtol=0, atol=2e-6)
+        np.testing.assert_allclose(gv, vo[k], rtol=1e-4, atol=2e-5)
+    d = np.sqrt((po[0] - 0.5) ** 2 + (po[1] - 0.4) ** 2 + (po[2] - 0.5) ** 2)
+    assert (np.abs(d - 0.15) < 1e-5).sum() > 0, "no particle was pushed onto the sphere"
+    assert (po[1] == np.float32(0.05)).sum() > 0, "no particle hit the ground plane"
