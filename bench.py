@@ -111,6 +111,13 @@ def kernels_per_step(cfg):
     return 1 + (cfg.key_bits + 7) // 8 + 3  # histogram, passes, cell table, density, force
 
 
+def sharded_kernels_per_step(cfg):
+    """Our kernels per step on a rank with two neighbours: grid build, density,
+    2 density packs, gather, 2 force zones, 2 classifications (3 kernels
+    each), 4 packs, counts message, compaction, 2 halo remaps, 6 unpacks."""
+    return kernels_per_step(cfg) + 2 + 1 + 1 + 6 + 4 + 1 + 1 + 2 + 6
+
+
 def sph_params(forge_sph, cfg):
     return forge_sph.SphParams(cfg.h, cfg.mass, cfg.gas_constant, cfg.rest_density, cfg.viscosity)
 
@@ -327,6 +334,7 @@ def run_sharded(args, torch, dist, rank, world, local):
     halo = max_over_ranks(torch, dist, float(run.last_halo))
     # phase breakdown on a few extra (untimed) steps
     run.timing = []
+    run.timing_side = []
     for _ in range(3):
         run.step()
     torch.cuda.synchronize()
@@ -335,8 +343,12 @@ def run_sharded(args, torch, dist, rank, world, local):
     for (a, ea), (b, eb) in zip(ev[:-1], ev[1:]):
         if b != "start":
             phase_ms[b] = phase_ms.get(b, 0.0) + ea.elapsed_time(eb) / 3
+    side_ms = {}  # overlapped exchange: side-stream progress after the density round
+    for name, e, ref in run.timing_side:
+        side_ms[name] = side_ms.get(name, 0.0) + ref.elapsed_time(e) / 3
     run.timing = None
     phase_ms = {k: max_over_ranks(torch, dist, v) for k, v in sorted(phase_ms.items())}
+    side_ms = {k: max_over_ranks(torch, dist, v) for k, v in sorted(side_ms.items())}
 
     # e2e: the same sharded step with the rank's particle state read from and
     # written back to pinned host memory every step.
@@ -381,9 +393,10 @@ def run_sharded(args, torch, dist, rank, world, local):
                            "inputs_exceed_l2": True, "parallelism": f"x-slab over {world} GPUs (NCCL send/recv, exchange={args.comm})",
                            "max_halo_particles_per_rank": halo},
                 "phases_ms_max_over_ranks": phase_ms,
+                "overlap_ms_after_ghost_rho_max_over_ranks": side_ms,
                 "e2e": {"value": cfg.n * e2e_steps / (e2e_ms / 1e3), "unit": "particle-steps/s",
                         "h2d_bytes_per_step": tot_bytes, "d2h_bytes_per_step": tot_bytes},
-                "gpu_launches": (kernels_per_step(cfg) + 1) * args.steps * world,
+                "gpu_launches": sharded_kernels_per_step(cfg) * args.steps * world,
                 "clocks": clk}
         print(json.dumps(line), flush=True)
 

@@ -10,6 +10,7 @@ namespace forge {
 constexpr uint32_t kDevTimeout = 0x1u;
 constexpr uint32_t kDevKeyRange = 0x2u;
 constexpr uint32_t kDevCapacity = 0x4u;
+constexpr uint32_t kDevZone = 0x8u;  // an interior particle of a zoned force pass entered the boundary zone
 
 // Upper bound on polls of one look-back status word before a wait gives up
 // and reports kDevTimeout (~0.3 s with the back-off below). A predecessor

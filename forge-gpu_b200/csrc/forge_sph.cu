@@ -2,6 +2,7 @@
 // reporting around the sm_100a kernels in radix_sort.cuh, grid.cuh, sph.cuh.
 // Single translation unit -> libforge_sph.so.
 #include <algorithm>
+#include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -393,6 +394,12 @@ struct forge_grid {
     uint32_t* sorted_idx = nullptr;
     uint64_t n = 0;
     bool built = false;
+    bool force_gathered = false;  // a zone-1 force pass gathered velocities + density of this build
+    // Zone lists of a zoned force pass (allocated by the first one).
+    uint32_t* zone_idx = nullptr;     // [A (empty) | boundary | interior] sorted positions, max_n
+    uint32_t* zone_tiles = nullptr;   // classification tile counts
+    uint32_t* zone_counts = nullptr;  // list sizes A (0), boundary, interior
+    cudaEvent_t ev_zone = nullptr;  // gather + zone lists of the last boundary pass done
     // Phase-event ring for forge_grid_profile_* (5 events per step).
     std::vector<cudaEvent_t> prof_events;
     uint32_t prof_cap = 0, prof_next = 0, prof_count = 0;
@@ -475,6 +482,10 @@ extern "C" void forge_grid_destroy(forge_grid* g) {
     cudaFree(g->aux);
     cudaFree(g->scan_sums);
     cudaFree(g->q_offsets);
+    cudaFree(g->zone_idx);
+    cudaFree(g->zone_tiles);
+    cudaFree(g->zone_counts);
+    if (g->ev_zone) cudaEventDestroy(g->ev_zone);
     scratch_free(g->scratch);
     prof_free(g);
     delete g;
@@ -516,6 +527,7 @@ int grid_build_impl(forge_grid* g, const float* px, const float* py, const float
     prof_mark(g, 2, st);
     g->n = n;
     g->built = true;
+    g->force_gathered = false;
     g->sub_bits = sub_bits;
     return FORGE_OK;
 }
@@ -576,11 +588,68 @@ template <int TERMS, int EPI>
 void launch_force_t(forge_grid* g, const sph::SphConsts& c, const sph::StepEpi& ep, const sph::ForceOut& o,
                     cudaStream_t st) {
     if ((double)g->n / (double)g->C < kPairMaxOccupancy)
-        sph::force_kernel<TERMS, EPI><<<grid_blocks((g->n + 1) / 2, kSphThreads), kSphThreads, 0, st>>>(
-            g->pos4, g->vel4, g->aux, g->cell_start, g->sorted_idx, (uint32_t)g->n, geom_of(g, c.h), c, ep, o);
+        sph::force_kernel<TERMS, EPI, false><<<grid_blocks((g->n + 1) / 2, kSphThreads), kSphThreads, 0, st>>>(
+            g->pos4, g->vel4, g->aux, g->cell_start, g->sorted_idx, (uint32_t)g->n, geom_of(g, c.h), c, ep, o, {});
     else
-        sph::force_single_kernel<TERMS, EPI><<<grid_blocks(g->n, kSphThreads), kSphThreads, 0, st>>>(
-            g->pos4, g->vel4, g->aux, g->cell_start, g->sorted_idx, (uint32_t)g->n, geom_of(g, c.h), c, ep, o);
+        sph::force_single_kernel<TERMS, EPI, false><<<grid_blocks(g->n, kSphThreads), kSphThreads, 0, st>>>(
+            g->pos4, g->vel4, g->aux, g->cell_start, g->sorted_idx, (uint32_t)g->n, geom_of(g, c.h), c, ep, o, {});
+}
+
+// One zone of a zoned force step: the same kernels over a zone list. The
+// list size is known only on the device, so the grid covers n (blocks past
+// the list leave at once); short-lived blocks leave room for concurrent
+// work (the other zone, the exchange kernels, NCCL).
+int launch_force_zone(forge_grid* g, const sph::SphConsts& c, const sph::StepEpi& ep, const sph::ForceOut& o,
+                      uint32_t list, cudaStream_t st) {
+    const sph::ZoneList zl{g->zone_idx, g->zone_counts, list};
+    if ((double)g->n / (double)g->C < kPairMaxOccupancy)
+        sph::force_kernel<3, 1, true><<<grid_blocks((g->n + 1) / 2, kSphThreads), kSphThreads, 0, st>>>(
+            g->pos4, g->vel4, g->aux, g->cell_start, g->sorted_idx, (uint32_t)g->n, geom_of(g, c.h), c, ep, o, zl);
+    else
+        sph::force_single_kernel<3, 1, true><<<grid_blocks(g->n, kSphThreads), kSphThreads, 0, st>>>(
+            g->pos4, g->vel4, g->aux, g->cell_start, g->sorted_idx, (uint32_t)g->n, geom_of(g, c.h), c, ep, o, zl);
+    FORGE_LAUNCHED();
+    return FORGE_OK;
+}
+
+// First zoned pass on a grid: zone lists and their event.
+int zone_setup(forge_grid* g) {
+    if (g->zone_idx) return FORGE_OK;
+    const uint64_t rows = (uint64_t)g->geom.ny * g->geom.nz;
+    const uint64_t tiles = (rows + sph::kZoneRows - 1) / sph::kZoneRows;
+    FORGE_CUDA(dalloc(&g->zone_idx, std::max<uint64_t>(g->max_n, 1)));
+    FORGE_CUDA(dalloc(&g->zone_tiles, std::max<uint64_t>(tiles, 1) * slab::kLists));
+    FORGE_CUDA(dalloc(&g->zone_counts, slab::kLists));
+    FORGE_CUDA(cudaEventCreateWithFlags(&g->ev_zone, cudaEventDisableTiming));
+    return FORGE_OK;
+}
+
+// Splits the built grid's particles into the boundary and interior zone
+// lists by x-slice: interior = slices whose x-extent lies inside
+// [inner_lo, inner_hi). Ghosts fall in the boundary list (skipped there).
+int zone_classify(forge_grid* g, float inner_lo, float inner_hi, cudaStream_t st) {
+    const grid::GridGeom& G = g->geom;
+    const uint32_t row_len = (uint32_t)G.nx << g->sub_bits;
+    const double w = (double)G.cs / (double)(1u << g->sub_bits);  // slice width
+    auto edge = [&](float x, bool up) -> uint32_t {
+        if (std::isinf(x)) return x < 0 ? 0u : row_len;
+        if (!(x == x)) return 0u;
+        const double f = ((double)x - (double)G.ox) / w;
+        const double e = up ? std::ceil(f) : std::floor(f);
+        return (uint32_t)std::min<double>(std::max<double>(e, 0.0), (double)row_len);
+    };
+    // interior slices [k_lo, k_hi): lower edge >= inner_lo, upper edge <=
+    // inner_hi (a particle hashed into a slice by a rounded divide may sit a
+    // few ulps outside it; the guard check of the interior pass sees that)
+    const uint32_t k_lo = edge(inner_lo, true);
+    const uint32_t k_hi = std::max(k_lo, edge(inner_hi, false));
+    const sph::ZoneRows z{g->cell_start, (uint32_t)G.ny * (uint32_t)G.nz, row_len, k_lo, k_hi};
+    const uint32_t tiles = grid_blocks(z.rows, sph::kZoneRows);
+    sph::zone_rows_count_kernel<<<tiles, sph::kZoneRows, 0, st>>>(z, g->zone_tiles);
+    slab::classify_scan_kernel<<<1, 1024, 0, st>>>(g->zone_tiles, tiles, g->zone_counts);
+    sph::zone_rows_write_kernel<<<tiles, sph::kZoneRows, 0, st>>>(z, g->zone_tiles, g->zone_counts, g->zone_idx);
+    FORGE_LAUNCHED();
+    return FORGE_OK;
 }
 
 }  // namespace
@@ -723,29 +792,74 @@ sph::StepEpi epi_of(const forge_step_params* sp) {
 }
 }  // namespace
 
+namespace {
+
+int force_step_impl(const char* fn, forge_grid* g, const forge_sph_params* p, const forge_step_params* sp, float* px,
+                    float* py, float* pz, float* vx, float* vy, float* vz, const float* density, uint64_t n,
+                    uint64_t n_update, const forge_force_zone* zone, cudaStream_t st) {
+    if (!g || !p || !sp) return set_error(FORGE_ERR_INVALID_ARG, "%s: NULL grid or params", fn);
+    if (sp->n_ops > FORGE_STEP_MAX_OPS) return set_error(FORGE_ERR_INVALID_ARG, "%s: n_ops > 8", fn);
+    if (!g->built || g->n != n)
+        return set_error(FORGE_ERR_INVALID_ARG, "%s: the grid was not built for these %llu particles (last build: %llu)",
+                         fn, (unsigned long long)n, (unsigned long long)g->n);
+    if (n_update > n) return set_error(FORGE_ERR_INVALID_ARG, "%s: n_update > n", fn);
+    const uint32_t mode = zone ? zone->mode : 0u;
+    if (mode > FORGE_ZONE_INTERIOR) return set_error(FORGE_ERR_INVALID_ARG, "%s: bad zone mode %u", fn, mode);
+    if (mode == FORGE_ZONE_INTERIOR && !g->force_gathered)
+        return set_error(FORGE_ERR_INVALID_ARG, "%s: an interior pass must follow a boundary pass of the same build",
+                         fn);
+    if (n == 0) return FORGE_OK;
+    if (!px || !py || !pz || !vx || !vy || !vz || !density)
+        return set_error(FORGE_ERR_INVALID_ARG, "%s: NULL array", fn);
+    FORGE_DEVICE_SCOPE(g->device);
+    const sph::SphConsts c = make_consts(p);
+    // The interior pass reuses the boundary pass's cell-ordered velocities:
+    // the boundary particles' velocities have been updated in place since.
+    if (mode != FORGE_ZONE_INTERIOR) {
+        sph::gather_vel_rho_kernel<<<grid_blocks(n, 256), 256, 0, st>>>(g->sorted_idx, (uint32_t)n, vx, vy, vz,
+                                                                        density, c, g->vel4, g->aux);
+        FORGE_LAUNCHED();
+    }
+    g->force_gathered = mode == FORGE_ZONE_BOUNDARY;
+    sph::ForceOut o{vx, vy, vz, nullptr, nullptr, nullptr, px, py, pz, (uint32_t)n_update};
+    if (!mode) {
+        launch_force_t<3, 1>(g, c, epi_of(sp), o, st);
+        FORGE_LAUNCHED();
+        return FORGE_OK;
+    }
+    int rc;
+    if (mode == FORGE_ZONE_BOUNDARY) {
+        if ((rc = zone_setup(g)) != FORGE_OK) return rc;
+        if ((rc = zone_classify(g, zone->inner_lo, zone->inner_hi, st)) != FORGE_OK) return rc;
+        FORGE_CUDA(cudaEventRecord(g->ev_zone, st));
+    } else {
+        // the interior pass needs the gather and the lists, not the boundary
+        // kernel: on another stream the two passes run concurrently
+        FORGE_CUDA(cudaStreamWaitEvent(st, g->ev_zone, 0));
+    }
+    o.zone = mode;
+    o.glo = zone->guard_lo;
+    o.ghi = zone->guard_hi;
+    o.status = g->scratch.meta + kMetaErr;
+    return launch_force_zone(g, c, epi_of(sp), o, mode, st);
+}
+
+}  // namespace
+
 extern "C" int forge_sph_force_step(forge_grid* g, const forge_sph_params* p, const forge_step_params* sp,
                                     float* px, float* py, float* pz, float* vx, float* vy, float* vz,
                                     const float* density, uint64_t n, uint64_t n_update, void* stream) {
-    if (!g || !p || !sp) return set_error(FORGE_ERR_INVALID_ARG, "forge_sph_force_step: NULL grid or params");
-    if (sp->n_ops > FORGE_STEP_MAX_OPS) return set_error(FORGE_ERR_INVALID_ARG, "forge_sph_force_step: n_ops > 8");
-    if (!g->built || g->n != n)
-        return set_error(FORGE_ERR_INVALID_ARG,
-                         "forge_sph_force_step: the grid was not built for these %llu particles (last build: %llu)",
-                         (unsigned long long)n, (unsigned long long)g->n);
-    if (n_update > n) return set_error(FORGE_ERR_INVALID_ARG, "forge_sph_force_step: n_update > n");
-    if (n == 0) return FORGE_OK;
-    if (!px || !py || !pz || !vx || !vy || !vz || !density)
-        return set_error(FORGE_ERR_INVALID_ARG, "forge_sph_force_step: NULL array");
-    FORGE_DEVICE_SCOPE(g->device);
-    cudaStream_t st = as_stream(stream);
-    const sph::SphConsts c = make_consts(p);
-    sph::gather_vel_rho_kernel<<<grid_blocks(n, 256), 256, 0, st>>>(g->sorted_idx, (uint32_t)n, vx, vy, vz, density,
-                                                                    c, g->vel4, g->aux);
-    FORGE_LAUNCHED();
-    sph::ForceOut o{vx, vy, vz, nullptr, nullptr, nullptr, px, py, pz, (uint32_t)n_update};
-    launch_force_t<3, 1>(g, c, epi_of(sp), o, st);
-    FORGE_LAUNCHED();
-    return FORGE_OK;
+    return force_step_impl("forge_sph_force_step", g, p, sp, px, py, pz, vx, vy, vz, density, n, n_update, nullptr,
+                           as_stream(stream));
+}
+
+extern "C" int forge_sph_force_step_zone(forge_grid* g, const forge_sph_params* p, const forge_step_params* sp,
+                                         float* px, float* py, float* pz, float* vx, float* vy, float* vz,
+                                         const float* density, uint64_t n, uint64_t n_update,
+                                         const forge_force_zone* zone, void* stream) {
+    if (!zone) return set_error(FORGE_ERR_INVALID_ARG, "forge_sph_force_step_zone: zone is NULL");
+    return force_step_impl("forge_sph_force_step_zone", g, p, sp, px, py, pz, vx, vy, vz, density, n, n_update, zone,
+                           as_stream(stream));
 }
 
 extern "C" int forge_sph_step(forge_grid* g, const forge_sph_params* p, const forge_step_params* sp, float* px,
@@ -850,9 +964,11 @@ extern "C" int forge_slab_classify(forge_slab* h, const float* x, uint64_t n, fl
     }
     const slab::ClassifyArgs a{lo, hi, reach, flags};
     const uint32_t tiles = grid_blocks(n, slab::kTile);
-    slab::classify_count_kernel<<<tiles, slab::kThreads, 0, st>>>(x, (uint32_t)n, nullptr, a, h->tile_counts);
+    slab::classify_count_kernel<<<tiles, slab::kThreads, 0, st>>>(slab::XMember{x, a}, (uint32_t)n,
+                                                                  nullptr, h->tile_counts);
     slab::classify_scan_kernel<<<1, 1024, 0, st>>>(h->tile_counts, tiles, counts);
-    slab::classify_write_kernel<<<tiles, slab::kThreads, 0, st>>>(x, (uint32_t)n, nullptr, a, h->tile_counts,
+    slab::classify_write_kernel<<<tiles, slab::kThreads, 0, st>>>(slab::XMember{x, a}, (uint32_t)n,
+                                                                  nullptr, h->tile_counts,
                                                                   counts, idx_out);
     FORGE_LAUNCHED();
     return FORGE_OK;

@@ -17,22 +17,30 @@ constexpr int kLists = 3;  // A (either side), L (left), R (right)
 
 struct ClassifyArgs {
     float lo, hi, reach;
-    uint32_t flags;  // 1 has left neighbour, 2 has right neighbour, 4 halo mode (else migrate mode)
+    uint32_t flags;  // 1 has left neighbour, 2 has right neighbour, 4 halo mode (else migrate mode),
+                     // 8 (halo mode) in-slab rows only: lo <= x on the left, x < hi on the right
 };
 
 // Membership bits of element x in lists A, L, R.
 __device__ __forceinline__ uint32_t member_bits(float x, const ClassifyArgs& a) {
-    const bool halo = a.flags & 4u;
-    const bool l = (a.flags & 1u) && (halo ? x < a.lo + a.reach : x < a.lo);
-    const bool r = (a.flags & 2u) && (halo ? x >= a.hi - a.reach : x >= a.hi);
+    const bool halo = a.flags & 4u, in_slab = a.flags & 8u;
+    const bool l = (a.flags & 1u) && (halo ? x < a.lo + a.reach && (!in_slab || x >= a.lo) : x < a.lo);
+    const bool r = (a.flags & 2u) && (halo ? x >= a.hi - a.reach && (!in_slab || x < a.hi) : x >= a.hi);
     const bool all = !halo && (l || r);
     return (all ? 1u : 0u) | (l ? 2u : 0u) | (r ? 4u : 0u);
 }
 
+// Membership of element i by its x coordinate (the slab lists).
+struct XMember {
+    const float* __restrict__ x;
+    ClassifyArgs a;
+    __device__ __forceinline__ uint32_t operator()(uint32_t i) const { return member_bits(x[i], a); }
+};
+
 // Pass 1: per-tile counts of each list.
+template <class M>
 __global__ void __launch_bounds__(kThreads)
-    classify_count_kernel(const float* __restrict__ x, uint32_t n, const uint32_t* __restrict__ n_sub, ClassifyArgs a,
-                          uint32_t* __restrict__ tile_counts) {
+    classify_count_kernel(M m, uint32_t n, const uint32_t* __restrict__ n_sub, uint32_t* __restrict__ tile_counts) {
     __shared__ uint32_t s[kLists];
     if (n_sub) n -= *n_sub;  // live length known only on the device
     if (threadIdx.x < kLists) s[threadIdx.x] = 0;
@@ -43,7 +51,7 @@ __global__ void __launch_bounds__(kThreads)
     for (int k = 0; k < kItems; ++k) {
         const uint32_t i = base + k * kThreads + threadIdx.x;
         if (i < n) {
-            const uint32_t b = member_bits(x[i], a);
+            const uint32_t b = m(i);
 #pragma unroll
             for (int l = 0; l < kLists; ++l) c[l] += (b >> l) & 1u;
         }
@@ -83,8 +91,9 @@ __global__ void __launch_bounds__(1024)
 
 // Pass 3: write each list's element indices in ascending order, packed as
 // [A | L | R].
+template <class M>
 __global__ void __launch_bounds__(kThreads)
-    classify_write_kernel(const float* __restrict__ x, uint32_t n, const uint32_t* __restrict__ n_sub, ClassifyArgs a,
+    classify_write_kernel(M m, uint32_t n, const uint32_t* __restrict__ n_sub,
                           const uint32_t* __restrict__ tile_offsets, const uint32_t* __restrict__ counts,
                           uint32_t* __restrict__ out) {
     __shared__ uint32_t s_scan[kThreads / 32 + 1];
@@ -95,7 +104,7 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
     for (int k = 0; k < kItems; ++k) {
         const uint32_t i = base + k;
-        bits[k] = i < n ? member_bits(x[i], a) : 0u;
+        bits[k] = i < n ? m(i) : 0u;
 #pragma unroll
         for (int l = 0; l < kLists; ++l) c[l] += (bits[k] >> l) & 1u;
     }
@@ -205,6 +214,31 @@ __global__ void __launch_bounds__(256)
     }
 }
 
+// Column indices taken before compact_kernel(gone, k) -> after it: an index
+// t >= keep = n - k (t not in gone) is the r-th surviving tail column, r =
+// (t - keep) - |gone in [keep, t)|, and moved to the r-th hole gone[r].
+// k is read from *k_dev; cnt from *cnt_dev when set.
+__global__ void __launch_bounds__(256)
+    remap_after_compact_kernel(uint32_t* __restrict__ idx, uint32_t cnt, const uint32_t* __restrict__ cnt_dev,
+                               uint32_t n, const uint32_t* __restrict__ gone, const uint32_t* __restrict__ k_dev) {
+    if (cnt_dev) cnt = *cnt_dev;
+    const uint32_t k = *k_dev, keep = n - k;
+    auto lower = [&](uint32_t v) {  // |{gone[j] < v}|
+        uint32_t lo = 0, hi = k;
+        while (lo < hi) {
+            const uint32_t mid = (lo + hi) >> 1;
+            if (gone[mid] < v) lo = mid + 1;
+            else hi = mid;
+        }
+        return lo;
+    };
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < cnt; i += gridDim.x * blockDim.x) {
+        const uint32_t t = idx[i];
+        if (t < keep) continue;
+        idx[i] = gone[(t - keep) - (lower(t) - lower(keep))];
+    }
+}
+
 // The counts message and bookkeeping from the two classifications:
 // mig = [A, L, R], halo = [0, L, R] -> msg[0..3] = mL, hL, mR, hR; msg[8] = A.
 __global__ void counts_msg_kernel(const uint32_t* __restrict__ mig, const uint32_t* __restrict__ halo,
@@ -214,6 +248,154 @@ __global__ void counts_msg_kernel(const uint32_t* __restrict__ mig, const uint32
     msg[2] = mig[2];
     msg[3] = halo[2];
     msg[8] = mig[0];
+}
+
+}  // namespace slab
+}  // namespace forge
+
+namespace forge {
+namespace slab {
+
+// One-pass selection of round 1 of the overlapped exchange: for each owned
+// particle, membership in five lists -- migrants A (either side), ML, MR and
+// in-slab halo rows HL, HR -- counted, scanned and written (with the records
+// packed straight into the two send buffers) by three kernels.
+constexpr int kXLists = 5;  // A, ML, MR, HL, HR
+
+__device__ __forceinline__ uint32_t xchg_bits(float x, float lo, float hi, float reach, uint32_t sides) {
+    const bool hasl = sides & 1u, hasr = sides & 2u;
+    const bool ml = hasl && x < lo, mr = hasr && x >= hi;
+    const bool hl = hasl && x >= lo && x < lo + reach;
+    const bool hr = hasr && x < hi && x >= hi - reach;
+    return ((ml || mr) ? 1u : 0u) | (ml ? 2u : 0u) | (mr ? 4u : 0u) | (hl ? 8u : 0u) | (hr ? 16u : 0u);
+}
+
+struct XchgArgs {
+    const float* cols;  // rows x, y, z, vx, vy, vz, id; row stride ld
+    uint64_t ld;
+    uint32_t n;
+    float lo, hi, reach;
+    uint32_t sides;
+};
+
+__global__ void __launch_bounds__(kThreads) xchg_count_kernel(XchgArgs a, uint32_t* __restrict__ tile_counts) {
+    __shared__ uint32_t s[kXLists];
+    if (threadIdx.x < kXLists) s[threadIdx.x] = 0;
+    __syncthreads();
+    uint32_t c[kXLists] = {0, 0, 0, 0, 0};
+    const uint32_t base = blockIdx.x * kTile;
+#pragma unroll
+    for (int k = 0; k < kItems; ++k) {
+        const uint32_t i = base + k * kThreads + threadIdx.x;
+        if (i < a.n) {
+            const uint32_t b = xchg_bits(a.cols[i], a.lo, a.hi, a.reach, a.sides);
+#pragma unroll
+            for (int l = 0; l < kXLists; ++l) c[l] += (b >> l) & 1u;
+        }
+    }
+#pragma unroll
+    for (int l = 0; l < kXLists; ++l) {
+        uint32_t v = c[l];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if ((threadIdx.x & 31) == 0 && v) atomicAdd(&s[l], v);
+    }
+    __syncthreads();
+    if (threadIdx.x < kXLists) tile_counts[blockIdx.x * kXLists + threadIdx.x] = s[threadIdx.x];
+}
+
+// One block: tile offsets per list, totals to counts[0..3) = A, ML, MR and
+// counts[4], counts[5] = HL, HR (counts[3] = 0: the layout of the two-pass
+// exchange), and the counts message msg[0..3] = ML, HL, MR, HR, msg[8] = A,
+// msg[4..8) (the neighbours' counts, received later) = 0.
+__global__ void __launch_bounds__(1024)
+    xchg_scan_kernel(uint32_t* __restrict__ tile_counts, uint32_t tiles, uint32_t* __restrict__ counts,
+                     uint64_t* __restrict__ msg) {
+    __shared__ uint32_t s_scan[1024 / 32 + 1];
+    __shared__ uint32_t s_tot[kXLists];
+    for (int l = 0; l < kXLists; ++l) {
+        uint32_t carry = 0;
+        for (uint32_t b = 0; b < tiles; b += 1024) {
+            const uint32_t t = b + threadIdx.x;
+            const uint32_t v = t < tiles ? tile_counts[t * kXLists + l] : 0u;
+            uint32_t total;
+            const uint32_t ex = block_exclusive_scan<1024>(v, s_scan, &total);
+            if (t < tiles) tile_counts[t * kXLists + l] = carry + ex;
+            carry += total;
+        }
+        if (threadIdx.x == 0) s_tot[l] = carry;
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        counts[0] = s_tot[0];
+        counts[1] = s_tot[1];
+        counts[2] = s_tot[2];
+        counts[3] = 0;
+        counts[4] = s_tot[3];
+        counts[5] = s_tot[4];
+        msg[0] = s_tot[1];
+        msg[1] = s_tot[3];
+        msg[2] = s_tot[2];
+        msg[3] = s_tot[4];
+        msg[4] = msg[5] = msg[6] = msg[7] = 0;
+        msg[8] = s_tot[0];
+    }
+}
+
+struct XchgOut {
+    uint32_t* gone;    // [A | ML | MR]
+    uint32_t* halo_l;  // HL column indices
+    uint32_t* halo_r;
+    float* send_l;     // records: [ML | HL], 7 floats each
+    float* send_r;     // [MR | HR]
+};
+
+__global__ void __launch_bounds__(kThreads)
+    xchg_write_kernel(XchgArgs a, const uint32_t* __restrict__ tile_offsets, const uint32_t* __restrict__ counts,
+                      XchgOut o) {
+    __shared__ uint32_t s_scan[kThreads / 32 + 1];
+    const uint32_t base = blockIdx.x * kTile + threadIdx.x * kItems;  // blocked: 16 consecutive per thread
+    uint32_t bits[kItems];
+    uint32_t c[kXLists] = {0, 0, 0, 0, 0};
+#pragma unroll
+    for (int k = 0; k < kItems; ++k) {
+        const uint32_t i = base + k;
+        bits[k] = i < a.n ? xchg_bits(a.cols[i], a.lo, a.hi, a.reach, a.sides) : 0u;
+#pragma unroll
+        for (int l = 0; l < kXLists; ++l) c[l] += (bits[k] >> l) & 1u;
+    }
+    const uint32_t nA = counts[0], nML = counts[1], nMR = counts[2];
+#pragma unroll
+    for (int l = 0; l < kXLists; ++l) {
+        uint32_t total;
+        uint32_t pos = block_exclusive_scan<kThreads>(c[l], s_scan, &total) + tile_offsets[blockIdx.x * kXLists + l];
+        if (!c[l]) continue;
+#pragma unroll
+        for (int k = 0; k < kItems; ++k) {
+            if (!((bits[k] >> l) & 1u)) continue;
+            const uint32_t i = base + k;
+            float* rec = nullptr;
+            if (l == 0) {
+                o.gone[pos] = i;
+            } else if (l == 1) {
+                o.gone[nA + pos] = i;
+                rec = o.send_l + (size_t)pos * 7;
+            } else if (l == 2) {
+                o.gone[nA + nML + pos] = i;
+                rec = o.send_r + (size_t)pos * 7;
+            } else if (l == 3) {
+                o.halo_l[pos] = i;
+                rec = o.send_l + (size_t)(nML + pos) * 7;
+            } else {
+                o.halo_r[pos] = i;
+                rec = o.send_r + (size_t)(nMR + pos) * 7;
+            }
+            if (rec)
+#pragma unroll
+                for (int r = 0; r < 7; ++r) rec[r] = a.cols[r * a.ld + i];
+            ++pos;
+        }
+    }
 }
 
 }  // namespace slab

@@ -105,6 +105,12 @@ struct forge_slab_comm {
     uint32_t g_hr = 0, n_ghr = 0;         // halo from right
     uint32_t g_ml = 0, g_mr = 0;          // our migrants to left / right
     bool have_round = false;
+    // split round 1 (forge_slab_exchange_begin / _end)
+    uint32_t* xtiles = nullptr;          // tile counts of the one-pass selection
+    cudaStream_t pend_stream = nullptr;  // begin's stream
+    cudaEvent_t ev_counts = nullptr, ev_payload = nullptr;
+    bool pending = false;
+    uint64_t pend_n_own = 0;
 };
 
 namespace {
@@ -115,10 +121,12 @@ void slab_comm_free(forge_slab_comm* c) {
     forge_slab_destroy(c->sel);
     for (void* p : {(void*)c->idx, (void*)c->idx_h, (void*)c->counts, (void*)c->halo_l, (void*)c->halo_r, (void*)c->send_l,
                     (void*)c->send_r, (void*)c->recv_l, (void*)c->recv_r, (void*)c->rho_send_l,
-                    (void*)c->rho_send_r, (void*)c->rho_recv_l, (void*)c->rho_recv_r, (void*)c->dcount})
+                    (void*)c->rho_send_r, (void*)c->rho_recv_l, (void*)c->rho_recv_r, (void*)c->dcount, (void*)c->xtiles})
         cudaFree(p);
     cudaFreeHost(c->hcounts);
     cudaFreeHost(c->hcount);
+    for (cudaEvent_t e : {c->ev_counts, c->ev_payload})
+        if (e) cudaEventDestroy(e);
     delete c;
 }
 
@@ -138,9 +146,11 @@ int classify_async(forge_slab_comm* c, const float* x, uint64_t n, const uint32_
     }
     const slab::ClassifyArgs a{c->lo, c->hi, c->reach, flags};
     const uint32_t tiles = grid_blocks(n, slab::kTile);
-    slab::classify_count_kernel<<<tiles, slab::kThreads, 0, st>>>(x, (uint32_t)n, n_sub, a, c->sel->tile_counts);
+    slab::classify_count_kernel<<<tiles, slab::kThreads, 0, st>>>(slab::XMember{x, a}, (uint32_t)n,
+                                                                  n_sub, c->sel->tile_counts);
     slab::classify_scan_kernel<<<1, 1024, 0, st>>>(c->sel->tile_counts, tiles, counts);
-    slab::classify_write_kernel<<<tiles, slab::kThreads, 0, st>>>(x, (uint32_t)n, n_sub, a, c->sel->tile_counts,
+    slab::classify_write_kernel<<<tiles, slab::kThreads, 0, st>>>(slab::XMember{x, a}, (uint32_t)n,
+                                                                  n_sub, c->sel->tile_counts,
                                                                   counts, idx);
     FORGE_LAUNCHED();
     return FORGE_OK;
@@ -195,8 +205,11 @@ extern "C" int forge_slab_comm_create(const uint8_t* id, int rank, int world, in
               dalloc(&c->rho_send_l, m) == cudaSuccess && dalloc(&c->rho_send_r, m) == cudaSuccess &&
               dalloc(&c->rho_recv_l, m) == cudaSuccess && dalloc(&c->rho_recv_r, m) == cudaSuccess &&
               dalloc(&c->dcount, 9) == cudaSuccess &&
+              dalloc(&c->xtiles, (m + slab::kTile - 1) / slab::kTile * slab::kXLists) == cudaSuccess &&
               cudaMallocHost(&c->hcounts, 3 * sizeof(uint32_t)) == cudaSuccess &&
               cudaMallocHost(&c->hcount, 9 * sizeof(uint64_t)) == cudaSuccess;
+    ok = ok && cudaEventCreateWithFlags(&c->ev_counts, cudaEventDisableTiming) == cudaSuccess &&
+         cudaEventCreateWithFlags(&c->ev_payload, cudaEventDisableTiming) == cudaSuccess;
     if (!ok) {
         slab_comm_free(c);
         return set_error(FORGE_ERR_CUDA, "forge_slab_comm_create: allocation failed (capacity %llu)",
@@ -223,15 +236,119 @@ extern "C" void forge_slab_comm_destroy(forge_slab_comm* c) {
     if (c) slab_comm_free(c);
 }
 
+namespace {
+
+uint32_t slab_sides(const forge_slab_comm* c) { return (c->left >= 0 ? 1u : 0u) | (c->right >= 0 ? 2u : 0u); }
+
+// Sends the counts message of the two classifications (migrant sizes in
+// counts[0..3), halo sizes in counts[3..6)) to the neighbours, receives
+// theirs and copies everything to the pinned host mirror, on `st`.
+int exchange_counts(forge_slab_comm* c, cudaStream_t st, bool make_msg = true) {
+    if (make_msg) {  // else the selection wrote the message (and zeroed the receive words)
+        slab::counts_msg_kernel<<<1, 1, 0, st>>>(c->counts, c->counts + 3, c->dcount);
+        FORGE_LAUNCHED();
+        FORGE_CUDA(cudaMemsetAsync(c->dcount + 4, 0, 4 * sizeof(uint64_t), st));
+    }
+    FORGE_NCCL(g_nccl.GroupStart());
+    if (c->left >= 0) {
+        FORGE_NCCL(g_nccl.Send(c->dcount + 0, 2, ncclUint64, c->left, c->comm, st));
+        FORGE_NCCL(g_nccl.Recv(c->dcount + 4, 2, ncclUint64, c->left, c->comm, st));
+    }
+    if (c->right >= 0) {
+        FORGE_NCCL(g_nccl.Send(c->dcount + 2, 2, ncclUint64, c->right, c->comm, st));
+        FORGE_NCCL(g_nccl.Recv(c->dcount + 6, 2, ncclUint64, c->right, c->comm, st));
+    }
+    FORGE_NCCL(g_nccl.GroupEnd());
+    FORGE_CUDA(cudaMemcpyAsync(c->hcount, c->dcount, 9 * sizeof(uint64_t), cudaMemcpyDeviceToHost, st));
+    return FORGE_OK;
+}
+
+// Message sizes of the round, from the host mirror of the counts.
+struct RoundSizes {
+    uint32_t ml, hl, mr, hr;      // sent: migrants / halo rows, left and right
+    uint64_t aml, ahl, amr, ahr;  // received
+    uint32_t keep;                // owned columns left after the migrants
+};
+
+int round_sizes(const forge_slab_comm* c, uint64_t n_own, uint64_t ld, RoundSizes& z) {
+    const uint64_t* h = c->hcount;
+    z = RoundSizes{(uint32_t)h[0], (uint32_t)h[1], (uint32_t)h[2], (uint32_t)h[3], h[4], h[5], h[6], h[7],
+                   (uint32_t)(n_own - h[8])};
+    if ((uint64_t)z.ml + z.hl > c->cap || (uint64_t)z.mr + z.hr > c->cap || z.aml + z.ahl > c->cap ||
+        z.amr + z.ahr > c->cap)
+        return set_error(FORGE_ERR_CAPACITY, "forge_slab_exchange: message exceeds capacity");
+    const uint64_t n_new = z.keep + z.aml + z.amr, ng = z.ahl + z.ahr + z.ml + z.mr;
+    if (n_new + ng > ld) return set_error(FORGE_ERR_CAPACITY, "forge_slab_exchange: owned + ghosts exceed ld");
+    return FORGE_OK;
+}
+
+int send_payload(forge_slab_comm* c, const RoundSizes& z, cudaStream_t st) {
+    FORGE_NCCL(g_nccl.GroupStart());
+    if (c->left >= 0) {
+        if (z.ml + z.hl) FORGE_NCCL(g_nccl.Send(c->send_l, (z.ml + z.hl) * kSlabRows, ncclFloat32, c->left, c->comm, st));
+        if (z.aml + z.ahl)
+            FORGE_NCCL(g_nccl.Recv(c->recv_l, (z.aml + z.ahl) * kSlabRows, ncclFloat32, c->left, c->comm, st));
+    }
+    if (c->right >= 0) {
+        if (z.mr + z.hr)
+            FORGE_NCCL(g_nccl.Send(c->send_r, (z.mr + z.hr) * kSlabRows, ncclFloat32, c->right, c->comm, st));
+        if (z.amr + z.ahr)
+            FORGE_NCCL(g_nccl.Recv(c->recv_r, (z.amr + z.ahr) * kSlabRows, ncclFloat32, c->right, c->comm, st));
+    }
+    FORGE_NCCL(g_nccl.GroupEnd());
+    return FORGE_OK;
+}
+
+// Arrivals after the kept owned columns, then the ghosts: halo from left,
+// halo from right, our migrants to left, to right. Records the layout for
+// the density round.
+int place_arrivals(forge_slab_comm* c, float* cols, uint64_t ld, const RoundSizes& z, uint64_t* n_own_out,
+                   uint64_t* n_ghost_out, cudaStream_t st) {
+    int rc;
+    uint32_t o = z.keep;
+    if ((rc = unpack(c->recv_l, (uint32_t)z.aml, cols, ld, o, st)) != FORGE_OK) return rc;
+    c->arr_l = o;
+    c->n_arr_l = (uint32_t)z.aml;
+    o += (uint32_t)z.aml;
+    if ((rc = unpack(c->recv_r, (uint32_t)z.amr, cols, ld, o, st)) != FORGE_OK) return rc;
+    c->arr_r = o;
+    c->n_arr_r = (uint32_t)z.amr;
+    o += (uint32_t)z.amr;
+    c->g_hl = o;
+    c->n_ghl = (uint32_t)z.ahl;
+    if ((rc = unpack(c->recv_l + z.aml * kSlabRows, (uint32_t)z.ahl, cols, ld, o, st)) != FORGE_OK) return rc;
+    o += (uint32_t)z.ahl;
+    c->g_hr = o;
+    c->n_ghr = (uint32_t)z.ahr;
+    if ((rc = unpack(c->recv_r + z.amr * kSlabRows, (uint32_t)z.ahr, cols, ld, o, st)) != FORGE_OK) return rc;
+    o += (uint32_t)z.ahr;
+    c->g_ml = o;
+    if ((rc = unpack(c->send_l, z.ml, cols, ld, o, st)) != FORGE_OK) return rc;
+    o += z.ml;
+    c->g_mr = o;
+    if ((rc = unpack(c->send_r, z.mr, cols, ld, o, st)) != FORGE_OK) return rc;
+    c->n_hl = z.hl;
+    c->n_hr = z.hr;
+    c->n_ml = z.ml;
+    c->n_mr = z.mr;
+    c->have_round = true;
+    *n_own_out = z.keep + z.aml + z.amr;
+    *n_ghost_out = z.ahl + z.ahr + z.ml + z.mr;
+    return FORGE_OK;
+}
+
+}  // namespace
+
 extern "C" int forge_slab_exchange(forge_slab_comm* c, float* cols, uint64_t ld, uint64_t n_own, int migrate,
                                    uint64_t* n_own_out, uint64_t* n_ghost_out, void* stream) {
     if (!c || !cols || !n_own_out || !n_ghost_out)
         return set_error(FORGE_ERR_INVALID_ARG, "forge_slab_exchange: NULL argument");
     if (n_own > c->cap || ld < c->cap)
         return set_error(FORGE_ERR_CAPACITY, "forge_slab_exchange: n_own or ld does not fit the capacity");
+    if (c->pending) return set_error(FORGE_ERR_INVALID_ARG, "forge_slab_exchange: a split round is open");
     FORGE_DEVICE_SCOPE(c->device);
     cudaStream_t st = as_stream(stream);
-    const uint32_t sides = (c->left >= 0 ? 1u : 0u) | (c->right >= 0 ? 2u : 0u);
+    const uint32_t sides = slab_sides(c);
     uint32_t* cm = c->counts;      // migrant list sizes A, L, R
     uint32_t* ch = c->counts + 3;  // halo list sizes 0, L, R
     int rc;
@@ -254,76 +371,82 @@ extern "C" int forge_slab_exchange(forge_slab_comm* c, float* cols, uint64_t ld,
     if ((rc = pack_list(c, cols, ld, c->idx_h, ch, 1, cm + 1, c->send_l, c->halo_l, st)) != FORGE_OK) return rc;
     if ((rc = pack_list(c, cols, ld, c->idx_h, ch, 2, cm + 2, c->send_r, c->halo_r, st)) != FORGE_OK) return rc;
     // 3. counts: ours to the neighbours, theirs back, everything to the host
-    slab::counts_msg_kernel<<<1, 1, 0, st>>>(cm, ch, c->dcount);
-    FORGE_LAUNCHED();
-    FORGE_CUDA(cudaMemsetAsync(c->dcount + 4, 0, 4 * sizeof(uint64_t), st));
-    FORGE_NCCL(g_nccl.GroupStart());
-    if (c->left >= 0) {
-        FORGE_NCCL(g_nccl.Send(c->dcount + 0, 2, ncclUint64, c->left, c->comm, st));
-        FORGE_NCCL(g_nccl.Recv(c->dcount + 4, 2, ncclUint64, c->left, c->comm, st));
-    }
-    if (c->right >= 0) {
-        FORGE_NCCL(g_nccl.Send(c->dcount + 2, 2, ncclUint64, c->right, c->comm, st));
-        FORGE_NCCL(g_nccl.Recv(c->dcount + 6, 2, ncclUint64, c->right, c->comm, st));
-    }
-    FORGE_NCCL(g_nccl.GroupEnd());
-    FORGE_CUDA(cudaMemcpyAsync(c->hcount, c->dcount, 9 * sizeof(uint64_t), cudaMemcpyDeviceToHost, st));
+    if ((rc = exchange_counts(c, st)) != FORGE_OK) return rc;
     FORGE_CUDA(cudaStreamSynchronize(st));
-    const uint32_t ml = (uint32_t)c->hcount[0], hl = (uint32_t)c->hcount[1];
-    const uint32_t mr = (uint32_t)c->hcount[2], hr = (uint32_t)c->hcount[3];
-    const uint64_t aml = c->hcount[4], ahl = c->hcount[5], amr = c->hcount[6], ahr = c->hcount[7];
-    const uint32_t keep = (uint32_t)(n_own - c->hcount[8]);
-    if ((uint64_t)ml + hl > c->cap || (uint64_t)mr + hr > c->cap || aml + ahl > c->cap || amr + ahr > c->cap)
-        return set_error(FORGE_ERR_CAPACITY, "forge_slab_exchange: message exceeds capacity");
-    const uint64_t n_new = keep + aml + amr;
-    const uint64_t ng = ahl + ahr + ml + mr;
-    if (n_new + ng > ld) return set_error(FORGE_ERR_CAPACITY, "forge_slab_exchange: owned + ghosts exceed ld");
-    // 4. payload
-    FORGE_NCCL(g_nccl.GroupStart());
-    if (c->left >= 0) {
-        if (ml + hl) FORGE_NCCL(g_nccl.Send(c->send_l, (ml + hl) * kSlabRows, ncclFloat32, c->left, c->comm, st));
-        if (aml + ahl) FORGE_NCCL(g_nccl.Recv(c->recv_l, (aml + ahl) * kSlabRows, ncclFloat32, c->left, c->comm, st));
+    RoundSizes z;
+    if ((rc = round_sizes(c, n_own, ld, z)) != FORGE_OK) return rc;
+    // 4. payload, 5. arrivals, then ghosts
+    if ((rc = send_payload(c, z, st)) != FORGE_OK) return rc;
+    return place_arrivals(c, cols, ld, z, n_own_out, n_ghost_out, st);
+}
+
+extern "C" int forge_slab_exchange_begin(forge_slab_comm* c, const float* cols, uint64_t ld, uint64_t n_own,
+                                         void* stream) {
+    if (!c || !cols) return set_error(FORGE_ERR_INVALID_ARG, "forge_slab_exchange_begin: NULL argument");
+    if (n_own > c->cap || ld < c->cap)
+        return set_error(FORGE_ERR_CAPACITY, "forge_slab_exchange_begin: n_own or ld does not fit the capacity");
+    if (c->pending) return set_error(FORGE_ERR_INVALID_ARG, "forge_slab_exchange_begin: a split round is open");
+    FORGE_DEVICE_SCOPE(c->device);
+    cudaStream_t sd = as_stream(stream);
+    // Migrants and in-slab halo rows (disjoint) from one read of the
+    // uncompacted columns, records packed as they are listed; the halo lists
+    // keep the uncompacted indices until _end remaps them.
+    if (n_own) {
+        const slab::XchgArgs a{cols, ld, (uint32_t)n_own, c->lo, c->hi, c->reach, slab_sides(c)};
+        const uint32_t tiles = grid_blocks(n_own, slab::kTile);
+        slab::xchg_count_kernel<<<tiles, slab::kThreads, 0, sd>>>(a, c->xtiles);
+        slab::xchg_scan_kernel<<<1, 1024, 0, sd>>>(c->xtiles, tiles, c->counts, c->dcount);
+        slab::xchg_write_kernel<<<tiles, slab::kThreads, 0, sd>>>(
+            a, c->xtiles, c->counts, slab::XchgOut{c->idx, c->halo_l, c->halo_r, c->send_l, c->send_r});
+        FORGE_LAUNCHED();
+    } else {
+        FORGE_CUDA(cudaMemsetAsync(c->counts, 0, 6 * sizeof(uint32_t), sd));
+        FORGE_CUDA(cudaMemsetAsync(c->dcount, 0, 9 * sizeof(uint64_t), sd));
     }
-    if (c->right >= 0) {
-        if (mr + hr) FORGE_NCCL(g_nccl.Send(c->send_r, (mr + hr) * kSlabRows, ncclFloat32, c->right, c->comm, st));
-        if (amr + ahr) FORGE_NCCL(g_nccl.Recv(c->recv_r, (amr + ahr) * kSlabRows, ncclFloat32, c->right, c->comm, st));
-    }
-    FORGE_NCCL(g_nccl.GroupEnd());
-    // 5. arrivals, then ghosts
-    uint32_t o = keep;
-    if ((rc = unpack(c->recv_l, (uint32_t)aml, cols, ld, o, st)) != FORGE_OK) return rc;
-    c->arr_l = o;
-    c->n_arr_l = (uint32_t)aml;
-    o += (uint32_t)aml;
-    if ((rc = unpack(c->recv_r, (uint32_t)amr, cols, ld, o, st)) != FORGE_OK) return rc;
-    c->arr_r = o;
-    c->n_arr_r = (uint32_t)amr;
-    o += (uint32_t)amr;
-    c->g_hl = o;
-    c->n_ghl = (uint32_t)ahl;
-    if ((rc = unpack(c->recv_l + aml * kSlabRows, (uint32_t)ahl, cols, ld, o, st)) != FORGE_OK) return rc;
-    o += (uint32_t)ahl;
-    c->g_hr = o;
-    c->n_ghr = (uint32_t)ahr;
-    if ((rc = unpack(c->recv_r + amr * kSlabRows, (uint32_t)ahr, cols, ld, o, st)) != FORGE_OK) return rc;
-    o += (uint32_t)ahr;
-    c->g_ml = o;
-    if ((rc = unpack(c->send_l, ml, cols, ld, o, st)) != FORGE_OK) return rc;
-    o += ml;
-    c->g_mr = o;
-    if ((rc = unpack(c->send_r, mr, cols, ld, o, st)) != FORGE_OK) return rc;
-    c->n_hl = hl;
-    c->n_hr = hr;
-    c->n_ml = ml;
-    c->n_mr = mr;
-    c->have_round = true;
-    *n_own_out = n_new;
-    *n_ghost_out = ng;
+    int rc;
+    if ((rc = exchange_counts(c, sd, false)) != FORGE_OK) return rc;
+    FORGE_CUDA(cudaEventRecord(c->ev_counts, sd));
+    c->pend_stream = sd;
+    c->pending = true;
+    c->pend_n_own = n_own;
     return FORGE_OK;
+}
+
+extern "C" int forge_slab_exchange_end(forge_slab_comm* c, float* cols, uint64_t ld, uint64_t* n_own_out,
+                                       uint64_t* n_ghost_out, void* stream) {
+    if (!c || !cols || !n_own_out || !n_ghost_out)
+        return set_error(FORGE_ERR_INVALID_ARG, "forge_slab_exchange_end: NULL argument");
+    if (!c->pending) return set_error(FORGE_ERR_INVALID_ARG, "forge_slab_exchange_end: no forge_slab_exchange_begin");
+    if (ld < c->cap) return set_error(FORGE_ERR_CAPACITY, "forge_slab_exchange_end: ld does not fit the capacity");
+    c->pending = false;
+    FORGE_DEVICE_SCOPE(c->device);
+    cudaStream_t st = as_stream(stream), sd = c->pend_stream;
+    const uint64_t n_own = c->pend_n_own;
+    int rc;
+    FORGE_CUDA(cudaEventSynchronize(c->ev_counts));  // the interior pass keeps running meanwhile
+    RoundSizes z;
+    if ((rc = round_sizes(c, n_own, ld, z)) != FORGE_OK) return rc;
+    if ((rc = send_payload(c, z, sd)) != FORGE_OK) return rc;
+    FORGE_CUDA(cudaEventRecord(c->ev_payload, sd));
+    FORGE_CUDA(cudaStreamWaitEvent(st, c->ev_payload, 0));
+    if (n_own - z.keep) {
+        uint32_t* cm = c->counts;
+        slab::compact_kernel<<<1, 1024, 0, st>>>(cols, ld, kSlabRows, (uint32_t)n_own, c->idx, 0u, cm);
+        const uint32_t gb = (uint32_t)c->sms * 2;
+        if (z.hl)
+            slab::remap_after_compact_kernel<<<std::min(grid_blocks(z.hl, 256), gb), 256, 0, st>>>(
+                c->halo_l, z.hl, nullptr, (uint32_t)n_own, c->idx, cm);
+        if (z.hr)
+            slab::remap_after_compact_kernel<<<std::min(grid_blocks(z.hr, 256), gb), 256, 0, st>>>(
+                c->halo_r, z.hr, nullptr, (uint32_t)n_own, c->idx, cm);
+        FORGE_LAUNCHED();
+    }
+    return place_arrivals(c, cols, ld, z, n_own_out, n_ghost_out, st);
 }
 
 extern "C" int forge_slab_exchange_rho(forge_slab_comm* c, float* rho, void* stream) {
     if (!c || !rho) return set_error(FORGE_ERR_INVALID_ARG, "forge_slab_exchange_rho: NULL argument");
+    if (c->pending) return set_error(FORGE_ERR_INVALID_ARG, "forge_slab_exchange_rho: a split round is open");
     if (!c->have_round) return set_error(FORGE_ERR_INVALID_ARG, "forge_slab_exchange_rho: no exchange round yet");
     FORGE_DEVICE_SCOPE(c->device);
     cudaStream_t st = as_stream(stream);

@@ -288,7 +288,109 @@ struct ForceOut {
     float* py;
     float* pz;
     uint32_t limit;  // only particles with original index < limit are written
+    // Interior pass of a zoned step (zone == 2): a particle whose x before
+    // or after the step lies below glo or at/above ghi sets kDevZone in
+    // *status (it is, or moved, too close to a face for the overlapped
+    // exchange).
+    uint32_t zone = 0;
+    float glo = 0.f, ghi = 0.f;
+    uint32_t* status = nullptr;
 };
+
+// Sorted positions of one zone of a zoned force pass: list `list` (1 =
+// boundary, 2 = interior) of a classification [A | L | R] with device-side
+// sizes counts[3].
+struct ZoneList {
+    const uint32_t* idx = nullptr;
+    const uint32_t* counts = nullptr;
+    uint32_t list = 0;
+};
+
+// Zone lists from the cell-start table. With keys cell << sub_bits | slice
+// and x the fastest cell axis, each grid row (cy, cz) is one run of the
+// cell order, and the interior zone -- x-slices [k_lo, k_hi) of the row --
+// one contiguous piece of it: per row, boundary = [b0, i0) u [i1, e),
+// interior = [i0, i1). Lists come out in the cell order (row by row), so
+// consecutive entries are mostly neighbours in the same row.
+constexpr int kZoneRows = 256;  // rows per block (one per thread)
+
+struct ZoneRows {
+    const uint32_t* __restrict__ cell_start;
+    uint32_t rows;     // ny * nz
+    uint32_t row_len;  // table entries per row: nx << sub_bits
+    uint32_t k_lo, k_hi;
+    __device__ __forceinline__ void seg(uint32_t r, uint32_t& b0, uint32_t& i0, uint32_t& i1, uint32_t& e) const {
+        const uint32_t* t = cell_start + (size_t)r * row_len;
+        b0 = __ldg(t);
+        i0 = __ldg(t + k_lo);
+        i1 = __ldg(t + k_hi);
+        e = __ldg(t + row_len);
+    }
+};
+
+// Per-tile sums of the boundary and interior lengths (tile_counts[t*3 + 1],
+// [t*3 + 2]; [t*3] = 0), in the layout slab::classify_scan_kernel scans.
+__global__ void __launch_bounds__(kZoneRows) zone_rows_count_kernel(ZoneRows z, uint32_t* __restrict__ tile_counts) {
+    __shared__ uint32_t s[2];
+    if (threadIdx.x < 2) s[threadIdx.x] = 0;
+    __syncthreads();
+    const uint32_t r = blockIdx.x * kZoneRows + threadIdx.x;
+    uint32_t lb = 0, li = 0;
+    if (r < z.rows) {
+        uint32_t b0, i0, i1, e;
+        z.seg(r, b0, i0, i1, e);
+        lb = (i0 - b0) + (e - i1);
+        li = i1 - i0;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        lb += __shfl_xor_sync(0xffffffffu, lb, o);
+        li += __shfl_xor_sync(0xffffffffu, li, o);
+    }
+    if ((threadIdx.x & 31) == 0) {
+        if (lb) atomicAdd(&s[0], lb);
+        if (li) atomicAdd(&s[1], li);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        tile_counts[blockIdx.x * 3 + 0] = 0;
+        tile_counts[blockIdx.x * 3 + 1] = s[0];
+        tile_counts[blockIdx.x * 3 + 2] = s[1];
+    }
+}
+
+// Writes the lists [A (empty) | boundary | interior] of sorted positions.
+__global__ void __launch_bounds__(kZoneRows)
+    zone_rows_write_kernel(ZoneRows z, const uint32_t* __restrict__ tile_offsets, const uint32_t* __restrict__ counts,
+                           uint32_t* __restrict__ out) {
+    __shared__ uint32_t s_scan[kZoneRows / 32 + 1];
+    __shared__ uint32_t s_seg[kZoneRows][6];
+    const uint32_t r = blockIdx.x * kZoneRows + threadIdx.x;
+    uint32_t b0 = 0, i0 = 0, i1 = 0, e = 0;
+    if (r < z.rows) z.seg(r, b0, i0, i1, e);
+    uint32_t total;
+    const uint32_t ob = block_exclusive_scan<kZoneRows>((i0 - b0) + (e - i1), s_scan, &total) +
+                        tile_offsets[blockIdx.x * 3 + 1] + counts[0];
+    const uint32_t oi = block_exclusive_scan<kZoneRows>(i1 - i0, s_scan, &total) + tile_offsets[blockIdx.x * 3 + 2] +
+                        counts[0] + counts[1];
+    s_seg[threadIdx.x][0] = b0;
+    s_seg[threadIdx.x][1] = i0;
+    s_seg[threadIdx.x][2] = i1;
+    s_seg[threadIdx.x][3] = e;
+    s_seg[threadIdx.x][4] = ob;
+    s_seg[threadIdx.x][5] = oi;
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t nrows = min((uint32_t)kZoneRows, z.rows - blockIdx.x * kZoneRows);
+    for (uint32_t q = warp; q < nrows; q += kZoneRows / 32) {
+        const uint32_t qb0 = s_seg[q][0], qi0 = s_seg[q][1], qi1 = s_seg[q][2], qe = s_seg[q][3];
+        const uint32_t qob = s_seg[q][4], qoi = s_seg[q][5];
+        const uint32_t la = qi0 - qb0;
+        for (uint32_t j = lane; j < la; j += 32) out[qob + j] = qb0 + j;
+        for (uint32_t j = lane; j < qe - qi1; j += 32) out[qob + la + j] = qi1 + j;
+        for (uint32_t j = lane; j < qi1 - qi0; j += 32) out[qoi + j] = qi0 + j;
+    }
+}
 
 struct StepOp {
     uint32_t kind;  // FORGE_OP_*
@@ -513,6 +615,8 @@ __device__ __forceinline__ void force_finish(const ForceAcc& A, uint32_t i, cons
         }
         if (ep.flags & 4u) box_op(x, y, z, vx, vy, vz, ep.bmin, ep.bmax, ep.restitution);
     }
+    if (out.zone == 2 && (x < out.glo || x >= out.ghi || A.p.x < out.glo || A.p.x >= out.ghi))
+        atomicOr(out.status, kDevZone);
     out.px[i] = x;
     out.py[i] = y;
     out.pz[i] = z;
@@ -524,13 +628,11 @@ __device__ __forceinline__ void force_finish(const ForceAcc& A, uint32_t i, cons
 // Force pass, one particle per thread (dense cells, where the hit loop
 // dominates and a second particle would only add divergence).
 template <int TERMS, int EPI>
-__global__ void __launch_bounds__(128)
-    force_single_kernel(const float4* __restrict__ pos4, const float4* __restrict__ vel4,
-                        const float2* __restrict__ aux, const uint32_t* __restrict__ cell_start,
-                        const uint32_t* __restrict__ sorted_idx, uint32_t n, Geom g, SphConsts c, StepEpi ep,
-                        ForceOut out) {
-    const uint32_t s = blockIdx.x * blockDim.x + threadIdx.x;
-    if (s >= n) return;
+__device__ __forceinline__ void force_single_at(uint32_t s, const float4* __restrict__ pos4,
+                                                const float4* __restrict__ vel4, const float2* __restrict__ aux,
+                                                const uint32_t* __restrict__ cell_start,
+                                                const uint32_t* __restrict__ sorted_idx, const Geom& g,
+                                                const SphConsts& c, const StepEpi& ep, const ForceOut& out) {
     const uint32_t i = sorted_idx[s];
     if (i >= out.limit) return;  // not updated (a ghost of a sharded run)
     const float* __restrict__ pj = reinterpret_cast<const float*>(aux);
@@ -548,27 +650,28 @@ __global__ void __launch_bounds__(128)
     force_finish<EPI>(A, i, ep, out);
 }
 
-// Force pass, two consecutive cell-ordered particles per thread with the same
-// window logic as density_pair_kernel (union walk in one cell, three
-// segments for adjacent cells, two single walks otherwise). A particle with
-// rho < 1e-6 (1/rho stored as 0) walks nothing and keeps its velocity.
-template <int TERMS, int EPI>
-__global__ void __launch_bounds__(128)
-    force_kernel(const float4* __restrict__ pos4, const float4* __restrict__ vel4, const float2* __restrict__ aux,
-                 const uint32_t* __restrict__ cell_start, const uint32_t* __restrict__ sorted_idx, uint32_t n, Geom g,
-                 SphConsts c, StepEpi ep, ForceOut out) {
-    const uint32_t s0 = 2u * (blockIdx.x * blockDim.x + threadIdx.x);
-    if (s0 >= n) return;
-    const bool has1 = s0 + 1 < n;
+// Two cell-ordered particles s0, s1 (s1 valid if has1) with the same window
+// logic as density_pair_kernel (union walk when both lie in one row, two
+// single walks otherwise). NEAR: the two need not be adjacent in the cell
+// order (zone lists), so the union walk also requires their cells to be at
+// most two apart. A particle with rho < 1e-6 (1/rho stored as 0) walks
+// nothing and keeps its velocity.
+template <int TERMS, int EPI, bool NEAR>
+__device__ __forceinline__ void force_pair_at(uint32_t s0, uint32_t s1, bool has1, const float4* __restrict__ pos4,
+                                              const float4* __restrict__ vel4, const float2* __restrict__ aux,
+                                              const uint32_t* __restrict__ cell_start,
+                                              const uint32_t* __restrict__ sorted_idx, const Geom& g,
+                                              const SphConsts& c, const StepEpi& ep, const ForceOut& out) {
     const float* __restrict__ pj = reinterpret_cast<const float*>(aux);
     ForceAcc A = force_acc(pos4, vel4, aux, s0, c);
-    ForceAcc B = force_acc(pos4, vel4, aux, has1 ? s0 + 1 : s0, c);
-    const uint32_t i0 = sorted_idx[s0], i1 = has1 ? sorted_idx[s0 + 1] : 0xffffffffu;
+    ForceAcc B = force_acc(pos4, vel4, aux, has1 ? s1 : s0, c);
+    const uint32_t i0 = sorted_idx[s0], i1 = has1 ? sorted_idx[s1] : 0xffffffffu;
     // rho < 1e-6 (1/rho stored as 0) or not updated (ghost): no walk
     const bool va = A.v.w != 0.f && i0 < out.limit, vb = has1 && B.v.w != 0.f && i1 < out.limit;
     const Frame f0 = make_frame(A.p, g);
     const Frame f1 = make_frame(B.p, g);
-    if (va && vb && g.pairable && f0.cy == f1.cy && f0.cz == f1.cz) {
+    const bool near = !NEAR || abs(f0.f_own - f1.f_own) <= (2 << g.sub_bits);
+    if (va && vb && g.pairable && f0.cy == f1.cy && f0.cz == f1.cz && near) {
 #pragma unroll 1
         for (int r = 0; r < 9; ++r) {
             int l0, h0, l1, h1, lo, hi;
@@ -600,6 +703,54 @@ __global__ void __launch_bounds__(128)
     }
     force_finish<EPI>(A, i0, ep, out);
     if (has1) force_finish<EPI>(B, i1, ep, out);
+}
+
+__device__ __forceinline__ const uint32_t* zone_begin(const ZoneList& z, uint32_t& cnt) {
+    cnt = z.counts[z.list];
+    return z.idx + z.counts[0] + (z.list == 2 ? z.counts[1] : 0u);
+}
+
+template <int TERMS, int EPI, bool LIST>
+__global__ void __launch_bounds__(128)
+    force_single_kernel(const float4* __restrict__ pos4, const float4* __restrict__ vel4,
+                        const float2* __restrict__ aux, const uint32_t* __restrict__ cell_start,
+                        const uint32_t* __restrict__ sorted_idx, uint32_t n, Geom g, SphConsts c, StepEpi ep,
+                        ForceOut out, ZoneList zl) {
+    if (!LIST) {
+        const uint32_t s = blockIdx.x * blockDim.x + threadIdx.x;
+        if (s < n) force_single_at<TERMS, EPI>(s, pos4, vel4, aux, cell_start, sorted_idx, g, c, ep, out);
+        return;
+    }
+    // LIST: the grid covers an upper bound of the list (its size is only on
+    // the device); threads past its end leave at once
+    uint32_t cnt;
+    const uint32_t* lst = zone_begin(zl, cnt);
+    const uint32_t t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t < cnt) force_single_at<TERMS, EPI>(lst[t], pos4, vel4, aux, cell_start, sorted_idx, g, c, ep, out);
+}
+
+// Force pass, two consecutive cell-ordered particles per thread (LIST: two
+// consecutive entries of a zone list).
+template <int TERMS, int EPI, bool LIST>
+__global__ void __launch_bounds__(128)
+    force_kernel(const float4* __restrict__ pos4, const float4* __restrict__ vel4, const float2* __restrict__ aux,
+                 const uint32_t* __restrict__ cell_start, const uint32_t* __restrict__ sorted_idx, uint32_t n, Geom g,
+                 SphConsts c, StepEpi ep, ForceOut out, ZoneList zl) {
+    if (!LIST) {
+        const uint32_t s0 = 2u * (blockIdx.x * blockDim.x + threadIdx.x);
+        if (s0 < n)
+            force_pair_at<TERMS, EPI, false>(s0, s0 + 1, s0 + 1 < n, pos4, vel4, aux, cell_start, sorted_idx, g, c,
+                                             ep, out);
+        return;
+    }
+    uint32_t cnt;
+    const uint32_t* lst = zone_begin(zl, cnt);
+    const uint32_t t = 2u * (blockIdx.x * blockDim.x + threadIdx.x);
+    if (t < cnt) {
+        const bool has1 = t + 1 < cnt;
+        force_pair_at<TERMS, EPI, true>(lst[t], has1 ? lst[t + 1] : 0u, has1, pos4, vel4, aux, cell_start,
+                                        sorted_idx, g, c, ep, out);
+    }
 }
 
 }  // namespace sph

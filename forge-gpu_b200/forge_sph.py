@@ -68,8 +68,9 @@ EXPORTED = (
     "forge_sph_force_step",
     "forge_slab_create", "forge_slab_destroy", "forge_slab_classify", "forge_slab_compact",
     "forge_nccl_unique_id", "forge_slab_comm_create", "forge_slab_comm_destroy", "forge_slab_exchange",
-    "forge_slab_exchange_rho",
+    "forge_slab_exchange_rho", "forge_sph_force_step_zone", "forge_slab_exchange_begin", "forge_slab_exchange_end",
 )
+ZONE_BOUNDARY, ZONE_INTERIOR = 1, 2
 STATIC_SORT_MAX_N = 1 << 20
 
 
@@ -94,6 +95,12 @@ class StepParams(ctypes.Structure):
     _fields_ = [("dt", ctypes.c_float), ("gravity", ctypes.c_float * 3), ("box_min", ctypes.c_float * 3),
                 ("box_max", ctypes.c_float * 3), ("restitution", ctypes.c_float), ("flags", ctypes.c_uint32),
                 ("n_ops", ctypes.c_uint32), ("ops", StepOp * 8)]
+
+
+class ForceZone(ctypes.Structure):
+    """forge_force_zone: the x-split of forge_sph_force_step_zone."""
+    _fields_ = [("mode", ctypes.c_uint32), ("inner_lo", ctypes.c_float), ("inner_hi", ctypes.c_float),
+                ("guard_lo", ctypes.c_float), ("guard_hi", ctypes.c_float)]
 
 
 _lib = None
@@ -141,6 +148,10 @@ def lib() -> ctypes.CDLL:
         "forge_slab_compact": (i32, [vp, u64, u32, u64, vp, u64, vp]),
         "forge_sph_force_step": (i32, [vp, ctypes.POINTER(SphParams), ctypes.POINTER(StepParams), vp, vp, vp, vp,
                                        vp, vp, vp, u64, u64, vp]),
+        "forge_sph_force_step_zone": (i32, [vp, ctypes.POINTER(SphParams), ctypes.POINTER(StepParams), vp, vp, vp,
+                                            vp, vp, vp, vp, u64, u64, ctypes.POINTER(ForceZone), vp]),
+        "forge_slab_exchange_begin": (i32, [vp, vp, u64, u64, vp]),
+        "forge_slab_exchange_end": (i32, [vp, vp, u64, ctypes.POINTER(u64), ctypes.POINTER(u64), vp]),
         "forge_grid_profile_read": (i32, [vp, ctypes.POINTER(f32), u32, ctypes.POINTER(u32)]),
     }
     for name, (res, args) in sig.items():

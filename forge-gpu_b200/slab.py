@@ -26,6 +26,7 @@ from __future__ import annotations
 
 import ctypes
 
+import numpy as np
 import torch
 
 # Payload columns: x, y, z, vx, vy, vz, id (int32 bits carried in a float32).
@@ -42,6 +43,29 @@ class SlabGeometry:
         self.hi = x0 + w * (rank + 1)
         self.first = rank == 0
         self.last = rank == world - 1
+
+    def force_zones(self, reach: float, margin: float | None = None):
+        """(inner_lo, inner_hi, guard_lo, guard_hi) in float32 for the split
+        force pass. An interior particle must start and end the step at
+        least `reach` inside every face that has a neighbour (guard), so no
+        halo or migrant list can see it; the interior zone starts `margin`
+        (default h/4, the largest displacement allowed in one step) further
+        in. Sums in float32, like the classification's lo + reach."""
+        f32 = np.float32
+        inf = f32(np.inf)
+        lo, hi, r = f32(self.lo), f32(self.hi), f32(reach)
+        m = f32(self.h / 4 if margin is None else margin)
+        if self.first:
+            inner_lo = guard_lo = -inf
+        else:
+            guard_lo = lo + r
+            inner_lo = guard_lo + m
+        if self.last:
+            inner_hi = guard_hi = inf
+        else:
+            guard_hi = hi - r
+            inner_hi = guard_hi - m
+        return float(inner_lo), float(inner_hi), float(guard_lo), float(guard_hi)
 
     def owned_mask(self, x: torch.Tensor) -> torch.Tensor:
         m = torch.ones_like(x, dtype=torch.bool)
@@ -206,6 +230,21 @@ class NcclComm:
                                                 torch.cuda.current_stream().cuda_stream))
         run.n, run.ng = n_own.value, ng.value
 
+    split = True  # supports the exchange overlapped with the interior force pass
+
+    def exchange_begin(self) -> None:
+        run = self.run
+        self.f.check(self.L.forge_slab_exchange_begin(self.h, run.cols.data_ptr(), run.cols.stride(0), run.n,
+                                                      torch.cuda.current_stream().cuda_stream))
+
+    def exchange_end(self) -> None:
+        run = self.run
+        n_own, ng = ctypes.c_uint64(), ctypes.c_uint64()
+        self.f.check(self.L.forge_slab_exchange_end(self.h, run.cols.data_ptr(), run.cols.stride(0),
+                                                    ctypes.byref(n_own), ctypes.byref(ng),
+                                                    torch.cuda.current_stream().cuda_stream))
+        run.n, run.ng = n_own.value, ng.value
+
     def exchange_rho(self, rho: torch.Tensor) -> None:
         self.f.check(self.L.forge_slab_exchange_rho(self.h, rho.data_ptr(), torch.cuda.current_stream().cuda_stream))
 
@@ -251,6 +290,8 @@ class SlabRun:
         self.n = n_own
         self.ng = 0
         self.timing = None  # set to a list to record per-phase CUDA events
+        self.timing_side = []
+        self._hp = None  # high-priority stream of the split force pass
         self.comm = NcclComm(self, dist, forge_sph) if comm == "nccl" else PyComm(self, dist, comm_device)
         self.comm.exchange(migrate=False)  # initial halo
 
@@ -259,6 +300,14 @@ class SlabRun:
             ev = torch.cuda.Event(enable_timing=True)
             ev.record()
             self.timing.append((name, ev))
+
+    def _mark_side(self, name):
+        """Event on the current (side) stream, timed from the step's last
+        main-stream mark (the overlapped exchange's progress)."""
+        if self.timing is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            self.timing_side.append((name, ev, self.timing[-1][1]))
 
     @property
     def capacity(self) -> int:
@@ -304,11 +353,40 @@ class SlabRun:
         if perm is not None:
             rho = rho[perm]
             C[:, :n] = C[:, perm]
-        self.backend.force_step([C[k, :n] for k in range(6)], rho, n, n if perm is not None else n_own)
-        if perm is not None:
-            C[:, perm] = C[:, :n].clone()
-        self._mark("force")
-        self.comm.exchange(migrate=True)
+        n_upd = n if perm is not None else n_own
+        cols6 = [C[k, :n] for k in range(6)]
+        if getattr(self.comm, "split", False):
+            zones = self.geo.force_zones(self.reach)
+            if perm is None:
+                # boundary zone on a high-priority stream, round 1 starting
+                # as soon as it is done, while the interior zone runs on the
+                # main stream alongside both
+                main = torch.cuda.current_stream()
+                if self._hp is None:
+                    self._hp = torch.cuda.Stream(device=main.device, priority=-1)
+                self._hp.wait_stream(main)
+                with torch.cuda.stream(self._hp):
+                    self.backend.force_step(cols6, rho, n, n_upd, zone=(1,) + zones)
+                    self._mark_side("boundary_done")
+                    self.comm.exchange_begin()
+                    self._mark_side("counts_done")
+                self.backend.force_step(cols6, rho, n, n_upd, zone=(2,) + zones)
+            else:
+                self.backend.force_step(cols6, rho, n, n_upd, zone=(1,) + zones)
+                self.backend.force_step(cols6, rho, n, n_upd, zone=(2,) + zones)
+                C[:, perm] = C[:, :n].clone()
+                self.comm.exchange_begin()
+            self._mark("force")
+            self.comm.exchange_end()  # the main stream waits for the payload, which followed the boundary zone
+            if perm is None:
+                with torch.cuda.stream(self._hp):
+                    self._mark_side("payload_done")
+        else:
+            self.backend.force_step(cols6, rho, n, n_upd)
+            if perm is not None:
+                C[:, perm] = C[:, :n].clone()
+            self._mark("force")
+            self.comm.exchange(migrate=True)
         self._mark("exchange")
 
 
@@ -316,9 +394,12 @@ def torch_classify(x, n, lo, hi, reach, flags):
     """forge_slab_classify with torch ops (CPU ranks in tests)."""
     x = x[:n]
     none = torch.zeros(n, dtype=torch.bool, device=x.device)
-    halo = bool(flags & 4)
+    halo, in_slab = bool(flags & 4), bool(flags & 8)
     left = (x < lo + reach if halo else x < lo) if flags & 1 else none
     right = (x >= hi - reach if halo else x >= hi) if flags & 2 else none
+    if halo and in_slab:
+        left = left & (x >= lo)
+        right = right & (x < hi)
     both = none if halo else (left | right)
     return tuple(torch.nonzero(m).flatten() for m in (both, left, right))
 
@@ -391,8 +472,16 @@ class GpuBackend:
                                               n, rho.data_ptr(), self._st()))
         return rho
 
-    def force_step(self, cols, rho, n, n_update):
-        """Force + epilogue in place; rows >= n_update (ghosts) are skipped."""
-        self.f.check(self.L.forge_sph_force_step(self.grid.handle, ctypes.byref(self.sp), ctypes.byref(self.stp),
-                                                 *(c.data_ptr() for c in cols), rho.data_ptr(), n, n_update,
-                                                 self._st()))
+    def force_step(self, cols, rho, n, n_update, zone=None):
+        """Force + epilogue in place; rows >= n_update (ghosts) are skipped.
+        zone = (mode, inner_lo, inner_hi, guard_lo, guard_hi) runs one half of
+        the split pass (forge_sph_force_step_zone)."""
+        if zone is None:
+            self.f.check(self.L.forge_sph_force_step(self.grid.handle, ctypes.byref(self.sp),
+                                                     ctypes.byref(self.stp), *(c.data_ptr() for c in cols),
+                                                     rho.data_ptr(), n, n_update, self._st()))
+            return
+        z = self.f.ForceZone(*zone)
+        self.f.check(self.L.forge_sph_force_step_zone(self.grid.handle, ctypes.byref(self.sp), ctypes.byref(self.stp),
+                                                      *(c.data_ptr() for c in cols), rho.data_ptr(), n, n_update,
+                                                      ctypes.byref(z), self._st()))

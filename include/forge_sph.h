@@ -56,6 +56,7 @@ enum forge_status {
 #define FORGE_DEV_TIMEOUT 0x1u
 #define FORGE_DEV_KEY_RANGE 0x2u
 #define FORGE_DEV_CAPACITY 0x4u
+#define FORGE_DEV_ZONE 0x8u
 
 /* Copy the calling thread's last error message into buf (NUL-terminated).
  * Returns the full message length. */
@@ -294,6 +295,37 @@ FORGE_API int forge_sph_force_step(forge_grid* g, const forge_sph_params* p, con
                                    float* px, float* py, float* pz, float* vx, float* vy, float* vz,
                                    const float* density, uint64_t n, uint64_t n_update, void* stream);
 
+/* Split form of forge_sph_force_step for overlapping the slab exchange with
+ * the force pass. The owned particles (i < n_update) are split by grid cell:
+ * the interior zone is the cells whose x-extent lies inside
+ * [inner_lo, inner_hi) (+-inf for an open side), the boundary zone the other
+ * cells. Call once with FORGE_ZONE_BOUNDARY (gathers velocities + density,
+ * lists both zones, updates the boundary particles), then, on the same grid
+ * build, once with FORGE_ZONE_INTERIOR (updates the rest from the same
+ * gathered state). The two calls together equal one forge_sph_force_step bit
+ * for bit. The interior call waits, on its own stream, only for the boundary
+ * call's gather and lists, so the two force kernels may run concurrently
+ * when the calls use two streams; once the boundary call's work on its
+ * stream is done the boundary particles' columns are final and may be read
+ * (e.g. by forge_slab_exchange_begin enqueued on that stream). An interior
+ * particle whose x before or after the step lies outside
+ * [guard_lo, guard_hi) sets FORGE_DEV_ZONE in the grid's status
+ * (forge_grid_check): it is, or moved, too close to a face for the
+ * overlapped exchange to classify it safely. The first boundary call on a
+ * grid allocates its zone lists (4 bytes per particle). */
+#define FORGE_ZONE_BOUNDARY 1u
+#define FORGE_ZONE_INTERIOR 2u
+typedef struct forge_force_zone {
+    uint32_t mode;
+    float inner_lo, inner_hi;
+    float guard_lo, guard_hi;
+} forge_force_zone;
+
+FORGE_API int forge_sph_force_step_zone(forge_grid* g, const forge_sph_params* p, const forge_step_params* sp,
+                                        float* px, float* py, float* pz, float* vx, float* vy, float* vz,
+                                        const float* density, uint64_t n, uint64_t n_update,
+                                        const forge_force_zone* zone, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Slab-exchange helpers for the sharded step. No counterpart in the        */
 /* reference: its multi-GPU API is a stub (forge-runtime/src/cuda.rs:134-178). */
@@ -306,9 +338,11 @@ FORGE_API int forge_slab_create(uint64_t max_n, int device, forge_slab** out);
 FORGE_API void forge_slab_destroy(forge_slab* h);
 
 /* Ordered selection against the slab [lo, hi). flags: 1 = has a left
- * neighbour, 2 = has a right neighbour, 4 = halo mode.
+ * neighbour, 2 = has a right neighbour, 4 = halo mode, 8 = (halo mode)
+ * in-slab rows only.
  *   migrate mode: L = {i : x[i] < lo}, R = {i : x[i] >= hi}, A = L u R
  *   halo mode:    L = {i : x[i] < lo + reach}, R = {i : x[i] >= hi - reach}, A = {}
+ *   with 8:       L = {i : lo <= x[i] < lo + reach}, R = {i : hi - reach <= x[i] < hi}
  * (L only with a left neighbour, R only with a right one). idx_out receives
  * [A | L | R], each ascending -- at most 2n entries, so it must hold 2n;
  * counts[3] (device) = |A|, |L|, |R|. */
@@ -342,9 +376,29 @@ FORGE_API void forge_slab_comm_destroy(forge_slab_comm* c);
  * migrants (x outside the slab) leave the owned columns and go to the
  * neighbour, together with the halo rows (owned particles within reach of a
  * face); arrivals are appended to the owned columns, then the ghosts.
- * Synchronises `stream` three times (list sizes and counts). */
+ * Synchronises `stream` once (the exchanged message sizes). */
 FORGE_API int forge_slab_exchange(forge_slab_comm* c, float* cols, uint64_t ld, uint64_t n_own, int migrate,
                                   uint64_t* n_own_out, uint64_t* n_ghost_out, void* stream);
+
+/* Round 1 split for overlap with the interior force pass (same result as
+ * forge_slab_exchange with migrate = 1, up to the order of the halo rows):
+ *   stream B: forge_sph_force_step_zone(BOUNDARY)
+ *             forge_slab_exchange_begin   classify + pack migrants and halo
+ *                                         rows, exchange the counts
+ *   stream A: forge_sph_force_step_zone(INTERIOR)
+ *             forge_slab_exchange_end     wait (host) for the counts, send the
+ *                                         payload on stream B, then on stream
+ *                                         A: remove the migrants, append
+ *                                         arrivals and ghosts.
+ * Halo rows are taken among the owned particles still in the slab
+ * (lo <= x < lo + reach, hi - reach <= x < hi), so begin may read the
+ * columns while the interior pass writes particles at least `reach` away
+ * from both faces (the zone's guard). No call on `c` may come between the
+ * two; stream B should have a high priority. */
+FORGE_API int forge_slab_exchange_begin(forge_slab_comm* c, const float* cols, uint64_t ld, uint64_t n_own,
+                                        void* stream);
+FORGE_API int forge_slab_exchange_end(forge_slab_comm* c, float* cols, uint64_t ld, uint64_t* n_own_out,
+                                      uint64_t* n_ghost_out, void* stream);
 
 /* Round 2 (after density): every ghost receives its owner's density in
  * rho[] (indexed like the columns). No host synchronisation. */

@@ -90,7 +90,7 @@ def test_slab_classify_and_compact_match_torch(cuda, n):
     x = (torch_.rand(n, generator=g) * 1.2 - 0.1).cuda()
     cfg = _cfg()
     be = slab.GpuBackend(forge_sph, cfg, max(n, 1), 0)
-    for flags in (1, 2, 3, 5, 6, 7):
+    for flags in (1, 2, 3, 5, 6, 7, 13, 14, 15):
         got = be.classify(x, n, 0.25, 0.75, 0.05, flags)
         want = slab.torch_classify(x, n, 0.25, 0.75, 0.05, flags)
         for a, b in zip(got, want):

@@ -322,3 +322,69 @@ def test_fused_epilogue_ops_vs_oracle(cuda):
     d = np.sqrt((po[0] - 0.5) ** 2 + (po[1] - 0.4) ** 2 + (po[2] - 0.5) ** 2)
     assert (np.abs(d - 0.15) < 1e-5).sum() > 0, "no particle was pushed onto the sphere"
     assert (po[1] == np.float32(0.05)).sum() > 0, "no particle hit the ground plane"
+
+
+def _force_step_run(torch, cfg, pos, vel, n_update, zones):
+    """forge_sph_density + forge_sph_force_step (zones None) or the split
+    forge_sph_force_step_zone calls (zones = [(mode, inner_lo, inner_hi,
+    guard_lo, guard_hi), ...])."""
+    L = forge_sph.lib()
+    sp, _ = make_step(cfg)
+    g = forge_sph.HashGrid(cfg.cell_size, cfg.dims, (0, 0, 0), cfg.n, 0)
+    p, v = [dev(torch, x) for x in pos], [dev(torch, x) for x in vel]
+    rho = torch.empty(cfg.n, dtype=torch.float32, device="cuda")
+    forge_sph.check(L.forge_sph_density(g.handle, ctypes.byref(gparams(cfg)), *(x.data_ptr() for x in p), cfg.n,
+                                        rho.data_ptr(), None))
+    args = [x.data_ptr() for x in p + v] + [rho.data_ptr(), cfg.n, n_update]
+    if zones is None:
+        forge_sph.check(L.forge_sph_force_step(g.handle, ctypes.byref(gparams(cfg)), ctypes.byref(sp), *args, None))
+    else:
+        for z in zones:
+            forge_sph.check(L.forge_sph_force_step_zone(g.handle, ctypes.byref(gparams(cfg)), ctypes.byref(sp), *args,
+                                                        ctypes.byref(forge_sph.ForceZone(*z)), None))
+    return g, [host_f32(t) for t in p + v]
+
+
+@pytest.mark.parametrize("name", ["ref65k", "dambreak65k"])
+def test_zoned_force_step_equals_whole_pass(cuda, name):
+    """Boundary zone then interior zone (the split a sharded step overlaps
+    its exchange with) updates every particle exactly once and equals the
+    single forge_sph_force_step bit for bit, ghosts (i >= n_update) untouched;
+    covers both force kernels (pair and single-particle)."""
+    cfg = workloads.config(name)
+    pos, vel = workloads.particles(cfg)
+    n_upd = cfg.n - 1000
+    zones = (0.31, 0.59, 0.25, 0.65)  # interior: x-slices 50..93 (cs/4 = 0.00625 wide) inside [0.31, 0.59)
+    g0, want = _force_step_run(cuda, cfg, pos, vel, n_upd, None)
+    g1, got = _force_step_run(cuda, cfg, pos, vel, n_upd, [(1,) + zones, (2,) + zones])
+    g1.check()
+    for a, b in zip(got, want):
+        assert np.array_equal(a, b)
+    for a, b in zip(got, pos + vel):
+        assert np.array_equal(a[n_upd:], b[n_upd:])
+    # the boundary pass alone leaves the interior particles as they were
+    _, half = _force_step_run(cuda, cfg, pos, vel, n_upd, [(1,) + zones])
+    fx = pos[0] / np.float32(cfg.cell_size)  # the kernels' slice of x: cell * 4 + floor(4 * frac)
+    cx = np.clip(np.floor(fx), 0, cfg.dims[0] - 1)
+    k = cx * 4 + np.clip(np.floor((fx - cx.astype(np.float32)) * np.float32(4)), 0, 3)
+    inner = (k >= 50) & (k < 94)
+    inner[n_upd:] = False
+    assert inner.sum() > 1000
+    outer = ~inner
+    outer[n_upd:] = False
+    for a, b, c in zip(half, pos + vel, want):
+        assert np.array_equal(a[inner], b[inner])
+        assert np.array_equal(a[outer], c[outer])
+
+
+def test_zoned_force_step_guard_and_order(cuda):
+    """An interior particle that ends outside [guard_lo, guard_hi) sets
+    FORGE_DEV_ZONE (reported by forge_grid_check); an interior pass without a
+    boundary pass of the same build is refused."""
+    cfg = workloads.config("ref65k")
+    pos, vel = workloads.particles(cfg)
+    g, _ = _force_step_run(cuda, cfg, pos, vel, cfg.n, [(1, 0.3, 0.6, 0.25, 0.65), (2, 0.3, 0.6, 0.45, 0.46)])
+    with pytest.raises(forge_sph.ForgeError, match="0x8"):
+        g.check()
+    with pytest.raises(forge_sph.ForgeError, match="interior pass must follow"):
+        _force_step_run(cuda, cfg, pos, vel, cfg.n, [(2, 0.3, 0.6, 0.25, 0.65)])
