@@ -343,7 +343,7 @@ def run_sharded(args, torch, dist, rank, world, local):
     for (a, ea), (b, eb) in zip(ev[:-1], ev[1:]):
         if b != "start":
             phase_ms[b] = phase_ms.get(b, 0.0) + ea.elapsed_time(eb) / 3
-    side_ms = {}  # overlapped exchange: side-stream progress after the density round
+    side_ms = {}  # overlapped rounds: side-stream progress after the prepare step
     for name, e, ref in run.timing_side:
         side_ms[name] = side_ms.get(name, 0.0) + ref.elapsed_time(e) / 3
     run.timing = None
@@ -393,7 +393,7 @@ def run_sharded(args, torch, dist, rank, world, local):
                            "inputs_exceed_l2": True, "parallelism": f"x-slab over {world} GPUs (NCCL send/recv, exchange={args.comm})",
                            "max_halo_particles_per_rank": halo},
                 "phases_ms_max_over_ranks": phase_ms,
-                "overlap_ms_after_ghost_rho_max_over_ranks": side_ms,
+                "overlap_ms_after_prepare_max_over_ranks": side_ms,
                 "e2e": {"value": cfg.n * e2e_steps / (e2e_ms / 1e3), "unit": "particle-steps/s",
                         "h2d_bytes_per_step": tot_bytes, "d2h_bytes_per_step": tot_bytes},
                 "gpu_launches": sharded_kernels_per_step(cfg) * args.steps * world,

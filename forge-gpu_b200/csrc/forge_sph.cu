@@ -394,7 +394,7 @@ struct forge_grid {
     uint32_t* sorted_idx = nullptr;
     uint64_t n = 0;
     bool built = false;
-    bool force_gathered = false;  // a zone-1 force pass gathered velocities + density of this build
+    bool force_gathered = false;  // a zone prepare step gathered velocities + density of this build
     // Zone lists of a zoned force pass (allocated by the first one).
     uint32_t* zone_idx = nullptr;     // [A (empty) | boundary | interior] sorted positions, max_n
     uint32_t* zone_tiles = nullptr;   // classification tile counts
@@ -804,38 +804,49 @@ int force_step_impl(const char* fn, forge_grid* g, const forge_sph_params* p, co
                          fn, (unsigned long long)n, (unsigned long long)g->n);
     if (n_update > n) return set_error(FORGE_ERR_INVALID_ARG, "%s: n_update > n", fn);
     const uint32_t mode = zone ? zone->mode : 0u;
-    if (mode > FORGE_ZONE_INTERIOR) return set_error(FORGE_ERR_INVALID_ARG, "%s: bad zone mode %u", fn, mode);
+    if (mode > FORGE_ZONE_PREPARE) return set_error(FORGE_ERR_INVALID_ARG, "%s: bad zone mode %u", fn, mode);
     if (mode == FORGE_ZONE_INTERIOR && !g->force_gathered)
-        return set_error(FORGE_ERR_INVALID_ARG, "%s: an interior pass must follow a boundary pass of the same build",
-                         fn);
+        return set_error(FORGE_ERR_INVALID_ARG,
+                         "%s: an interior pass must follow a prepare or boundary pass of the same build", fn);
     if (n == 0) return FORGE_OK;
     if (!px || !py || !pz || !vx || !vy || !vz || !density)
         return set_error(FORGE_ERR_INVALID_ARG, "%s: NULL array", fn);
     FORGE_DEVICE_SCOPE(g->device);
     const sph::SphConsts c = make_consts(p);
-    // The interior pass reuses the boundary pass's cell-ordered velocities:
-    // the boundary particles' velocities have been updated in place since.
-    if (mode != FORGE_ZONE_INTERIOR) {
-        sph::gather_vel_rho_kernel<<<grid_blocks(n, 256), 256, 0, st>>>(g->sorted_idx, (uint32_t)n, vx, vy, vz,
-                                                                        density, c, g->vel4, g->aux);
-        FORGE_LAUNCHED();
-    }
-    g->force_gathered = mode == FORGE_ZONE_BOUNDARY;
     sph::ForceOut o{vx, vy, vz, nullptr, nullptr, nullptr, px, py, pz, (uint32_t)n_update};
     if (!mode) {
+        sph::gather_vel_rho_kernel<<<grid_blocks(n, 256), 256, 0, st>>>(g->sorted_idx, (uint32_t)n, vx, vy, vz,
+                                                                        density, c, g->vel4, g->aux);
+        g->force_gathered = false;
         launch_force_t<3, 1>(g, c, epi_of(sp), o, st);
         FORGE_LAUNCHED();
         return FORGE_OK;
     }
     int rc;
-    if (mode == FORGE_ZONE_BOUNDARY) {
+    const bool prepared = g->force_gathered;
+    if (mode == FORGE_ZONE_PREPARE || (mode == FORGE_ZONE_BOUNDARY && !prepared)) {
+        // cell-ordered velocities + density, both zone lists: what the two
+        // zones' kernels read (the boundary particles' columns are updated
+        // in place afterwards, so this is done once per build)
+        sph::gather_vel_rho_kernel<<<grid_blocks(n, 256), 256, 0, st>>>(g->sorted_idx, (uint32_t)n, vx, vy, vz,
+                                                                        density, c, g->vel4, g->aux);
+        FORGE_LAUNCHED();
         if ((rc = zone_setup(g)) != FORGE_OK) return rc;
         if ((rc = zone_classify(g, zone->inner_lo, zone->inner_hi, st)) != FORGE_OK) return rc;
         FORGE_CUDA(cudaEventRecord(g->ev_zone, st));
+        g->force_gathered = true;
+        if (mode == FORGE_ZONE_PREPARE) return FORGE_OK;
     } else {
-        // the interior pass needs the gather and the lists, not the boundary
-        // kernel: on another stream the two passes run concurrently
+        // the zone passes need the gather and the lists, not each other: on
+        // two streams their kernels run concurrently
         FORGE_CUDA(cudaStreamWaitEvent(st, g->ev_zone, 0));
+        if (mode == FORGE_ZONE_BOUNDARY && n_update < n) {
+            // ghost densities may have arrived since the prepare pass
+            sph::ghost_rho_kernel<<<grid_blocks(n, 256), 256, 0, st>>>(g->sorted_idx, (uint32_t)n,
+                                                                       (uint32_t)n_update, density, c, g->vel4,
+                                                                       g->aux);
+            FORGE_LAUNCHED();
+        }
     }
     o.zone = mode;
     o.glo = zone->guard_lo;

@@ -258,6 +258,22 @@ __global__ void __launch_bounds__(256)
     aux[s] = a;
 }
 
+// Re-derives 1/rho, p/rho and rho of the ghosts (original index >= limit)
+// from density[] after their owners' values arrived.
+__global__ void __launch_bounds__(256)
+    ghost_rho_kernel(const uint32_t* __restrict__ svals, uint32_t n, uint32_t limit, const float* __restrict__ rho,
+                     SphConsts c, float4* __restrict__ vel4, float2* __restrict__ aux) {
+    const uint32_t s = blockIdx.x * blockDim.x + threadIdx.x;
+    if (s >= n) return;
+    const uint32_t i = svals[s];
+    if (i < limit) return;
+    float inv_rho;
+    float2 a;
+    density_derived(rho[i], c, inv_rho, a);
+    vel4[s].w = inv_rho;
+    aux[s] = a;
+}
+
 // ---------------------------------------------------------------------------
 // Force pass. TERMS: 1 pressure, 2 viscosity, 3 both (fused). Jacobi: all
 // neighbour data come from the cell-ordered snapshot (pos4, vel4, aux), so

@@ -70,7 +70,7 @@ EXPORTED = (
     "forge_nccl_unique_id", "forge_slab_comm_create", "forge_slab_comm_destroy", "forge_slab_exchange",
     "forge_slab_exchange_rho", "forge_sph_force_step_zone", "forge_slab_exchange_begin", "forge_slab_exchange_end",
 )
-ZONE_BOUNDARY, ZONE_INTERIOR = 1, 2
+ZONE_BOUNDARY, ZONE_INTERIOR, ZONE_PREPARE = 1, 2, 3
 STATIC_SORT_MAX_N = 1 << 20
 
 

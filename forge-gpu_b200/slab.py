@@ -302,12 +302,13 @@ class SlabRun:
             self.timing.append((name, ev))
 
     def _mark_side(self, name):
-        """Event on the current (side) stream, timed from the step's last
-        main-stream mark (the overlapped exchange's progress)."""
+        """Event on the current (side) stream, timed from the step's
+        "prepare" mark on the main stream (the overlapped rounds' progress)."""
         if self.timing is not None:
             ev = torch.cuda.Event(enable_timing=True)
             ev.record()
-            self.timing_side.append((name, ev, self.timing[-1][1]))
+            ref = next(e for k, e in reversed(self.timing) if k == "prepare")
+            self.timing_side.append((name, ev, ref))
 
     @property
     def capacity(self) -> int:
@@ -334,6 +335,9 @@ class SlabRun:
             raise RuntimeError(f"slab rank {self.geo.rank}: {n} particles exceed capacity {self.capacity}")
 
     def step(self) -> None:
+        if getattr(self.comm, "split", False) and not self.order_by_id:
+            self._step_overlapped()
+            return
         C = self.cols
         self._mark("start")
         n_own, n = self.n, self.n + self.ng
@@ -355,32 +359,15 @@ class SlabRun:
             C[:, :n] = C[:, perm]
         n_upd = n if perm is not None else n_own
         cols6 = [C[k, :n] for k in range(6)]
-        if getattr(self.comm, "split", False):
+        if getattr(self.comm, "split", False):  # the zoned pass and split round 1, in sequence
             zones = self.geo.force_zones(self.reach)
-            if perm is None:
-                # boundary zone on a high-priority stream, round 1 starting
-                # as soon as it is done, while the interior zone runs on the
-                # main stream alongside both
-                main = torch.cuda.current_stream()
-                if self._hp is None:
-                    self._hp = torch.cuda.Stream(device=main.device, priority=-1)
-                self._hp.wait_stream(main)
-                with torch.cuda.stream(self._hp):
-                    self.backend.force_step(cols6, rho, n, n_upd, zone=(1,) + zones)
-                    self._mark_side("boundary_done")
-                    self.comm.exchange_begin()
-                    self._mark_side("counts_done")
-                self.backend.force_step(cols6, rho, n, n_upd, zone=(2,) + zones)
-            else:
-                self.backend.force_step(cols6, rho, n, n_upd, zone=(1,) + zones)
-                self.backend.force_step(cols6, rho, n, n_upd, zone=(2,) + zones)
+            self.backend.force_step(cols6, rho, n, n_upd, zone=(1,) + zones)
+            self.backend.force_step(cols6, rho, n, n_upd, zone=(2,) + zones)
+            if perm is not None:
                 C[:, perm] = C[:, :n].clone()
-                self.comm.exchange_begin()
             self._mark("force")
-            self.comm.exchange_end()  # the main stream waits for the payload, which followed the boundary zone
-            if perm is None:
-                with torch.cuda.stream(self._hp):
-                    self._mark_side("payload_done")
+            self.comm.exchange_begin()
+            self.comm.exchange_end()
         else:
             self.backend.force_step(cols6, rho, n, n_upd)
             if perm is not None:
@@ -388,6 +375,44 @@ class SlabRun:
             self._mark("force")
             self.comm.exchange(migrate=True)
         self._mark("exchange")
+
+    def _step_overlapped(self) -> None:
+        """The step with both exchange rounds off the critical path.
+
+        main stream:  density -> prepare (gather, zone lists) -> interior
+                      force -> [wait payload] finish round 1
+        side stream (high priority), after prepare: density round -> ghost
+                      densities re-read -> boundary force -> round 1 begin
+                      (selection, counts) -> payload (enqueued by the finish)
+        Interior particles have no ghost neighbours and are not in any
+        exchange list, so the interior force overlaps both rounds."""
+        C = self.cols
+        self._mark("start")
+        n_own, n = self.n, self.n + self.ng
+        rho = self.backend.density([C[k, :n] for k in range(3)], n)
+        self._mark("density")
+        cols6 = [C[k, :n] for k in range(6)]
+        zones = self.geo.force_zones(self.reach)
+        self.backend.force_step(cols6, rho, n, n_own, zone=(3,) + zones)
+        self._mark("prepare")
+        main = torch.cuda.current_stream()
+        if self._hp is None:
+            self._hp = torch.cuda.Stream(device=main.device, priority=-1)
+        self._hp.wait_stream(main)
+        with torch.cuda.stream(self._hp):
+            self.comm.exchange_rho(rho)
+            self._mark_side("ghost_rho_done")
+            self.backend.force_step(cols6, rho, n, n_own, zone=(1,) + zones)
+            self._mark_side("boundary_done")
+            self.comm.exchange_begin()
+            self._mark_side("counts_done")
+        self.backend.force_step(cols6, rho, n, n_own, zone=(2,) + zones)
+        self._mark("force")
+        self.comm.exchange_end()  # the main stream waits for the payload, which followed the boundary zone
+        with torch.cuda.stream(self._hp):
+            self._mark_side("payload_done")
+        self._mark("exchange")
+        rho.record_stream(self._hp)
 
 
 def torch_classify(x, n, lo, hi, reach, flags):

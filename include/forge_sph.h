@@ -296,25 +296,32 @@ FORGE_API int forge_sph_force_step(forge_grid* g, const forge_sph_params* p, con
                                    const float* density, uint64_t n, uint64_t n_update, void* stream);
 
 /* Split form of forge_sph_force_step for overlapping the slab exchange with
- * the force pass. The owned particles (i < n_update) are split by grid cell:
- * the interior zone is the cells whose x-extent lies inside
- * [inner_lo, inner_hi) (+-inf for an open side), the boundary zone the other
- * cells. Call once with FORGE_ZONE_BOUNDARY (gathers velocities + density,
- * lists both zones, updates the boundary particles), then, on the same grid
- * build, once with FORGE_ZONE_INTERIOR (updates the rest from the same
- * gathered state). The two calls together equal one forge_sph_force_step bit
- * for bit. The interior call waits, on its own stream, only for the boundary
- * call's gather and lists, so the two force kernels may run concurrently
- * when the calls use two streams; once the boundary call's work on its
- * stream is done the boundary particles' columns are final and may be read
- * (e.g. by forge_slab_exchange_begin enqueued on that stream). An interior
- * particle whose x before or after the step lies outside
- * [guard_lo, guard_hi) sets FORGE_DEV_ZONE in the grid's status
+ * the force pass. The owned particles (i < n_update) are split by grid cell
+ * x-slice: the interior zone is the slices whose x-extent lies inside
+ * [inner_lo, inner_hi) (+-inf for an open side), the boundary zone the rest.
+ * Modes, on one grid build:
+ *   FORGE_ZONE_PREPARE   gather velocities + density in cell order, list
+ *                        both zones (no force kernel);
+ *   FORGE_ZONE_BOUNDARY  update the boundary particles (preceded by the
+ *                        prepare step if none ran; else it first re-reads
+ *                        the ghosts' densities, i >= n_update, which may
+ *                        have arrived since);
+ *   FORGE_ZONE_INTERIOR  update the interior particles (needs a prepare or
+ *                        boundary call before it).
+ * BOUNDARY + INTERIOR equal one forge_sph_force_step bit for bit. Each zone
+ * call waits, on its own stream, only for the prepare step, so the two
+ * zones' kernels may run concurrently on two streams; interior particles
+ * have no ghost neighbours, so the interior pass may also run before the
+ * ghost densities arrive. Once a boundary call's work is done its particles'
+ * columns are final and may be read (e.g. by forge_slab_exchange_begin
+ * enqueued after it). An interior particle whose x before or after the step
+ * lies outside [guard_lo, guard_hi) sets FORGE_DEV_ZONE in the grid's status
  * (forge_grid_check): it is, or moved, too close to a face for the
- * overlapped exchange to classify it safely. The first boundary call on a
- * grid allocates its zone lists (4 bytes per particle). */
+ * overlapped exchange to classify it safely. The first prepare on a grid
+ * allocates its zone lists (4 bytes per particle). */
 #define FORGE_ZONE_BOUNDARY 1u
 #define FORGE_ZONE_INTERIOR 2u
+#define FORGE_ZONE_PREPARE 3u
 typedef struct forge_force_zone {
     uint32_t mode;
     float inner_lo, inner_hi;

@@ -388,3 +388,52 @@ def test_zoned_force_step_guard_and_order(cuda):
         g.check()
     with pytest.raises(forge_sph.ForgeError, match="interior pass must follow"):
         _force_step_run(cuda, cfg, pos, vel, cfg.n, [(2, 0.3, 0.6, 0.25, 0.65)])
+
+
+def test_zoned_prepare_then_late_ghost_densities(cuda):
+    """The overlapped sharded order: prepare (gather + lists) with stale ghost
+    densities, the ghosts' exact densities written afterwards, then the
+    boundary pass (which re-reads them) and the interior pass on a second
+    stream -- equal to one forge_sph_force_step on the exact densities."""
+    torch = cuda
+    cfg = workloads.config("ref65k")
+    pos, vel = workloads.particles(cfg)
+    n_own = cfg.n - 5000  # the last 5000 play the ghosts
+    L = forge_sph.lib()
+    sp, _ = make_step(cfg)
+    zones = (0.31, 0.59, 0.25, 0.65)
+
+    def run(split):
+        g = forge_sph.HashGrid(cfg.cell_size, cfg.dims, (0, 0, 0), cfg.n, 0)
+        p, v = [dev(torch, x) for x in pos], [dev(torch, x) for x in vel]
+        rho = torch.empty(cfg.n, dtype=torch.float32, device="cuda")
+        forge_sph.check(L.forge_sph_density(g.handle, ctypes.byref(gparams(cfg)), *(x.data_ptr() for x in p), cfg.n,
+                                            rho.data_ptr(), None))
+        args = [x.data_ptr() for x in p + v] + [rho.data_ptr(), cfg.n, n_own]
+        if not split:
+            forge_sph.check(L.forge_sph_force_step(g.handle, ctypes.byref(gparams(cfg)), ctypes.byref(sp), *args,
+                                                   None))
+        else:
+            exact = rho[n_own:].clone()
+            rho[n_own:] *= 1.5  # stale ghost densities at prepare time
+
+            def zone(mode, stream):
+                forge_sph.check(L.forge_sph_force_step_zone(g.handle, ctypes.byref(gparams(cfg)), ctypes.byref(sp),
+                                                            *args, ctypes.byref(forge_sph.ForceZone(mode, *zones)),
+                                                            stream.cuda_stream))
+            main = torch.cuda.current_stream()
+            zone(forge_sph.ZONE_PREPARE, main)
+            side = torch.cuda.Stream(priority=-1)
+            side.wait_stream(main)
+            with torch.cuda.stream(side):
+                rho[n_own:] = exact  # the density round
+                zone(forge_sph.ZONE_BOUNDARY, side)
+            zone(forge_sph.ZONE_INTERIOR, main)
+            main.wait_stream(side)
+        torch.cuda.synchronize()
+        g.check()
+        return [host_f32(t) for t in p + v]
+
+    want, got = run(False), run(True)
+    for a, b in zip(got, want):
+        assert np.array_equal(a, b)
