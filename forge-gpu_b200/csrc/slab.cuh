@@ -160,36 +160,6 @@ __global__ void __launch_bounds__(1024)
 namespace forge {
 namespace slab {
 
-// out[i*rows + r] = cols[r*ld + idx[i]]: columns listed in idx -> row-major
-// records of `rows` floats (the message layout of the slab exchange).
-__global__ void __launch_bounds__(256)
-    pack_kernel(const float* __restrict__ cols, uint64_t ld, uint32_t rows, const uint32_t* __restrict__ idx,
-                uint32_t k, float* __restrict__ out) {
-    const uint32_t t = blockIdx.x * blockDim.x + threadIdx.x;
-    if (t >= k * rows) return;
-    const uint32_t i = t / rows, r = t - i * rows;
-    out[t] = cols[r * ld + idx[i]];
-}
-
-// cols[r*ld + dst + i] = in[i*rows + r] for i < k.
-__global__ void __launch_bounds__(256)
-    unpack_kernel(const float* __restrict__ in, uint32_t k, uint32_t rows, float* __restrict__ cols, uint64_t ld,
-                  uint32_t dst) {
-    const uint32_t t = blockIdx.x * blockDim.x + threadIdx.x;
-    if (t >= k * rows) return;
-    const uint32_t i = t / rows, r = t - i * rows;
-    cols[r * ld + dst + i] = in[t];
-}
-
-// out[i] = rho[list[i]] for i < k1, rho[start + i - k1] for k1 <= i < k1 + k2.
-__global__ void __launch_bounds__(256)
-    rho_pack_kernel(const float* __restrict__ rho, const uint32_t* __restrict__ list, uint32_t k1, uint32_t start,
-                    uint32_t k2, float* __restrict__ out) {
-    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < k1) out[i] = rho[list[i]];
-    else if (i < k1 + k2) out[i] = rho[start + i - k1];
-}
-
 }  // namespace slab
 }  // namespace forge
 
@@ -217,11 +187,10 @@ __global__ void __launch_bounds__(256)
 // Column indices taken before compact_kernel(gone, k) -> after it: an index
 // t >= keep = n - k (t not in gone) is the r-th surviving tail column, r =
 // (t - keep) - |gone in [keep, t)|, and moved to the r-th hole gone[r].
-// k is read from *k_dev; cnt from *cnt_dev when set.
+// Remaps lists a (na entries) and b (nb) in place; k is read from *k_dev.
 __global__ void __launch_bounds__(256)
-    remap_after_compact_kernel(uint32_t* __restrict__ idx, uint32_t cnt, const uint32_t* __restrict__ cnt_dev,
+    remap_after_compact_kernel(uint32_t* __restrict__ a, uint32_t na, uint32_t* __restrict__ b, uint32_t nb,
                                uint32_t n, const uint32_t* __restrict__ gone, const uint32_t* __restrict__ k_dev) {
-    if (cnt_dev) cnt = *cnt_dev;
     const uint32_t k = *k_dev, keep = n - k;
     auto lower = [&](uint32_t v) {  // |{gone[j] < v}|
         uint32_t lo = 0, hi = k;
@@ -232,10 +201,10 @@ __global__ void __launch_bounds__(256)
         }
         return lo;
     };
-    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < cnt; i += gridDim.x * blockDim.x) {
-        const uint32_t t = idx[i];
-        if (t < keep) continue;
-        idx[i] = gone[(t - keep) - (lower(t) - lower(keep))];
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < na + nb; i += gridDim.x * blockDim.x) {
+        uint32_t* p = i < na ? a + i : b + (i - na);
+        const uint32_t t = *p;
+        if (t >= keep) *p = gone[(t - keep) - (lower(t) - lower(keep))];
     }
 }
 
@@ -395,6 +364,65 @@ __global__ void __launch_bounds__(kThreads)
                 for (int r = 0; r < 7; ++r) rec[r] = a.cols[r * a.ld + i];
             ++pos;
         }
+    }
+}
+
+}  // namespace slab
+}  // namespace forge
+
+namespace forge {
+namespace slab {
+
+// Up to six record blocks copied into the column buffer by one launch:
+// block b moves cnt[b] records of 7 floats from src[b] to columns
+// [dst[b], dst[b] + cnt[b]).
+struct UnpackSet {
+    const float* src[6];
+    uint32_t cnt[6];
+    uint32_t dst[6];
+};
+
+__global__ void __launch_bounds__(256)
+    unpack_set_kernel(UnpackSet u, uint32_t total, float* __restrict__ cols, uint64_t ld) {
+    for (uint32_t t = blockIdx.x * blockDim.x + threadIdx.x; t < total * 7; t += gridDim.x * blockDim.x) {
+        uint32_t rec = t / 7, r = t - rec * 7;
+        int b = 0;
+        while (rec >= u.cnt[b]) rec -= u.cnt[b++];  // total = sum(cnt) keeps b < 6
+        cols[r * ld + u.dst[b] + rec] = u.src[b][(size_t)rec * 7 + r];
+    }
+}
+
+// Up to four float blocks scattered by one launch: block b moves cnt[b]
+// values from src[b] to dst[b].
+struct CopySet {
+    const float* src[4];
+    float* dst[4];
+    uint32_t cnt[4];
+};
+
+__global__ void __launch_bounds__(256) copy_set_kernel(CopySet c, uint32_t total) {
+    for (uint32_t t = blockIdx.x * blockDim.x + threadIdx.x; t < total; t += gridDim.x * blockDim.x) {
+        uint32_t k = t;
+        int b = 0;
+        while (k >= c.cnt[b]) k -= c.cnt[b++];
+        c.dst[b][k] = c.src[b][k];
+    }
+}
+
+// Density messages to both neighbours by one launch: to side X, rho of
+// [halo rows sent to X (list), arrivals from X (columns start..)].
+struct RhoPackSet {
+    const uint32_t* list[2];
+    uint32_t k1[2], start[2], k2[2];
+    float* out[2];
+};
+
+__global__ void __launch_bounds__(256) rho_pack_set_kernel(const float* __restrict__ rho, RhoPackSet p) {
+    const uint32_t n0 = p.k1[0] + p.k2[0], n1 = p.k1[1] + p.k2[1];
+    for (uint32_t t = blockIdx.x * blockDim.x + threadIdx.x; t < n0 + n1; t += gridDim.x * blockDim.x) {
+        const int s = t < n0 ? 0 : 1;
+        const uint32_t i = s ? t - n0 : t;
+        p.out[s][i] = i < p.k1[s] ? rho[p.list[s][i]] : rho[p.start[s] + i - p.k1[s]];
     }
 }
 

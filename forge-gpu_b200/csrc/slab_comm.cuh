@@ -130,13 +130,6 @@ void slab_comm_free(forge_slab_comm* c) {
     delete c;
 }
 
-int unpack(const float* in, uint32_t k, float* cols, uint64_t ld, uint32_t dst, cudaStream_t st) {
-    if (!k) return FORGE_OK;
-    slab::unpack_kernel<<<grid_blocks((uint64_t)k * kSlabRows, 256), 256, 0, st>>>(in, k, kSlabRows, cols, ld, dst);
-    FORGE_LAUNCHED();
-    return FORGE_OK;
-}
-
 // Enqueues a classification of x[0, n - *n_sub) into idx/counts (no sync).
 int classify_async(forge_slab_comm* c, const float* x, uint64_t n, const uint32_t* n_sub, uint32_t flags,
                    uint32_t* idx, uint32_t* counts, cudaStream_t st) {
@@ -304,29 +297,29 @@ int send_payload(forge_slab_comm* c, const RoundSizes& z, cudaStream_t st) {
 // the density round.
 int place_arrivals(forge_slab_comm* c, float* cols, uint64_t ld, const RoundSizes& z, uint64_t* n_own_out,
                    uint64_t* n_ghost_out, cudaStream_t st) {
-    int rc;
-    uint32_t o = z.keep;
-    if ((rc = unpack(c->recv_l, (uint32_t)z.aml, cols, ld, o, st)) != FORGE_OK) return rc;
-    c->arr_l = o;
-    c->n_arr_l = (uint32_t)z.aml;
-    o += (uint32_t)z.aml;
-    if ((rc = unpack(c->recv_r, (uint32_t)z.amr, cols, ld, o, st)) != FORGE_OK) return rc;
-    c->arr_r = o;
-    c->n_arr_r = (uint32_t)z.amr;
-    o += (uint32_t)z.amr;
-    c->g_hl = o;
-    c->n_ghl = (uint32_t)z.ahl;
-    if ((rc = unpack(c->recv_l + z.aml * kSlabRows, (uint32_t)z.ahl, cols, ld, o, st)) != FORGE_OK) return rc;
-    o += (uint32_t)z.ahl;
-    c->g_hr = o;
-    c->n_ghr = (uint32_t)z.ahr;
-    if ((rc = unpack(c->recv_r + z.amr * kSlabRows, (uint32_t)z.ahr, cols, ld, o, st)) != FORGE_OK) return rc;
-    o += (uint32_t)z.ahr;
-    c->g_ml = o;
-    if ((rc = unpack(c->send_l, z.ml, cols, ld, o, st)) != FORGE_OK) return rc;
-    o += z.ml;
-    c->g_mr = o;
-    if ((rc = unpack(c->send_r, z.mr, cols, ld, o, st)) != FORGE_OK) return rc;
+    // layout: kept | arrivals from L | from R | ghosts: halo from L | halo
+    // from R | our migrants to L | to R
+    const uint32_t aml = (uint32_t)z.aml, amr = (uint32_t)z.amr, ahl = (uint32_t)z.ahl, ahr = (uint32_t)z.ahr;
+    c->arr_l = z.keep;
+    c->n_arr_l = aml;
+    c->arr_r = c->arr_l + aml;
+    c->n_arr_r = amr;
+    c->g_hl = c->arr_r + amr;
+    c->n_ghl = ahl;
+    c->g_hr = c->g_hl + ahl;
+    c->n_ghr = ahr;
+    c->g_ml = c->g_hr + ahr;
+    c->g_mr = c->g_ml + z.ml;
+    const slab::UnpackSet u{{c->recv_l, c->recv_r, c->recv_l + (size_t)aml * kSlabRows,
+                             c->recv_r + (size_t)amr * kSlabRows, c->send_l, c->send_r},
+                            {aml, amr, ahl, ahr, z.ml, z.mr},
+                            {c->arr_l, c->arr_r, c->g_hl, c->g_hr, c->g_ml, c->g_mr}};
+    const uint32_t total = aml + amr + ahl + ahr + z.ml + z.mr;
+    if (total) {
+        slab::unpack_set_kernel<<<std::min(grid_blocks((uint64_t)total * kSlabRows, 256), (uint32_t)c->sms * 8), 256,
+                                  0, st>>>(u, total, cols, ld);
+        FORGE_LAUNCHED();
+    }
     c->n_hl = z.hl;
     c->n_hr = z.hr;
     c->n_ml = z.ml;
@@ -432,13 +425,9 @@ extern "C" int forge_slab_exchange_end(forge_slab_comm* c, float* cols, uint64_t
     if (n_own - z.keep) {
         uint32_t* cm = c->counts;
         slab::compact_kernel<<<1, 1024, 0, st>>>(cols, ld, kSlabRows, (uint32_t)n_own, c->idx, 0u, cm);
-        const uint32_t gb = (uint32_t)c->sms * 2;
-        if (z.hl)
-            slab::remap_after_compact_kernel<<<std::min(grid_blocks(z.hl, 256), gb), 256, 0, st>>>(
-                c->halo_l, z.hl, nullptr, (uint32_t)n_own, c->idx, cm);
-        if (z.hr)
-            slab::remap_after_compact_kernel<<<std::min(grid_blocks(z.hr, 256), gb), 256, 0, st>>>(
-                c->halo_r, z.hr, nullptr, (uint32_t)n_own, c->idx, cm);
+        if (z.hl + z.hr)
+            slab::remap_after_compact_kernel<<<std::min(grid_blocks(z.hl + z.hr, 256), (uint32_t)c->sms * 2), 256, 0,
+                                               st>>>(c->halo_l, z.hl, c->halo_r, z.hr, (uint32_t)n_own, c->idx, cm);
         FORGE_LAUNCHED();
     }
     return place_arrivals(c, cols, ld, z, n_own_out, n_ghost_out, st);
@@ -451,13 +440,15 @@ extern "C" int forge_slab_exchange_rho(forge_slab_comm* c, float* rho, void* str
     FORGE_DEVICE_SCOPE(c->device);
     cudaStream_t st = as_stream(stream);
     const uint32_t kl = c->n_hl + c->n_arr_l, kr = c->n_hr + c->n_arr_r;
-    if (kl)
-        slab::rho_pack_kernel<<<grid_blocks(kl, 256), 256, 0, st>>>(rho, c->halo_l, c->n_hl, c->arr_l, c->n_arr_l,
-                                                                     c->rho_send_l);
-    if (kr)
-        slab::rho_pack_kernel<<<grid_blocks(kr, 256), 256, 0, st>>>(rho, c->halo_r, c->n_hr, c->arr_r, c->n_arr_r,
-                                                                     c->rho_send_r);
-    FORGE_LAUNCHED();
+    if (kl + kr) {
+        const slab::RhoPackSet pk{{c->halo_l, c->halo_r},
+                                  {c->n_hl, c->n_hr},
+                                  {c->arr_l, c->arr_r},
+                                  {c->n_arr_l, c->n_arr_r},
+                                  {c->rho_send_l, c->rho_send_r}};
+        slab::rho_pack_set_kernel<<<std::min(grid_blocks(kl + kr, 256), (uint32_t)c->sms * 4), 256, 0, st>>>(rho, pk);
+        FORGE_LAUNCHED();
+    }
     // from X: [X's halo rows to us | our migrants to X]
     const uint32_t il = c->n_ghl + c->n_ml, ir = c->n_ghr + c->n_mr;
     FORGE_NCCL(g_nccl.GroupStart());
@@ -470,14 +461,12 @@ extern "C" int forge_slab_exchange_rho(forge_slab_comm* c, float* rho, void* str
         if (ir) FORGE_NCCL(g_nccl.Recv(c->rho_recv_r, ir, ncclFloat32, c->right, c->comm, st));
     }
     FORGE_NCCL(g_nccl.GroupEnd());
-    auto d2d = [&](float* dst, const float* src, uint32_t k) -> int {
-        if (k) FORGE_CUDA(cudaMemcpyAsync(dst, src, k * sizeof(float), cudaMemcpyDeviceToDevice, st));
-        return FORGE_OK;
-    };
-    int rc;
-    if ((rc = d2d(rho + c->g_hl, c->rho_recv_l, c->n_ghl)) != FORGE_OK) return rc;
-    if ((rc = d2d(rho + c->g_ml, c->rho_recv_l + c->n_ghl, c->n_ml)) != FORGE_OK) return rc;
-    if ((rc = d2d(rho + c->g_hr, c->rho_recv_r, c->n_ghr)) != FORGE_OK) return rc;
-    if ((rc = d2d(rho + c->g_mr, c->rho_recv_r + c->n_ghr, c->n_mr)) != FORGE_OK) return rc;
+    if (il + ir) {
+        const slab::CopySet cp{{c->rho_recv_l, c->rho_recv_l + c->n_ghl, c->rho_recv_r, c->rho_recv_r + c->n_ghr},
+                               {rho + c->g_hl, rho + c->g_ml, rho + c->g_hr, rho + c->g_mr},
+                               {c->n_ghl, c->n_ml, c->n_ghr, c->n_mr}};
+        slab::copy_set_kernel<<<std::min(grid_blocks(il + ir, 256), (uint32_t)c->sms * 4), 256, 0, st>>>(cp, il + ir);
+        FORGE_LAUNCHED();
+    }
     return FORGE_OK;
 }
