@@ -166,6 +166,31 @@ def time_steps(torch, fn, steps):
     return s.elapsed_time(e)
 
 
+def time_steps_flushed(torch, fn, steps):
+    """Device time of `steps` calls of fn, each preceded (outside its timed
+    span) by a 256 MB write that evicts the 126 MB L2: for workloads whose
+    state fits in L2."""
+    junk = torch.empty(64 << 20, dtype=torch.float32, device="cuda")
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    torch.cuda.synchronize()
+    for s, e in ev:
+        junk.fill_(1.0)
+        s.record()
+        fn()
+        e.record()
+    torch.cuda.synchronize()
+    return sum(s.elapsed_time(e) for s, e in ev)
+
+
+L2_BYTES = 126e6
+
+
+def state_bytes(cfg):
+    """Per-step device state the SPH step touches: caller SoA arrays (28 B) +
+    the grid's cell-ordered copies, keys, indices and sort buffers (~68 B)."""
+    return cfg.n * 96
+
+
 def max_over_ranks(torch, dist, v):
     if dist is None:
         return v
@@ -186,7 +211,8 @@ def run_sph_single(torch, forge_sph, cfg, steps, warmup, rank_dev, clocks=True):
     if clocks:
         ck.start()
         time.sleep(0.3)
-    ms = time_steps(torch, run.step, steps)
+    flush = state_bytes(cfg) < 2 * L2_BYTES
+    ms = (time_steps_flushed if flush else time_steps)(torch, run.step, steps)
     clk = ck.stop() if clocks else None
     run.grid.check()
     buf = (ctypes.c_float * (4 * steps))()
@@ -195,6 +221,7 @@ def run_sph_single(torch, forge_sph, cfg, steps, warmup, rank_dev, clocks=True):
     ph = np.array(buf[:4 * got.value], np.float64).reshape(-1, 4)
     forge_sph.check(L.forge_grid_profile_enable(run.grid.handle, 0))
     phase_ms = {k: float(ph[:, i].mean()) for i, k in enumerate(PHASES)}
+    run.l2_flushed = flush
     return run, ms, phase_ms, clk, pos, vel
 
 
@@ -278,7 +305,8 @@ def cpu_threads():
     return oracle.max_threads()
 
 
-CPU_SAMPLE = {"sharded16m": 1_024_000, "dambreak1m": 131_072, "blobs4m": 262_144, "ref65k": 65_536}
+CPU_SAMPLE = {"sharded16m": 1_024_000, "dambreak1m": 262_144, "dambreak1m_h025": 131_072, "blobs4m": 262_144,
+              "ref65k": 65_536}
 
 
 def reference_arm(args, rank, world):
@@ -408,7 +436,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="sharded16m",
-                    choices=["sharded16m", "dambreak1m", "dambreak65k", "blobs4m", "ref65k"])
+                    choices=["sharded16m", "dambreak1m", "dambreak1m_h025", "dambreak65k", "blobs4m", "ref65k"])
     ap.add_argument("--no-extra", action="store_true", help="skip the 1M dam-break and 2^28 sort extras")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
     ap.add_argument("--comm", choices=["nccl", "torch"], default="nccl",
@@ -437,6 +465,7 @@ def main():
     cfg = workloads.config(args.workload)
     hbm, peak_kind = peaks()
     run, ms, phase_ms, clk, pos, vel = run_sph_single(torch, forge_sph, cfg, args.steps, args.warmup, local)
+    flushed = run.l2_flushed
     ms_step = ms / args.steps
     value = cfg.n / (ms_step / 1e3)
     ab = alg_bytes(cfg)
@@ -456,7 +485,8 @@ def main():
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": cfg.name, "particles": cfg.n, "cells": cfg.cells, "h": cfg.h,
-                       "key_bits": cfg.key_bits, "inputs_exceed_l2": cfg.n * 24 > 126e6,
+                       "key_bits": cfg.key_bits, "inputs_exceed_l2": state_bytes(cfg) >= 2 * L2_BYTES,
+                       "l2_flushed_between_steps": flushed,
                        "parallelism": "single GPU"},
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm, "unit": "GB/s",
                          "frac": achieved / hbm, "traffic": traffic, "peak_kind": peak_kind},
@@ -477,9 +507,17 @@ def main():
         extra = {}
         c1 = workloads.config("dambreak1m")
         r1, ms1, ph1, _, _, _ = run_sph_single(torch, forge_sph, c1, 50, 5, local, clocks=False)
-        del r1
         extra["dambreak1m"] = {"value": c1.n / (ms1 / 50 / 1e3), "unit": "particle-steps/s",
-                               "ms_per_step": ms1 / 50, "phases_ms": ph1}
+                               "ms_per_step": ms1 / 50, "phases_ms": ph1, "l2_flushed_between_steps": r1.l2_flushed,
+                               "h": c1.h, "particles_per_cell": 8}
+        del r1
+        torch.cuda.empty_cache()
+        c2 = workloads.config("dambreak1m_h025")
+        r2, ms2, ph2, _, _, _ = run_sph_single(torch, forge_sph, c2, 20, 3, local, clocks=False)
+        extra["dambreak1m_h025"] = {"value": c2.n / (ms2 / 20 / 1e3), "unit": "particle-steps/s",
+                                    "ms_per_step": ms2 / 20, "phases_ms": ph2,
+                                    "l2_flushed_between_steps": r2.l2_flushed, "h": c2.h, "particles_per_cell": 125}
+        del r2
         torch.cuda.empty_cache()
         for kind in ("uniform", "morton"):
             extra["radix_sort_2^28_" + kind] = sort_rate(torch, forge_sph, kind, 1 << 28)

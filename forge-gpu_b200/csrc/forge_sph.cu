@@ -382,6 +382,7 @@ struct forge_grid {
     uint32_t* kc = nullptr;
     uint32_t* vc = nullptr;
     uint32_t* cell_start = nullptr;  // (C << kSphSubBits) + 1
+    uint32_t* chunk_val = nullptr;   // marks of whole table chunks to fill (grid::kFillChunk entries each)
     uint32_t sub_bits = 0;           // x-slices of the last build (0: plain cells)
     float4* pos4 = nullptr;          // cell-ordered (x, y, z, key)
     float4* vel4 = nullptr;          // cell-ordered (vx, vy, vz, 1/rho)
@@ -453,6 +454,9 @@ extern "C" int forge_grid_create(float cell_size, uint32_t nx, uint32_t ny, uint
     bool ok = dalloc(&g->cell_idx, m) == cudaSuccess && dalloc(&g->kb, m) == cudaSuccess &&
               dalloc(&g->vb, m) == cudaSuccess && dalloc(&g->kc, m) == cudaSuccess &&
               dalloc(&g->vc, m) == cudaSuccess && dalloc(&g->cell_start, (C << kSphSubBits) + 1) == cudaSuccess &&
+              dalloc(&g->chunk_val, (C << kSphSubBits) / grid::kFillChunk + 1) == cudaSuccess &&
+              cudaMemset(g->chunk_val, 0xff, ((C << kSphSubBits) / grid::kFillChunk + 1) * sizeof(uint32_t)) ==
+                  cudaSuccess &&
               dalloc(&g->pos4, m) == cudaSuccess && dalloc(&g->vel4, m) == cudaSuccess &&
               dalloc(&g->aux, m) == cudaSuccess &&
               dalloc(&g->scan_sums, m / grid::kScanTile + 1) == cudaSuccess &&
@@ -477,6 +481,7 @@ extern "C" void forge_grid_destroy(forge_grid* g) {
     cudaFree(g->kc);
     cudaFree(g->vc);
     cudaFree(g->cell_start);
+    cudaFree(g->chunk_val);
     cudaFree(g->pos4);
     cudaFree(g->vel4);
     cudaFree(g->aux);
@@ -520,9 +525,14 @@ int grid_build_impl(forge_grid* g, const float* px, const float* py, const float
     }
     prof_mark(g, 1, st);
     grid::GatherSrc gs{px, py, pz, stride, vx, vy, vz};
+    const uint32_t table = g->C << sub_bits;  // entries [0, table]
     grid::cell_start_gather_kernel<<<grid_blocks(n + 1, 256), 256, 0, st>>>(
-        g->sorted_keys, g->sorted_idx, nn, g->C << sub_bits, g->cell_start, gs, gather_pos ? g->pos4 : nullptr,
-        (gather_pos && vx) ? g->vel4 : nullptr);
+        g->sorted_keys, g->sorted_idx, nn, table, g->cell_start, gs, gather_pos ? g->pos4 : nullptr,
+        (gather_pos && vx) ? g->vel4 : nullptr, g->chunk_val);
+    const uint32_t chunks = table / grid::kFillChunk;  // whole chunks below entry `table`
+    if (chunks)
+        grid::fill_chunks_kernel<<<std::min(chunks, (uint32_t)g->scratch.sms * 8u), 256, 0, st>>>(g->cell_start,
+                                                                                                g->chunk_val, chunks);
     FORGE_LAUNCHED();
     prof_mark(g, 2, st);
     g->n = n;

@@ -89,8 +89,14 @@ __device__ __forceinline__ void warp_fill_runs(uint32_t* __restrict__ table, int
 
 // cell_start[c] = first sorted position whose key >= c, for c in [0, C],
 // so cell_start[C] == n (sph_fused.rs:280-390 without the scan or memsets).
-// Thread s in [0, n] owns the cells (key[s-1], key[s]]: each entry is
-// written exactly once, so the table needs no clearing.
+// Thread s in [0, n] owns the cells (key[s-1], key[s]]. A run longer than
+// two chunks of kFillChunk entries (a large empty region: the space around
+// a dam-break column, the cells past the last particle) is not written by
+// one warp: the thread writes its partial first chunk and the chunk holding
+// key[s], and marks the whole chunks between them in chunk_val[] for
+// fill_chunks_kernel, which writes them one block per chunk. Entries are
+// written once, except that whole chunks of a run may be written twice with
+// the same value; the table needs no clearing.
 // Optionally gathers positions (and velocities) into cell order:
 //   pos4[s] = (x, y, z, bits(key)), vel4[s] = (vx, vy, vz, 0).
 struct GatherSrc {
@@ -103,10 +109,13 @@ struct GatherSrc {
     const float* __restrict__ vz;
 };
 
+constexpr uint32_t kFillChunk = 1024;
+constexpr uint32_t kChunkFree = 0xffffffffu;  // chunk_val: not marked
+
 __global__ void __launch_bounds__(256)
     cell_start_gather_kernel(const uint32_t* __restrict__ skeys, const uint32_t* __restrict__ svals,
                              uint32_t n, uint32_t C, uint32_t* __restrict__ cell_start, GatherSrc src,
-                             float4* __restrict__ pos4, float4* __restrict__ vel4) {
+                             float4* __restrict__ pos4, float4* __restrict__ vel4, uint32_t* __restrict__ chunk_val) {
     const uint32_t s = blockIdx.x * blockDim.x + threadIdx.x;
     int64_t a = 1, b = 0;  // empty
     uint32_t key = 0;
@@ -115,12 +124,37 @@ __global__ void __launch_bounds__(256)
         a = (s == 0) ? 0 : (int64_t)skeys[s - 1] + 1;
         b = (s == n) ? (int64_t)C : (int64_t)key;
     }
+    constexpr int64_t K = kFillChunk;
+    int64_t a2 = 1, b2 = 0, ca = 1, cb = 0;  // second piece; whole chunks [ca, cb]
+    if (b - a + 1 > 2 * K) {
+        ca = (a + K - 1) / K;   // first whole chunk
+        cb = b / K - 1;         // last whole chunk before the one holding b
+        a2 = (b / K) * K;
+        b2 = b;
+        b = ca * K - 1;
+    }
     warp_fill_runs(cell_start, a, b, s);
+    warp_fill_runs(cell_start, a2, b2, s);
+    warp_fill_runs(chunk_val, ca, cb, s);
     if (s < n && pos4 != nullptr) {
         const uint32_t i = svals[s];
         const size_t o = (size_t)i * src.stride;
         pos4[s] = make_float4(src.px[o], src.py[o], src.pz[o], __uint_as_float(key));
         if (vel4 != nullptr) vel4[s] = make_float4(src.vx[i], src.vy[i], src.vz[i], 0.f);
+    }
+}
+
+// Whole chunks marked by cell_start_gather_kernel: block per chunk (grid-
+// stride), marks cleared for the next build.
+__global__ void __launch_bounds__(256)
+    fill_chunks_kernel(uint32_t* __restrict__ cell_start, uint32_t* __restrict__ chunk_val, uint32_t chunks) {
+    for (uint32_t k = blockIdx.x; k < chunks; k += gridDim.x) {
+        const uint32_t v = chunk_val[k];
+        if (v == kChunkFree) continue;  // uniform per block
+        uint4* t = reinterpret_cast<uint4*>(cell_start + (size_t)k * kFillChunk);
+        for (uint32_t j = threadIdx.x; j < kFillChunk / 4; j += blockDim.x) t[j] = make_uint4(v, v, v, v);
+        __syncthreads();
+        if (threadIdx.x == 0) chunk_val[k] = kChunkFree;
     }
 }
 

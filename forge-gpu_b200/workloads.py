@@ -9,11 +9,15 @@ publishes no dataset for them, so every input is generated here from a seed
                    velocities N(0, 0.01); trajectory steps use dt 1e-4,
                    gravity (0,-9.81,0), box [0,1]^3, restitution 1.0.
 * cfg2 "dambreak1m": the config asks for 1M particles on a 0.5h lattice in
-                   [0,0.4]x[0,0.8]x[0,0.4], which only holds 65,536; we keep
-                   the "1M" as N = 1,024,000: an 80x160x80 lattice at spacing
-                   h/5 = 0.005 filling the same region (125 particles per
-                   cell), h 0.025, grid 40^3, dt 1e-4. The literal 0.5h
-                   lattice is "dambreak65k".
+                   [0,0.4]x[0,0.8]x[0,0.4] with h = 0.025, which only holds
+                   65,536. We keep the 1M, the 0.5h lattice (the SPH
+                   resolution: 8 particles per cell, ~30 neighbours) and the
+                   region, and scale h: N = 1,024,000 on an 80x160x80 lattice
+                   at spacing 0.005, h = cell = 0.01, grid 100^3, dt 1e-4.
+                   Two other readings are kept as workloads: the literal
+                   h = 0.025 lattice ("dambreak65k", 65,536 particles) and
+                   1M at h = 0.025 ("dambreak1m_h025": spacing h/5, 125
+                   particles per cell, ~500 neighbours).
 * cfg3 "sharded16m": 320x160x320 lattice at spacing h/2 in [0,1]x[0,0.5]x[0,1],
                    h = 0.00625, grid 160^3, dt 2.5e-5.
 * cfg4 "blobs4m":  4,194,304 points from 64 Gaussian blobs (centres uniform
@@ -72,6 +76,9 @@ def config(name: str) -> SphConfig:
     if name == "ref65k":
         return SphConfig(name, 65536, 0.025, 0.025, (40, 40, 40), 1.0, steps=100)
     if name == "dambreak1m":
+        s = 0.01 / 2
+        return SphConfig(name, 80 * 160 * 80, 0.01, 0.01, (100, 100, 100), 1000.0 * s ** 3, steps=1000)
+    if name == "dambreak1m_h025":
         s = 0.025 / 5
         return SphConfig(name, 80 * 160 * 80, 0.025, 0.025, (40, 40, 40), 1000.0 * s ** 3, steps=1000)
     if name == "dambreak65k":
@@ -103,8 +110,8 @@ def particles(cfg: SphConfig, seed: int = SEED):
         pos = [rng.random(n, dtype=np.float32) for _ in range(3)]
         vel = [rng.normal(0.0, 0.01, n).astype(np.float32) for _ in range(3)]
         return pos, vel
-    if cfg.name == "dambreak1m":
-        pos = list(_lattice(80, 160, 80, 0.025 / 5))
+    if cfg.name in ("dambreak1m", "dambreak1m_h025"):
+        pos = list(_lattice(80, 160, 80, 0.005))
     elif cfg.name == "dambreak65k":
         pos = list(_lattice(32, 64, 32, 0.025 / 2))
     elif cfg.name == "sharded16m":
