@@ -344,10 +344,22 @@ def run_sharded(args, torch, dist, rank, world, local):
     cap = int(cfg.n / world * 1.3) + 4 * (cfg.n // cfg.dims[0]) + 1024
     dev = torch.device("cuda", local)
     be = slab.GpuBackend(forge_sph, cfg, cap, local)
-    run = slab.SlabRun(dist, rank, world, cfg, pos, vel, be, dev, capacity=cap, comm=args.comm, forge_sph=forge_sph)
+    # skewed workloads: bounds at particle-count quantiles, rebalanced every k steps
+    balance = args.rebalance_every > 0 if args.rebalance_every is not None else cfg.name == "blobs4m"
+    every = (args.rebalance_every or 10) if balance else 0
+    run = slab.SlabRun(dist, rank, world, cfg, pos, vel, be, dev, capacity=cap, comm=args.comm, forge_sph=forge_sph,
+                       balance=balance)
     del pos, vel
-    for _ in range(args.warmup):
+    count = [0]
+
+    def step():
         run.step()
+        count[0] += 1
+        if every and count[0] % every == 0:
+            run.rebalance()
+
+    for _ in range(args.warmup):
+        step()
     be.grid.check()
     torch.cuda.synchronize()
     dist.barrier()
@@ -355,10 +367,12 @@ def run_sharded(args, torch, dist, rank, world, local):
     ck.start()
     time.sleep(0.3)
     dist.barrier()
-    ms = time_steps(torch, run.step, args.steps)
+    ms = time_steps(torch, step, args.steps)
     clk = ck.stop()
     be.grid.check()
     ms_max = max_over_ranks(torch, dist, ms)
+    n_min = -max_over_ranks(torch, dist, -float(run.n_own))
+    n_max = max_over_ranks(torch, dist, float(run.n_own))
     halo = max_over_ranks(torch, dist, float(run.last_halo))
     # phase breakdown on a few extra (untimed) steps
     run.timing = []
@@ -391,7 +405,7 @@ def run_sharded(args, torch, dist, rank, world, local):
         for k in range(hbuf.shape[0]):
             run.cols[k, :cur].copy_(hbuf[k, :cur], non_blocking=True)
         run.n = cur
-        run.step()
+        step()
         cur = run.n
         for k in range(hbuf.shape[0]):
             hbuf[k, :cur].copy_(run.cols[k, :cur], non_blocking=True)
@@ -419,7 +433,9 @@ def run_sharded(args, torch, dist, rank, world, local):
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic",
                 "config": {"workload": cfg.name, "particles": cfg.n, "cells": cfg.cells, "h": cfg.h,
                            "inputs_exceed_l2": True, "parallelism": f"x-slab over {world} GPUs (NCCL send/recv, exchange={args.comm})",
-                           "max_halo_particles_per_rank": halo},
+                           "max_halo_particles_per_rank": halo,
+                           "slab_bounds": "particle-count quantiles, rebalanced every %d steps" % every if every
+                           else "uniform", "owned_per_rank_min_max": [n_min, n_max]},
                 "phases_ms_max_over_ranks": phase_ms,
                 "overlap_ms_after_prepare_max_over_ranks": side_ms,
                 "e2e": {"value": cfg.n * e2e_steps / (e2e_ms / 1e3), "unit": "particle-steps/s",
@@ -439,6 +455,9 @@ def main():
                     choices=["sharded16m", "dambreak1m", "dambreak1m_h025", "dambreak65k", "blobs4m", "ref65k"])
     ap.add_argument("--no-extra", action="store_true", help="skip the 1M dam-break and 2^28 sort extras")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
+    ap.add_argument("--rebalance-every", type=int, default=None,
+                    help="N>1: slab bounds at particle-count quantiles, rebalanced every K steps (0: uniform "
+                         "slabs; default: 10 for blobs4m, uniform otherwise)")
     ap.add_argument("--comm", choices=["nccl", "torch"], default="nccl",
                     help="N>1 exchange: in the library over NCCL, or in Python over torch.distributed")
     args = ap.parse_args()

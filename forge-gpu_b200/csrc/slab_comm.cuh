@@ -225,6 +225,15 @@ extern "C" int forge_slab_comm_create(const uint8_t* id, int rank, int world, in
     return FORGE_OK;
 }
 
+extern "C" int forge_slab_comm_set_bounds(forge_slab_comm* c, float lo, float hi) {
+    if (!c) return set_error(FORGE_ERR_INVALID_ARG, "forge_slab_comm_set_bounds: NULL communicator");
+    if (c->pending) return set_error(FORGE_ERR_INVALID_ARG, "forge_slab_comm_set_bounds: a split round is open");
+    if (!(lo < hi)) return set_error(FORGE_ERR_INVALID_ARG, "forge_slab_comm_set_bounds: lo >= hi");
+    c->lo = lo;
+    c->hi = hi;
+    return FORGE_OK;
+}
+
 extern "C" void forge_slab_comm_destroy(forge_slab_comm* c) {
     if (c) slab_comm_free(c);
 }

@@ -34,15 +34,21 @@ _NCOL = 7
 
 
 class SlabGeometry:
-    """Uniform x-slabs of [x0, x1)."""
+    """x-slabs of [x0, x1): uniform, or at explicit bounds b_0 < ... < b_W."""
 
-    def __init__(self, rank: int, world: int, x0: float, x1: float, h: float):
+    def __init__(self, rank: int, world: int, x0: float, x1: float, h: float, bounds=None):
         self.rank, self.world, self.h = rank, world, h
-        w = (x1 - x0) / world
-        self.lo = x0 + w * rank
-        self.hi = x0 + w * (rank + 1)
+        if bounds is None:
+            w = (x1 - x0) / world
+            bounds = [x0 + w * k for k in range(world)] + [x1]
+        self.set_bounds(bounds)
         self.first = rank == 0
         self.last = rank == world - 1
+
+    def set_bounds(self, bounds) -> None:
+        self.bounds = [float(b) for b in bounds]
+        self.lo = self.bounds[self.rank]
+        self.hi = self.bounds[self.rank + 1]
 
     def force_zones(self, reach: float, margin: float | None = None):
         """(inner_lo, inner_hi, guard_lo, guard_hi) in float32 for the split
@@ -74,6 +80,53 @@ class SlabGeometry:
         if not self.last:
             m &= x < self.hi
         return m
+
+
+def quantile_bounds(hist, x0: float, x1: float, world: int):
+    """Bounds b_0 = x0 < ... < b_W = x1 at the particle-count quantiles of
+    an x-histogram (bins over [x0, x1), linear inside a bin)."""
+    hist = np.asarray(hist, dtype=np.float64)
+    nb = hist.size
+    edges = x0 + (x1 - x0) * np.arange(nb + 1) / nb
+    cum = np.concatenate([[0.0], np.cumsum(hist)])
+    total = cum[-1]
+    if total <= 0:
+        return [x0 + (x1 - x0) * k / world for k in range(world)] + [x1]
+    out = [float(x0)]
+    for k in range(1, world):
+        q = total * k / world
+        j = min(max(int(np.searchsorted(cum, q, side="right")) - 1, 0), nb - 1)  # bin holding the quantile
+        frac = (q - cum[j]) / hist[j] if hist[j] > 0 else 0.0
+        out.append(float(edges[j] + frac * (edges[j + 1] - edges[j])))
+    out.append(float(x1))
+    return out
+
+
+def min_width_bounds(b, min_width: float):
+    """b with every slab at least min_width wide (inner bounds pushed right,
+    then left), rounded to float32 (the library compares in float32)."""
+    b = list(b)
+    for k in range(1, len(b) - 1):
+        b[k] = max(b[k], b[k - 1] + min_width)
+    for k in range(len(b) - 2, 0, -1):
+        b[k] = min(b[k], b[k + 1] - min_width)
+    return [float(np.float32(v)) for v in b]
+
+
+def balanced_bounds(hist, x0: float, x1: float, old, min_width: float):
+    """Rebalanced slab bounds: the quantile bounds of a global x-histogram,
+    each inner bound kept between the old bounds of its neighbours (so no
+    particle moves more than one slab) and every slab at least min_width
+    wide (so halos come from direct neighbours only). Returns the old bounds
+    when no such move exists. Pure host arithmetic on identical inputs:
+    every rank computes the same bounds."""
+    w = len(old) - 1
+    q = quantile_bounds(hist, x0, x1, w)
+    new = [float(old[0])] + [min(max(q[k], old[k - 1]), old[k + 1]) for k in range(1, w)] + [float(old[w])]
+    new = min_width_bounds(new, min_width)
+    ok = all(new[k + 1] - new[k] >= min_width * (1 - 1e-6) for k in range(w)) and all(
+        old[k - 1] <= new[k] <= old[k + 1] for k in range(1, w))
+    return new if ok else list(old)
 
 
 class Exchanger:
@@ -186,6 +239,9 @@ class PyComm:
         self.rho_slot = (torch.cat([blocks["hl"], blocks["ml"]]), torch.cat([blocks["hr"], blocks["mr"]]))
         run.n, run.ng = n_new, ng
 
+    def set_bounds(self, lo: float, hi: float) -> None:
+        pass  # reads run.geo
+
     def exchange_rho(self, rho: torch.Tensor) -> None:
         """Round 2: ghosts receive their owners' densities."""
         send_l, send_r = self.rho_send
@@ -232,6 +288,9 @@ class NcclComm:
 
     split = True  # supports the exchange overlapped with the interior force pass
 
+    def set_bounds(self, lo: float, hi: float) -> None:
+        self.f.check(self.L.forge_slab_comm_set_bounds(self.h, lo, hi))
+
     def exchange_begin(self) -> None:
         run = self.run
         self.f.check(self.L.forge_slab_exchange_begin(self.h, run.cols.data_ptr(), run.cols.stride(0), run.n,
@@ -274,10 +333,15 @@ class SlabRun:
 
     def __init__(self, dist, rank: int, world: int, cfg, pos, vel, backend, device: torch.device,
                  x_range=(0.0, 1.0), order_by_id: bool = False, comm_device=None, capacity: int | None = None,
-                 comm: str = "torch", forge_sph=None):
+                 comm: str = "torch", forge_sph=None, balance: bool = False, hist_bins: int = 4096):
         self.cfg, self.backend, self.device = cfg, backend, device
-        self.geo = SlabGeometry(rank, world, x_range[0], x_range[1], cfg.h)
+        self.dist, self.x_range, self.hist_bins = dist, x_range, hist_bins
         self.reach = cfg.h * (1.0 + 1e-5)
+        self.geo = SlabGeometry(rank, world, x_range[0], x_range[1], cfg.h)
+        if balance:  # initial bounds at the quantiles of the (identical on every rank) initial positions
+            hist = np.histogram(np.asarray(pos[0], np.float64), bins=hist_bins, range=x_range)[0]
+            self.geo.set_bounds(min_width_bounds(quantile_bounds(hist, x_range[0], x_range[1], world),
+                                                 2.0 * self.reach))
         self.order_by_id = order_by_id
         px = torch.as_tensor(pos[0])
         m = self.geo.owned_mask(px)
@@ -294,6 +358,30 @@ class SlabRun:
         self._hp = None  # high-priority stream of the split force pass
         self.comm = NcclComm(self, dist, forge_sph) if comm == "nccl" else PyComm(self, dist, comm_device)
         self.comm.exchange(migrate=False)  # initial halo
+
+    def rebalance(self) -> bool:
+        """Moves the slab bounds to the particle-count quantiles of the
+        global x-histogram of owned particles (one all-reduce of hist_bins
+        counts, the only collective of the sharded path), then reruns round
+        1 so particles outside the new slab migrate and the halos match.
+        Between steps only. Returns whether the bounds moved."""
+        x = self.cols[0, :self.n]
+        lo, hi = self.x_range
+        hist = torch.histc(x.float(), bins=self.hist_bins, min=lo, max=hi)
+        # histc drops values outside [lo, hi]: count them into the end bins
+        hist[0] += (x < lo).sum()
+        hist[-1] += (x > hi).sum()
+        if self.device.type == "cuda" and self.dist.get_backend() != "nccl":
+            hist = hist.cpu()
+        self.dist.all_reduce(hist)
+        new = balanced_bounds(hist.cpu().numpy(), lo, hi, self.geo.bounds, 2.0 * self.reach)
+        if new == self.geo.bounds:
+            return False
+        self.geo.set_bounds(new)
+        self.comm.set_bounds(self.geo.lo, self.geo.hi)
+        self.ng = 0  # ghosts of the old bounds
+        self.comm.exchange(migrate=True)
+        return True
 
     def _mark(self, name):
         if self.timing is not None:

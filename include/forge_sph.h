@@ -379,6 +379,13 @@ FORGE_API int forge_slab_comm_create(const uint8_t* id, int rank, int world, int
                                      float lo, float hi, float reach, forge_slab_comm** out);
 FORGE_API void forge_slab_comm_destroy(forge_slab_comm* c);
 
+/* Moves this rank's slab to [lo, hi) (load balancing). The next round 1
+ * (forge_slab_exchange with migrate = 1) sends every owned particle outside
+ * it to the neighbour: callers keep each new bound between the old
+ * neighbouring bounds, so no particle moves more than one slab, and every
+ * slab at least 2 * reach wide, so halos come from direct neighbours only. */
+FORGE_API int forge_slab_comm_set_bounds(forge_slab_comm* c, float lo, float hi);
+
 /* Round 1 (after a step's force pass, or once at start with migrate = 0):
  * migrants (x outside the slab) leave the owned columns and go to the
  * neighbour, together with the halo rows (owned particles within reach of a

@@ -119,3 +119,68 @@ def test_sharded_step_matches_single_process(tmp_path, world):
         oracle.step(p, sp, pos, vel, cfg.cell_size, cfg.dims)
     want = np.stack(pos + vel, axis=1)
     assert np.array_equal(got, want)
+
+
+def _skewed_inputs(cfg):
+    """Two dense clumps in x (a cfg4-like skew): uniform slabs are imbalanced."""
+    rng = np.random.Generator(np.random.PCG64(77))
+    n = cfg.n
+    x = np.where(np.arange(n) % 3 == 0, rng.normal(0.2, 0.04, n), rng.normal(0.7, 0.06, n))
+    pos = [np.clip(x, 0.0, 0.999).astype(np.float32), rng.random(n, dtype=np.float32),
+           rng.random(n, dtype=np.float32)]
+    vel = [(rng.normal(0.0, 1.0, n)).astype(np.float32) for _ in range(3)]
+    return pos, vel
+
+
+def _balanced_rank_main(rank, world, port, out_path):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        cfg = _cfg()
+        pos, vel = _skewed_inputs(cfg)
+        run = slab.SlabRun(dist, rank, world, cfg, pos, vel, OracleBackend(cfg), torch.device("cpu"),
+                           order_by_id=True, balance=True, hist_bins=256)
+        first = list(run.geo.bounds)
+        loads = [run.n_own]
+        moved = 0
+        for s in range(STEPS):
+            run.step()
+            if s % 2 == 1:
+                moved += int(run.rebalance())
+            loads.append(run.n_own)
+        states = [None] * world
+        dist.all_gather_object(states, (run.state.numpy().copy(), first, list(run.geo.bounds), loads, moved))
+        if rank == 0:
+            np.save(out_path, np.array(states, dtype=object), allow_pickle=True)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_balanced_slabs_with_rebalancing_match_single_process(tmp_path):
+    """cfg4's partition: initial bounds at particle-count
+    quantiles, rebalanced every 2 steps from an all-reduced x-histogram, each
+    bound kept between its old neighbours; the trajectory is still the
+    single-process one bit for bit and the loads stay balanced."""
+    world = 3
+    out = str(tmp_path / "states.npy")
+    mp.start_processes(_balanced_rank_main, args=(world, _free_port(), out), nprocs=world, join=True,
+                       start_method="spawn")
+    states = np.load(out, allow_pickle=True)
+    cfg = _cfg()
+    first = states[0][1]
+    assert all(s[1] == first for s in states), "ranks disagree on the bounds"
+    assert abs(first[1] - 1 / 3) > 0.02, "initial bounds are not the quantiles"
+    assert sum(s[4] for s in states) > 0, "no rebalancing moved a bound"
+    for k in range(STEPS + 1):
+        loads = [s[3][k] for s in states]
+        assert max(loads) < 1.25 * cfg.n / world, loads
+    rows = np.concatenate([s[0] for s in states])
+    ids = rows[:, 6].copy().view(np.int32)
+    assert np.array_equal(np.sort(ids), np.arange(cfg.n)), "particles lost or duplicated"
+    got = rows[np.argsort(ids), :6]
+    pos, vel = _skewed_inputs(cfg)
+    sp = oracle.StepParams(cfg.dt, cfg.gravity, cfg.box_min, cfg.box_max, cfg.restitution, 7)
+    p = oracle.SphParams(cfg.h, cfg.mass, cfg.gas_constant, cfg.rest_density, cfg.viscosity)
+    for _ in range(STEPS):
+        oracle.step(p, sp, pos, vel, cfg.cell_size, cfg.dims)
+    assert np.array_equal(got, np.stack(pos + vel, axis=1))
