@@ -141,6 +141,9 @@ class Exchanger:
         self.home = device
 
     def _p2p(self, sends: dict, recvs: dict) -> None:
+        if hasattr(self.dist, "exchange"):  # an in-process transport (MailboxHub)
+            self.dist.exchange(sends, recvs)
+            return
         ops = []
         for peer, t in sends.items():
             ops.append(self.dist.P2POp(self.dist.isend, t, peer))
@@ -188,6 +191,91 @@ class Exchanger:
         a = out[left].to(self.home) if left is not None else empty
         b = out[right].to(self.home) if right is not None else empty
         return a, b
+
+
+class ExchangeTimeout(RuntimeError):
+    """A neighbour's message did not arrive in time (a failed or stalled
+    rank); raised by the rank that waited."""
+
+
+class MailboxHub:
+    """In-process transport for ranks run as threads: the send/recv and
+    all-reduce subset of torch.distributed that the slab exchange uses, with
+    injected faults for failure-detection tests.
+
+    delay = (lo, hi) seconds of random sleep before each send; drop(src, dst,
+    seq) -> True discards that message (seq counts messages per src -> dst
+    pair); a receive that waits longer than `timeout` raises ExchangeTimeout.
+    Messages between a pair are FIFO, as NCCL's and gloo's are."""
+
+    def __init__(self, world: int, timeout: float = 10.0, delay=(0.0, 0.0), drop=None, seed: int = 0):
+        import queue
+        import random
+        import threading
+        self.world, self.timeout, self.delay, self.drop = world, timeout, delay, drop
+        self._q = {(a, b): queue.Queue() for a in range(world) for b in range(world)}
+        self._seq = {k: 0 for k in self._q}
+        self._rng = random.Random(seed)
+        self._lock = threading.Lock()
+        self._barrier = threading.Barrier(world, timeout=timeout)
+        self._acc = None
+
+    def rank(self, r: int) -> "MailboxRank":
+        return MailboxRank(self, r)
+
+
+class MailboxRank:
+    """One rank's view of a MailboxHub (passed where torch.distributed is)."""
+
+    def __init__(self, hub: MailboxHub, rank: int):
+        self.hub, self.r = hub, rank
+
+    def get_backend(self) -> str:
+        return "mailbox"
+
+    def get_rank(self) -> int:
+        return self.r
+
+    def exchange(self, sends: dict, recvs: dict) -> None:
+        import queue
+        import time
+        h = self.hub
+        for peer, t in sends.items():
+            with h._lock:
+                seq = h._seq[(self.r, peer)]
+                h._seq[(self.r, peer)] += 1
+                pause = h._rng.uniform(*h.delay)
+            if pause:
+                time.sleep(pause)
+            if h.drop is not None and h.drop(self.r, peer, seq):
+                continue
+            h._q[(self.r, peer)].put(t.detach().clone())
+        for peer, out in recvs.items():
+            try:
+                msg = h._q[(peer, self.r)].get(timeout=h.timeout)
+            except queue.Empty:
+                raise ExchangeTimeout(f"rank {self.r}: no message from rank {peer} within {h.timeout} s") from None
+            if msg.shape != out.shape:
+                raise ExchangeTimeout(f"rank {self.r}: message from rank {peer} has shape {tuple(msg.shape)}, "
+                                      f"expected {tuple(out.shape)} (a lost message shifted the stream)")
+            out.copy_(msg)
+
+    def all_reduce(self, t: torch.Tensor) -> None:
+        import threading
+        h = self.hub
+        try:
+            with h._lock:
+                h._acc = t.detach().clone() if h._acc is None else h._acc + t
+            h._barrier.wait()
+            t.copy_(h._acc)
+            if h._barrier.wait() == 0:
+                h._acc = None
+            h._barrier.wait()
+        except threading.BrokenBarrierError:
+            raise ExchangeTimeout(f"rank {self.r}: all-reduce partner missing after {h.timeout} s") from None
+
+    def broadcast_object_list(self, objs, src=0):
+        raise NotImplementedError("the library's NCCL exchange needs real ranks")
 
 
 class PyComm:

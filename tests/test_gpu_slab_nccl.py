@@ -30,18 +30,29 @@ def _inputs(cfg):
     return workloads.uniform_particles(cfg.n, seed=43, vsigma=1.0)
 
 
-def _rank_main(rank, world, port, out_path, order_by_id=True):
+def _skewed(cfg):
+    rng = np.random.Generator(np.random.PCG64(5))
+    n = cfg.n
+    x = np.where(np.arange(n) % 4 == 0, rng.normal(0.25, 0.05, n), rng.normal(0.75, 0.08, n))
+    pos = [np.clip(x, 0.0, 0.999).astype(np.float32), rng.random(n, dtype=np.float32),
+           rng.random(n, dtype=np.float32)]
+    return pos, [rng.normal(0.0, 1.0, n).astype(np.float32) for _ in range(3)]
+
+
+def _rank_main(rank, world, port, out_path, order_by_id=True, skewed=False):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)  # plumbing: the NCCL id broadcast
     try:
         torch.cuda.set_device(rank)
         cfg = _cfg()
-        pos, vel = _inputs(cfg)
+        pos, vel = _skewed(cfg) if skewed else _inputs(cfg)
         be = slab.GpuBackend(forge_sph, cfg, cfg.n, rank)
         run = slab.SlabRun(dist, rank, world, cfg, pos, vel, be, torch.device("cuda", rank), order_by_id=order_by_id,
-                           capacity=cfg.n + 8, comm="nccl", forge_sph=forge_sph)
-        for _ in range(STEPS):
+                           capacity=cfg.n + 8, comm="nccl", forge_sph=forge_sph, balance=skewed, hist_bins=256)
+        for s in range(STEPS):
             run.step()
+            if skewed and s % 2 == 1:
+                run.rebalance()
         be.grid.check()
         states = [None] * world
         dist.all_gather_object(states, run.state.cpu().numpy().copy())
@@ -59,9 +70,9 @@ def _free_port():
     return p
 
 
-def _sharded_rows(tmp_path, order_by_id):
+def _sharded_rows(tmp_path, order_by_id, skewed=False):
     out = str(tmp_path / "states.npy")
-    mp.start_processes(_rank_main, args=(2, _free_port(), out, order_by_id), nprocs=2, join=True,
+    mp.start_processes(_rank_main, args=(2, _free_port(), out, order_by_id, skewed), nprocs=2, join=True,
                        start_method="spawn")
     rows = np.concatenate(list(np.load(out, allow_pickle=True)))
     ids = rows[:, 6].copy().view(np.int32)
@@ -69,9 +80,9 @@ def _sharded_rows(tmp_path, order_by_id):
     return rows[np.argsort(ids), :6]
 
 
-def _single_gpu_rows():
+def _single_gpu_rows(skewed=False):
     cfg = _cfg()
-    pos, vel = _inputs(cfg)
+    pos, vel = _skewed(cfg) if skewed else _inputs(cfg)
     p = [torch.from_numpy(x.copy()).cuda() for x in pos]
     v = [torch.from_numpy(x.copy()).cuda() for x in vel]
     rho = torch.empty(cfg.n, dtype=torch.float32, device="cuda")
@@ -102,3 +113,11 @@ def test_nccl_overlapped_step_close_to_single_gpu(cuda, tmp_path):
     got, want = _sharded_rows(tmp_path, False), _single_gpu_rows()
     np.testing.assert_allclose(got[:, :3], want[:, :3], rtol=0, atol=1e-5)
     np.testing.assert_allclose(got[:, 3:], want[:, 3:], rtol=0, atol=1e-3)
+
+
+@two_gpus
+def test_nccl_balanced_rebalanced_step_matches_single_gpu(cuda, tmp_path):
+    """Skewed x distribution: slab bounds at particle-count quantiles,
+    rebalanced every 2 steps (forge_slab_comm_set_bounds + a migrating round
+    1); test mode, so bit for bit."""
+    assert np.array_equal(_sharded_rows(tmp_path, True, skewed=True), _single_gpu_rows(skewed=True))
