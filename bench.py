@@ -434,7 +434,8 @@ def run_sharded(args, torch, dist, rank, world, local):
                 "config": {"workload": cfg.name, "particles": cfg.n, "cells": cfg.cells, "h": cfg.h,
                            "inputs_exceed_l2": True, "parallelism": f"x-slab over {world} GPUs (NCCL send/recv, exchange={args.comm})",
                            "max_halo_particles_per_rank": halo,
-                           "slab_bounds": "particle-count quantiles, rebalanced every %d steps" % every if every
+                           "slab_bounds": "initial particle-count quantiles, rebalanced on the density-weighted x-histogram every %d steps"
+                           % every if every
                            else "uniform", "owned_per_rank_min_max": [n_min, n_max]},
                 "phases_ms_max_over_ranks": phase_ms,
                 "overlap_ms_after_prepare_max_over_ranks": side_ms,

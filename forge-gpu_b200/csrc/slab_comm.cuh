@@ -21,6 +21,9 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <chrono>
+#include <thread>
+
 namespace {
 
 struct NcclApi {
@@ -33,6 +36,8 @@ struct NcclApi {
     ncclResult_t (*Send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
     ncclResult_t (*Recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
     const char* (*GetErrorString)(ncclResult_t) = nullptr;
+    ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+    ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
 };
 
 std::mutex g_nccl_mu;
@@ -56,6 +61,8 @@ int nccl_load() {
     FORGE_NCCL_SYM(Send)
     FORGE_NCCL_SYM(Recv)
     FORGE_NCCL_SYM(GetErrorString)
+    FORGE_NCCL_SYM(CommAbort)
+    FORGE_NCCL_SYM(CommGetAsyncError)
 #undef FORGE_NCCL_SYM
     g_nccl.loaded = true;
     return FORGE_OK;
@@ -111,13 +118,18 @@ struct forge_slab_comm {
     cudaEvent_t ev_counts = nullptr, ev_payload = nullptr;
     bool pending = false;
     uint64_t pend_n_own = 0;
+    // failure detection: host waits give up after `timeout_s`, abort the
+    // communicator and fail every later call
+    double timeout_s = 60.0;
+    cudaEvent_t ev_sync = nullptr;
+    bool aborted = false;
 };
 
 namespace {
 
 void slab_comm_free(forge_slab_comm* c) {
     DeviceScope scope(c->device);
-    if (c->comm) g_nccl.CommDestroy(c->comm);
+    if (c->comm) (c->aborted ? g_nccl.CommAbort : g_nccl.CommDestroy)(c->comm);
     forge_slab_destroy(c->sel);
     for (void* p : {(void*)c->idx, (void*)c->idx_h, (void*)c->counts, (void*)c->halo_l, (void*)c->halo_r, (void*)c->send_l,
                     (void*)c->send_r, (void*)c->recv_l, (void*)c->recv_r, (void*)c->rho_send_l,
@@ -125,7 +137,7 @@ void slab_comm_free(forge_slab_comm* c) {
         cudaFree(p);
     cudaFreeHost(c->hcounts);
     cudaFreeHost(c->hcount);
-    for (cudaEvent_t e : {c->ev_counts, c->ev_payload})
+    for (cudaEvent_t e : {c->ev_counts, c->ev_payload, c->ev_sync})
         if (e) cudaEventDestroy(e);
     delete c;
 }
@@ -202,6 +214,7 @@ extern "C" int forge_slab_comm_create(const uint8_t* id, int rank, int world, in
               cudaMallocHost(&c->hcounts, 3 * sizeof(uint32_t)) == cudaSuccess &&
               cudaMallocHost(&c->hcount, 9 * sizeof(uint64_t)) == cudaSuccess;
     ok = ok && cudaEventCreateWithFlags(&c->ev_counts, cudaEventDisableTiming) == cudaSuccess &&
+         cudaEventCreateWithFlags(&c->ev_sync, cudaEventDisableTiming) == cudaSuccess &&
          cudaEventCreateWithFlags(&c->ev_payload, cudaEventDisableTiming) == cudaSuccess;
     if (!ok) {
         slab_comm_free(c);
@@ -225,6 +238,12 @@ extern "C" int forge_slab_comm_create(const uint8_t* id, int rank, int world, in
     return FORGE_OK;
 }
 
+extern "C" int forge_slab_comm_set_timeout(forge_slab_comm* c, double seconds) {
+    if (!c || !(seconds > 0)) return set_error(FORGE_ERR_INVALID_ARG, "forge_slab_comm_set_timeout: bad argument");
+    c->timeout_s = seconds;
+    return FORGE_OK;
+}
+
 extern "C" int forge_slab_comm_set_bounds(forge_slab_comm* c, float lo, float hi) {
     if (!c) return set_error(FORGE_ERR_INVALID_ARG, "forge_slab_comm_set_bounds: NULL communicator");
     if (c->pending) return set_error(FORGE_ERR_INVALID_ARG, "forge_slab_comm_set_bounds: a split round is open");
@@ -239,6 +258,37 @@ extern "C" void forge_slab_comm_destroy(forge_slab_comm* c) {
 }
 
 namespace {
+
+// Host wait for `ev` with failure detection: polls the event and the
+// communicator's asynchronous error; past the deadline (a neighbour that
+// stopped answering) or on an NCCL error it aborts the communicator, which
+// ends this rank's pending NCCL kernels, and fails.
+int wait_event(forge_slab_comm* c, cudaEvent_t ev, const char* what) {
+    const auto t0 = std::chrono::steady_clock::now();
+    for (uint32_t k = 0;; ++k) {
+        const cudaError_t e = cudaEventQuery(ev);
+        if (e == cudaSuccess) return FORGE_OK;
+        if (e != cudaErrorNotReady) return set_error(FORGE_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+        ncclResult_t ae = ncclSuccess;
+        if (g_nccl.CommGetAsyncError(c->comm, &ae) != ncclSuccess || ae != ncclSuccess) {
+            c->aborted = true;
+            g_nccl.CommAbort(c->comm);
+            c->comm = nullptr;
+            return set_error(FORGE_ERR_NCCL, "%s: NCCL error %s; communicator aborted", what,
+                             g_nccl.GetErrorString(ae));
+        }
+        const double waited = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+        if (waited > c->timeout_s) {
+            c->aborted = true;
+            g_nccl.CommAbort(c->comm);
+            c->comm = nullptr;
+            return set_error(FORGE_ERR_TIMEOUT,
+                             "%s: no progress for %.1f s (a neighbour stopped answering); communicator aborted", what,
+                             waited);
+        }
+        if (k > 64) std::this_thread::sleep_for(std::chrono::microseconds(20));
+    }
+}
 
 uint32_t slab_sides(const forge_slab_comm* c) { return (c->left >= 0 ? 1u : 0u) | (c->right >= 0 ? 2u : 0u); }
 
@@ -348,6 +398,7 @@ extern "C" int forge_slab_exchange(forge_slab_comm* c, float* cols, uint64_t ld,
     if (n_own > c->cap || ld < c->cap)
         return set_error(FORGE_ERR_CAPACITY, "forge_slab_exchange: n_own or ld does not fit the capacity");
     if (c->pending) return set_error(FORGE_ERR_INVALID_ARG, "forge_slab_exchange: a split round is open");
+    if (c->aborted) return set_error(FORGE_ERR_NCCL, "slab exchange: communicator aborted by an earlier failure");
     FORGE_DEVICE_SCOPE(c->device);
     cudaStream_t st = as_stream(stream);
     const uint32_t sides = slab_sides(c);
@@ -374,7 +425,8 @@ extern "C" int forge_slab_exchange(forge_slab_comm* c, float* cols, uint64_t ld,
     if ((rc = pack_list(c, cols, ld, c->idx_h, ch, 2, cm + 2, c->send_r, c->halo_r, st)) != FORGE_OK) return rc;
     // 3. counts: ours to the neighbours, theirs back, everything to the host
     if ((rc = exchange_counts(c, st)) != FORGE_OK) return rc;
-    FORGE_CUDA(cudaStreamSynchronize(st));
+    FORGE_CUDA(cudaEventRecord(c->ev_sync, st));
+    if ((rc = wait_event(c, c->ev_sync, "forge_slab_exchange")) != FORGE_OK) return rc;
     RoundSizes z;
     if ((rc = round_sizes(c, n_own, ld, z)) != FORGE_OK) return rc;
     // 4. payload, 5. arrivals, then ghosts
@@ -388,6 +440,7 @@ extern "C" int forge_slab_exchange_begin(forge_slab_comm* c, const float* cols, 
     if (n_own > c->cap || ld < c->cap)
         return set_error(FORGE_ERR_CAPACITY, "forge_slab_exchange_begin: n_own or ld does not fit the capacity");
     if (c->pending) return set_error(FORGE_ERR_INVALID_ARG, "forge_slab_exchange_begin: a split round is open");
+    if (c->aborted) return set_error(FORGE_ERR_NCCL, "slab exchange: communicator aborted by an earlier failure");
     FORGE_DEVICE_SCOPE(c->device);
     cudaStream_t sd = as_stream(stream);
     // Migrants and in-slab halo rows (disjoint) from one read of the
@@ -421,11 +474,13 @@ extern "C" int forge_slab_exchange_end(forge_slab_comm* c, float* cols, uint64_t
     if (!c->pending) return set_error(FORGE_ERR_INVALID_ARG, "forge_slab_exchange_end: no forge_slab_exchange_begin");
     if (ld < c->cap) return set_error(FORGE_ERR_CAPACITY, "forge_slab_exchange_end: ld does not fit the capacity");
     c->pending = false;
+    if (c->aborted) return set_error(FORGE_ERR_NCCL, "slab exchange: communicator aborted by an earlier failure");
     FORGE_DEVICE_SCOPE(c->device);
     cudaStream_t st = as_stream(stream), sd = c->pend_stream;
     const uint64_t n_own = c->pend_n_own;
     int rc;
-    FORGE_CUDA(cudaEventSynchronize(c->ev_counts));  // the interior pass keeps running meanwhile
+    // the interior pass keeps running meanwhile
+    if ((rc = wait_event(c, c->ev_counts, "forge_slab_exchange_end")) != FORGE_OK) return rc;
     RoundSizes z;
     if ((rc = round_sizes(c, n_own, ld, z)) != FORGE_OK) return rc;
     if ((rc = send_payload(c, z, sd)) != FORGE_OK) return rc;
@@ -446,6 +501,7 @@ extern "C" int forge_slab_exchange_rho(forge_slab_comm* c, float* rho, void* str
     if (!c || !rho) return set_error(FORGE_ERR_INVALID_ARG, "forge_slab_exchange_rho: NULL argument");
     if (c->pending) return set_error(FORGE_ERR_INVALID_ARG, "forge_slab_exchange_rho: a split round is open");
     if (!c->have_round) return set_error(FORGE_ERR_INVALID_ARG, "forge_slab_exchange_rho: no exchange round yet");
+    if (c->aborted) return set_error(FORGE_ERR_NCCL, "slab exchange: communicator aborted by an earlier failure");
     FORGE_DEVICE_SCOPE(c->device);
     cudaStream_t st = as_stream(stream);
     const uint32_t kl = c->n_hl + c->n_arr_l, kr = c->n_hr + c->n_arr_r;

@@ -444,30 +444,44 @@ class SlabRun:
         self.timing = None  # set to a list to record per-phase CUDA events
         self.timing_side = []
         self._hp = None  # high-priority stream of the split force pass
+        self.balance = balance
+        self._work_hist = None  # x-histogram of the last step's pair work (balancing runs)
         self.comm = NcclComm(self, dist, forge_sph) if comm == "nccl" else PyComm(self, dist, comm_device)
         self.comm.exchange(migrate=False)  # initial halo
 
-    def rebalance(self) -> bool:
-        """Moves the slab bounds to the particle-count quantiles of the
-        global x-histogram of owned particles (one all-reduce of hist_bins
-        counts, the only collective of the sharded path), then reruns round
-        1 so particles outside the new slab migrate and the halos match.
-        Between steps only. Returns whether the bounds moved."""
-        x = self.cols[0, :self.n]
+    def _x_hist(self, x: torch.Tensor, w: torch.Tensor | None) -> torch.Tensor:
         lo, hi = self.x_range
-        hist = torch.histc(x.float(), bins=self.hist_bins, min=lo, max=hi)
-        # histc drops values outside [lo, hi]: count them into the end bins
-        hist[0] += (x < lo).sum()
-        hist[-1] += (x > hi).sum()
+        nb = self.hist_bins
+        idx = ((x.double() - lo) * (nb / (hi - lo))).floor().clamp_(0, nb - 1).long()
+        return torch.bincount(idx, weights=None if w is None else w.double(), minlength=nb).double()
+
+    def _note_work(self, x: torch.Tensor, rho: torch.Tensor) -> None:
+        """Work histogram of the owned particles at density time (balancing
+        runs only): each particle weighs its density, which is proportional
+        to its neighbour count and so to its share of the pair work."""
+        if self.balance:
+            self._work_hist = self._x_hist(x, rho)
+
+    def rebalance(self) -> bool:
+        """Moves the slab bounds to the quantiles of a global x-histogram (one
+        all-reduce of hist_bins values, the only collective of the sharded
+        path), then reruns round 1 so particles outside the new slab migrate
+        and the halos match. The histogram is the work histogram of the last
+        step (skewed inputs balance pair work, not particle counts), or the
+        owned particles' counts before any step. Between steps only. Returns
+        whether the bounds moved."""
+        hist = self._work_hist if self._work_hist is not None else self._x_hist(self.cols[0, :self.n], None)
         if self.device.type == "cuda" and self.dist.get_backend() != "nccl":
             hist = hist.cpu()
         self.dist.all_reduce(hist)
+        lo, hi = self.x_range
         new = balanced_bounds(hist.cpu().numpy(), lo, hi, self.geo.bounds, 2.0 * self.reach)
         if new == self.geo.bounds:
             return False
         self.geo.set_bounds(new)
         self.comm.set_bounds(self.geo.lo, self.geo.hi)
         self.ng = 0  # ghosts of the old bounds
+        self._work_hist = None
         self.comm.exchange(migrate=True)
         return True
 
@@ -530,6 +544,7 @@ class SlabRun:
         self._mark("density")
         self.comm.exchange_rho(rho)
         self._mark("ghost_rho")
+        self._note_work(C[0, :n_own], rho[:n_own])  # owned-then-ghost layout here in both modes
         if perm is not None:
             rho = rho[perm]
             C[:, :n] = C[:, perm]
@@ -567,6 +582,7 @@ class SlabRun:
         n_own, n = self.n, self.n + self.ng
         rho = self.backend.density([C[k, :n] for k in range(3)], n)
         self._mark("density")
+        self._note_work(C[0, :n_own], rho[:n_own])
         cols6 = [C[k, :n] for k in range(6)]
         zones = self.geo.force_zones(self.reach)
         self.backend.force_step(cols6, rho, n, n_own, zone=(3,) + zones)

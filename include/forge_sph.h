@@ -379,6 +379,13 @@ FORGE_API int forge_slab_comm_create(const uint8_t* id, int rank, int world, int
                                      float lo, float hi, float reach, forge_slab_comm** out);
 FORGE_API void forge_slab_comm_destroy(forge_slab_comm* c);
 
+/* Failure detection: every host wait of the exchange (the message sizes)
+ * polls with a deadline, default 60 s. Past it -- a neighbour that stopped
+ * answering -- or on an asynchronous NCCL error the call aborts the
+ * communicator (ending this rank's pending NCCL kernels) and returns
+ * FORGE_ERR_TIMEOUT / FORGE_ERR_NCCL; every later exchange call on it fails. */
+FORGE_API int forge_slab_comm_set_timeout(forge_slab_comm* c, double seconds);
+
 /* Moves this rank's slab to [lo, hi) (load balancing). The next round 1
  * (forge_slab_exchange with migrate = 1) sends every owned particle outside
  * it to the neighbour: callers keep each new bound between the old

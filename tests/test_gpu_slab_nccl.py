@@ -5,6 +5,7 @@ Needs two visible GPUs; skipped on one."""
 import ctypes
 import os
 import socket
+import time
 
 import numpy as np
 import pytest
@@ -121,3 +122,52 @@ def test_nccl_balanced_rebalanced_step_matches_single_gpu(cuda, tmp_path):
     rebalanced every 2 steps (forge_slab_comm_set_bounds + a migrating round
     1); test mode, so bit for bit."""
     assert np.array_equal(_sharded_rows(tmp_path, True, skewed=True), _single_gpu_rows(skewed=True))
+
+
+def _dead_neighbour_main(rank, world, port, out_path):
+    """Rank 1 leaves between steps (no kernel or NCCL call in flight); rank
+    0's next exchange must fail with FORGE_ERR_TIMEOUT after its 2 s
+    deadline instead of hanging, with its communicator aborted."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    torch.cuda.set_device(rank)
+    cfg = _cfg()
+    pos, vel = _inputs(cfg)
+    be = slab.GpuBackend(forge_sph, cfg, cfg.n, rank)
+    run = slab.SlabRun(dist, rank, world, cfg, pos, vel, be, torch.device("cuda", rank), capacity=cfg.n + 8,
+                       comm="nccl", forge_sph=forge_sph)
+    forge_sph.check(forge_sph.lib().forge_slab_comm_set_timeout(run.comm.h, 2.0))
+    run.step()
+    torch.cuda.synchronize()
+    dist.barrier()  # both finished step 1
+    if rank == 1:
+        time.sleep(8.0)  # gone: never joins step 2
+        os._exit(0)
+    t0 = time.monotonic()
+    try:
+        run.step()
+        torch.cuda.synchronize()
+        res = "no error"
+    except forge_sph.ForgeError as e:
+        res = f"{e.code}|{e}"
+    took = time.monotonic() - t0
+    again = ""
+    try:
+        run.comm.exchange_rho(torch.zeros(8, device="cuda"))
+    except forge_sph.ForgeError as e:
+        again = str(e)
+    with open(out_path, "w") as f:
+        f.write(f"{res}\n{took}\n{again}\n")
+    os._exit(0)
+
+
+@two_gpus
+def test_nccl_dead_neighbour_times_out(cuda, tmp_path):
+    out = str(tmp_path / "result.txt")
+    mp.start_processes(_dead_neighbour_main, args=(2, _free_port(), out), nprocs=2, join=True,
+                       start_method="spawn")
+    res, took, again = open(out).read().split("\n")[:3]
+    assert res.startswith(f"{forge_sph.FORGE_ERR_TIMEOUT}|"), res
+    assert "aborted" in res
+    assert 1.5 < float(took) < 30.0
+    assert "aborted" in again

@@ -157,10 +157,11 @@ def _balanced_rank_main(rank, world, port, out_path):
 
 
 def test_balanced_slabs_with_rebalancing_match_single_process(tmp_path):
-    """cfg4's partition: initial bounds at particle-count
-    quantiles, rebalanced every 2 steps from an all-reduced x-histogram, each
-    bound kept between its old neighbours; the trajectory is still the
-    single-process one bit for bit and the loads stay balanced."""
+    """The partition for skewed inputs: initial bounds at particle-count
+    quantiles, rebalanced every 2 steps from an all-reduced work histogram
+    (x weighted by density), each bound kept between its old neighbours;
+    the trajectory is still the single-process one bit for bit and the
+    loads stay balanced."""
     world = 3
     out = str(tmp_path / "states.npy")
     mp.start_processes(_balanced_rank_main, args=(world, _free_port(), out), nprocs=world, join=True,
