@@ -194,7 +194,14 @@ __device__ __forceinline__ void poly6_two(const float4* __restrict__ pos4, uint3
 // segments (first only, both, second only) of their ordered ranges.
 // Different rows: two single walks. Each particle's sum keeps the reference
 // order.
-__global__ void __launch_bounds__(128)
+#ifndef FORGE_DENSITY_MIN_BLOCKS
+#define FORGE_DENSITY_MIN_BLOCKS 10  // 48 registers (a few spills): 10 blocks per SM
+#endif
+#ifndef FORGE_FORCE_MIN_BLOCKS
+#define FORGE_FORCE_MIN_BLOCKS 8  // 64 registers: 8 blocks per SM (the spills cost less than the occupancy gains)
+#endif
+
+__global__ void __launch_bounds__(128, FORGE_DENSITY_MIN_BLOCKS)
     density_pair_kernel(const float4* __restrict__ pos4, const uint32_t* __restrict__ cell_start,
                         const uint32_t* __restrict__ sorted_idx, uint32_t n, Geom g, SphConsts c,
                         float4* __restrict__ vel4, float2* __restrict__ aux, float* __restrict__ density_out) {
@@ -748,7 +755,7 @@ __global__ void __launch_bounds__(128)
 // Force pass, two consecutive cell-ordered particles per thread (LIST: two
 // consecutive entries of a zone list).
 template <int TERMS, int EPI, bool LIST>
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(128, FORGE_FORCE_MIN_BLOCKS)
     force_kernel(const float4* __restrict__ pos4, const float4* __restrict__ vel4, const float2* __restrict__ aux,
                  const uint32_t* __restrict__ cell_start, const uint32_t* __restrict__ sorted_idx, uint32_t n, Geom g,
                  SphConsts c, StepEpi ep, ForceOut out, ZoneList zl) {

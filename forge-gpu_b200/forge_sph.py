@@ -27,7 +27,7 @@ import os
 from dataclasses import dataclass, field
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libforge_sph.so")
+LIB_PATH = os.environ.get("FORGE_SPH_LIB") or os.path.join(_HERE, "libforge_sph.so")
 
 FORGE_OK = 0
 FORGE_ERR_INVALID_ARG = -1
