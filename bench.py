@@ -32,9 +32,9 @@ import numpy as np  # noqa: E402
 import workloads  # noqa: E402
 
 # DRAM bytes (read + write) per force+epilogue launch per particle, from the
-# ncu capture in profiles/sph_step_sharded16m_ncu.md (1,099 MB for 16,384,000
+# ncu capture in profiles/sph_step_sharded16m_ncu.md (755 + 381 MB for 16,384,000
 # particles, cfg3); applied to cfg3-like workloads only.
-FORCE_TRAFFIC_B_PER_PARTICLE = 1099.0e6 / 16384000
+FORCE_TRAFFIC_B_PER_PARTICLE = 1136.0e6 / 16384000
 
 
 def peaks():
