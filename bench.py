@@ -108,14 +108,31 @@ PHASES = ("sort", "cells_gather", "density", "force")
 
 
 def kernels_per_step(cfg):
-    return 1 + (cfg.key_bits + 7) // 8 + 3  # histogram, passes, cell table, density, force
+    """hash + histogram, the sort passes, cell table, chunk fill, density, force."""
+    return 1 + (cfg.key_bits + 7) // 8 + 2 + 2
 
 
 def sharded_kernels_per_step(cfg):
-    """Our kernels per step on a rank with two neighbours: grid build, density,
-    2 density packs, gather, 2 force zones, 2 classifications (3 kernels
-    each), 4 packs, counts message, compaction, 2 halo remaps, 6 unpacks."""
-    return kernels_per_step(cfg) + 2 + 1 + 1 + 6 + 4 + 1 + 1 + 2 + 6
+    """Our kernels per step on a rank with two neighbours (the overlapped
+    step): grid build (hash + histogram, passes, cell table, chunk fill),
+    density, prepare (gather + 3 zone-list kernels), density round (pack,
+    scatter), ghost densities, 2 force zones, round 1 (3 selection kernels,
+    compaction, halo remap, unpack)."""
+    return (1 + (cfg.key_bits + 7) // 8 + 2) + 1 + 4 + 2 + 1 + 2 + 6
+
+
+def lattice_pairs(cfg):
+    """Neighbours within h (self included) of an interior particle of a cubic
+    lattice config: the integer offsets with |offset| * spacing < h. None for
+    the random workloads."""
+    spacing = {"sharded16m": cfg.h / 2, "dambreak1m": cfg.h / 2, "dambreak1m_h025": cfg.h / 5,
+               "dambreak65k": cfg.h / 2}.get(cfg.name)
+    if spacing is None:
+        return None
+    m = int(cfg.h / spacing) + 1
+    r = np.arange(-m, m + 1)
+    d2 = r[:, None, None] ** 2 + r[None, :, None] ** 2 + r[None, None, :] ** 2
+    return int((d2 * spacing * spacing < cfg.h * cfg.h * (1 - 1e-9)).sum())
 
 
 def sph_params(forge_sph, cfg):
@@ -494,6 +511,7 @@ def main():
     traffic = None
     if dom == "force" and cfg.name == "sharded16m":
         traffic = FORCE_TRAFFIC_B_PER_PARTICLE * cfg.n
+    pairs = lattice_pairs(cfg)
     phases = {k: {"ms": phase_ms[k], "alg_bytes_per_particle": ab[k],
                   "achieved_gbs": ab[k] * cfg.n / (phase_ms[k] / 1e3) / 1e9,
                   "frac_of_hbm": ab[k] * cfg.n / (phase_ms[k] / 1e3) / 1e9 / hbm} for k in PHASES}
@@ -515,6 +533,11 @@ def main():
                     "h2d_bytes_per_step": e2e_bytes, "d2h_bytes_per_step": e2e_bytes},
             "gpu_launches": kernels_per_step(cfg) * args.steps,
             "clocks": clk}
+    if pairs is not None:  # the pair-evaluation rate of the neighbour passes (interior lattice particles)
+        line["neighbour_pairs"] = {
+            "within_h_per_particle_incl_self": pairs,
+            "density_pair_terms_per_s": pairs * cfg.n / (phase_ms["density"] / 1e3),
+            "force_pair_terms_per_s": (pairs - 1) * cfg.n / (phase_ms["force"] / 1e3)}
     if not args.no_cpu:
         m = CPU_SAMPLE.get(cfg.name, 262_144)
         cp, cv, m = cpu_sample(cfg, m)
