@@ -13,9 +13,17 @@
 //   forge_slab_exchange_rho (round 2, after density; sizes known, no sync)
 //     send rho of [halo sent to X, arrivals from X] to X; X's values land in
 //     [halo from X, our migrants to X].
-// One stream synchronisation per round 1 (after the count exchange: NCCL
-// needs the payload sizes on the host); every list size before it stays on
-// the device.
+// Round 1 split for overlap with the interior force pass:
+//   forge_slab_exchange_begin (after the boundary force, on the caller's
+//     side stream) one-pass selection of migrants and in-slab halo rows from
+//     the uncompacted columns, records packed as listed, counts exchanged
+//   forge_slab_exchange_end   (host waits for the counts) payload on the side
+//     stream; on the main stream, after it: compaction, remap of the halo
+//     lists to the compacted columns, arrivals and ghosts in one launch.
+// One host wait per round 1 (after the count exchange: NCCL needs the payload
+// sizes on the host); every list size before it stays on the device. Host
+// waits have a deadline: past it, or on an asynchronous NCCL error, the
+// communicator is aborted and every later call fails (failure detection).
 #pragma once
 
 #include <dlfcn.h>

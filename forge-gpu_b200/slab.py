@@ -15,9 +15,13 @@ x < lo_0, the last rank x >= hi). Every step:
   5. migration: owned particles that left the slab move to the neighbour.
 
 Only the two neighbour exchanges cross ranks (send/recv of counts, then
-payloads), no data-path collective. The per-rank compute is a Backend:
+payloads), no data-path collective; on GPU ranks (comm="nccl") steps 3 and
+5 run beside the interior half of step 4 (SlabRun._step_overlapped). Skewed
+inputs move the slab bounds every k steps (SlabRun.rebalance: one
+all-reduce of a work histogram). The per-rank compute is a Backend:
 GpuBackend runs the library's kernels (forge_sph_density,
-forge_sph_force_step) on the rank's GPU; tests supply a CPU backend.
+forge_sph_force_step[_zone]) on the rank's GPU; tests supply a CPU backend
+and, for failure detection, an in-process transport (MailboxHub).
 With ``order_by_id`` local arrays are kept in particle-id order, which makes
 each particle's neighbour order, and hence the result, identical to the
 single-device run.
