@@ -73,3 +73,22 @@ def test_no_gpu_fails_loudly():
         pytest.skip("GPU present")
     with pytest.raises(forge_sph.ForgeError):
         forge_sph.RadixSorter(16)
+
+
+def test_sharded_entry_points_reject_bad_arguments_without_gpu():
+    """The sharded-step entry points check their arguments before any device
+    call (no GPU needed)."""
+    L = forge_sph.lib()
+    bad = forge_sph.FORGE_ERR_INVALID_ARG
+    z = forge_sph.ForceZone(forge_sph.ZONE_BOUNDARY, 0.1, 0.9, 0.05, 0.95)
+    sp, stp = forge_sph.SphParams(), forge_sph.StepParams()
+    assert L.forge_sph_force_step_zone(None, ctypes.byref(sp), ctypes.byref(stp), *([None] * 7), 0, 0,
+                                       ctypes.byref(z), None) == bad
+    assert "NULL grid" in forge_sph.last_error()
+    assert L.forge_slab_comm_set_timeout(None, 1.0) == bad
+    assert L.forge_slab_comm_set_bounds(None, 0.0, 1.0) == bad
+    assert L.forge_slab_exchange_begin(None, None, 0, 0, None) == bad
+    n_own, ng = ctypes.c_uint64(), ctypes.c_uint64()
+    assert L.forge_slab_exchange_end(None, None, 0, ctypes.byref(n_own), ctypes.byref(ng), None) == bad
+    assert L.forge_slab_exchange_rho(None, None, None) == bad
+    assert L.forge_slab_comm_create(None, 0, 1, 0, 16, 0.0, 1.0, 0.1, None) == bad
