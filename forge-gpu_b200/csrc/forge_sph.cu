@@ -883,6 +883,21 @@ extern "C" int forge_sph_force_step_zone(forge_grid* g, const forge_sph_params* 
                            as_stream(stream));
 }
 
+extern "C" int forge_apply_ops(const forge_step_params* sp, float* px, float* py, float* pz, float* vx, float* vy,
+                               float* vz, uint64_t n, int device, void* stream) {
+    if (!sp) return set_error(FORGE_ERR_INVALID_ARG, "forge_apply_ops: params are NULL");
+    if (sp->n_ops > FORGE_STEP_MAX_OPS) return set_error(FORGE_ERR_INVALID_ARG, "forge_apply_ops: n_ops > 8");
+    if (n >= 0xffffffffull) return set_error(FORGE_ERR_INVALID_ARG, "forge_apply_ops: n too large");
+    if (n == 0 || sp->n_ops == 0) return FORGE_OK;
+    if (!px || !py || !pz || !vx || !vy || !vz)
+        return set_error(FORGE_ERR_INVALID_ARG, "forge_apply_ops: NULL position/velocity pointer");
+    FORGE_DEVICE_SCOPE(device);
+    sph::apply_ops_kernel<<<grid_blocks(n, 256), 256, 0, as_stream(stream)>>>(epi_of(sp), px, py, pz, vx, vy, vz,
+                                                                            (uint32_t)n);
+    FORGE_LAUNCHED();
+    return FORGE_OK;
+}
+
 extern "C" int forge_sph_step(forge_grid* g, const forge_sph_params* p, const forge_step_params* sp, float* px,
                               float* py, float* pz, float* vx, float* vy, float* vz, float* density, uint64_t n,
                               void* stream) {

@@ -776,5 +776,22 @@ __global__ void __launch_bounds__(128, FORGE_FORCE_MIN_BLOCKS)
     }
 }
 
+// The per-particle modules of an unfused pipeline: ep.ops[0..n_ops) in order
+// on each particle, the arithmetic of the fused force epilogue.
+__global__ void __launch_bounds__(256)
+    apply_ops_kernel(StepEpi ep, float* __restrict__ px, float* __restrict__ py, float* __restrict__ pz,
+                     float* __restrict__ vx, float* __restrict__ vy, float* __restrict__ vz, uint32_t n) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    float x = px[i], y = py[i], z = pz[i], u = vx[i], v = vy[i], w = vz[i];
+    apply_ops(ep, x, y, z, u, v, w);
+    px[i] = x;
+    py[i] = y;
+    pz[i] = z;
+    vx[i] = u;
+    vy[i] = v;
+    vz[i] = w;
+}
+
 }  // namespace sph
 }  // namespace forge

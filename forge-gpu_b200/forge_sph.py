@@ -68,7 +68,7 @@ EXPORTED = (
     "forge_sph_force_step",
     "forge_slab_create", "forge_slab_destroy", "forge_slab_classify", "forge_slab_compact",
     "forge_nccl_unique_id", "forge_slab_comm_create", "forge_slab_comm_destroy", "forge_slab_exchange",
-    "forge_slab_exchange_rho", "forge_slab_comm_set_bounds", "forge_slab_comm_set_timeout", "forge_sph_force_step_zone", "forge_slab_exchange_begin", "forge_slab_exchange_end",
+    "forge_apply_ops", "forge_slab_exchange_rho", "forge_slab_comm_set_bounds", "forge_slab_comm_set_timeout", "forge_sph_force_step_zone", "forge_slab_exchange_begin", "forge_slab_exchange_end",
 )
 ZONE_BOUNDARY, ZONE_INTERIOR, ZONE_PREPARE = 1, 2, 3
 STATIC_SORT_MAX_N = 1 << 20
@@ -141,6 +141,7 @@ def lib() -> ctypes.CDLL:
         "forge_slab_comm_create": (i32, [ctypes.c_char_p, i32, i32, i32, u64, f32, f32, f32, pvp]),
         "forge_slab_comm_destroy": (None, [vp]),
         "forge_slab_comm_set_bounds": (i32, [vp, f32, f32]),
+        "forge_apply_ops": (i32, [ctypes.POINTER(StepParams), vp, vp, vp, vp, vp, vp, u64, i32, vp]),
         "forge_slab_comm_set_timeout": (i32, [vp, ctypes.c_double]),
         "forge_slab_exchange": (i32, [vp, vp, u64, u64, i32, ctypes.POINTER(u64), ctypes.POINTER(u64), vp]),
         "forge_slab_exchange_rho": (i32, [vp, vp, vp]),

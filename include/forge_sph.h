@@ -270,6 +270,16 @@ FORGE_API int forge_sph_force(forge_grid* g, const forge_sph_params* p, uint32_t
                     float* vx_out, float* vy_out, float* vz_out,
                     float* ax_out, float* ay_out, float* az_out, void* stream);
 
+/* The per-particle modules of an unfused pipeline on device `device`:
+ * sp->ops[0..n_ops) (FORGE_OP_GRAVITY..FORGE_OP_BOX) applied in order to
+ * each of the n particles in place, with the arithmetic of the fused force
+ * epilogue -- GravityModule (gravity.rs:31-34), DragModule (drag.rs),
+ * IntegrateModule (integrate.rs:16-31), GroundPlaneModule, SphereCollider-
+ * Module, BoxColliderModule (box_collider.rs:36-46). sp->flags is ignored.
+ * Capture-safe. */
+FORGE_API int forge_apply_ops(const forge_step_params* sp, float* px, float* py, float* pz, float* vx, float* vy,
+                              float* vz, uint64_t n, int device, void* stream);
+
 /* One fused SPH step in place on the FieldSet arrays: grid rebuild,
  * density, pressure+viscosity (Jacobi), then the optional gravity /
  * integrate / box epilogue in pipeline order -- the work of

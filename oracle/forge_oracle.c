@@ -520,6 +520,16 @@ static void orc_apply_op(const orc_step_op* o, float dt, float* x, float* y, flo
 
 /* manifest_runner.rs:371-541: SphFused -> Gravity (gravity.rs:31-34) ->
  * Integrate (integrate.rs:16-31) -> BoxCollider (box_collider.rs:26-47). */
+/* The per-particle modules of an unfused pipeline (gravity.rs, drag.rs,
+ * integrate.rs, ground_plane.rs, sphere_collider.rs, box_collider.rs): the
+ * step's op list applied in order to every particle. */
+void orc_apply_ops(const orc_step_params* sp, float* px, float* py, float* pz, float* vx, float* vy, float* vz,
+                   uint64_t n) {
+    for (uint64_t i = 0; i < n; ++i)
+        for (uint32_t k = 0; k < sp->n_ops; ++k)
+            orc_apply_op(&sp->ops[k], sp->dt, &px[i], &py[i], &pz[i], &vx[i], &vy[i], &vz[i]);
+}
+
 void orc_step(const orc_sph_params* p, const orc_step_params* sp, float* px, float* py, float* pz, float* vx,
               float* vy, float* vz, float* density, uint64_t n, float cs, uint32_t nx, uint32_t ny, uint32_t nz,
               uint32_t* work, int threads) {

@@ -98,6 +98,10 @@ void orc_force(const orc_sph_params* p, uint32_t terms, const float* px, const f
                float cs, uint32_t nx, uint32_t ny, uint32_t nz, const uint32_t* cell_start,
                const uint32_t* sorted_idx, float dt, float* vx_out, float* vy_out, float* vz_out,
                float* ax, float* ay, float* az, int threads);
+/* sp->ops[0..n_ops) applied in order to every particle (unfused modules). */
+void orc_apply_ops(const orc_step_params* sp, float* px, float* py, float* pz, float* vx, float* vy, float* vz,
+                   uint64_t n);
+
 /* One manifest step in place: SphFused (grid rebuild, density, fused force)
  * -> Gravity -> Integrate -> BoxCollider (manifest_runner.rs:371-541).
  * `work` must hold 4*n + (C+1) uint32/float words. density nullable. */

@@ -65,6 +65,7 @@ def lib():
                                 _u, _u, f32, _f, _f, _f, vp, vp, vp, i32]
         L.orc_step.argtypes = [ctypes.POINTER(SphParams), ctypes.POINTER(StepParams), _f, _f, _f, _f, _f, _f, vp,
                                u64, f32, u32, u32, u32, _u, i32]
+        L.orc_apply_ops.argtypes = [ctypes.POINTER(StepParams), _f, _f, _f, _f, _f, _f, u64]
         L.orc_max_threads.restype = i32
         _lib = L
     return _lib
@@ -192,6 +193,11 @@ def step(p: SphParams, sp: StepParams, pos, vel, cs, dims, threads=1, want_densi
     lib().orc_step(ctypes.byref(p), ctypes.byref(sp), *pos, *vel, None if rho is None else rho.ctypes.data, n, cs,
                    *dims, work, threads)
     return rho
+
+
+def apply_ops(sp: StepParams, pos, vel) -> None:
+    """sp.ops[0..n_ops) in order on every particle, in place (orc_apply_ops)."""
+    lib().orc_apply_ops(ctypes.byref(sp), *pos, *vel, pos[0].size)
 
 
 def max_threads():

@@ -437,3 +437,31 @@ def test_zoned_prepare_then_late_ghost_densities(cuda):
     want, got = run(False), run(True)
     for a, b in zip(got, want):
         assert np.array_equal(a, b)
+
+
+def test_apply_ops_unfused_modules_vs_oracle(cuda):
+    """forge_apply_ops (the per-particle modules of an unfused pipeline) on
+    every particle, against the oracle applying the same op list."""
+    torch = cuda
+    n = 50_000
+    pos, vel = workloads.uniform_particles(n, seed=17, vsigma=0.5)
+    ops = [(forge_sph.OP_GRAVITY, [0.0, -9.81, 0.0]), (forge_sph.OP_DRAG, [2.0]), (forge_sph.OP_INTEGRATE, []),
+           (forge_sph.OP_GROUND, [0.05, 0.3]), (forge_sph.OP_SPHERE, [0.5, 0.4, 0.5, 0.15, 0.6]),
+           (forge_sph.OP_BOX, [0.0, 0.0, 0.0, 1.0, 1.0, 1.0, 0.8])]
+    sp, osp = forge_sph.StepParams(), oracle.StepParams()
+    for s in (sp, osp):
+        s.dt = 0.05  # large: particles reach the ground, the sphere and the walls
+        s.n_ops = len(ops)
+        for k, (kind, prm) in enumerate(ops):
+            s.ops[k].kind = kind
+            for q, val in enumerate(prm):
+                s.ops[k].p[q] = val
+    p, v = [dev(torch, x) for x in pos], [dev(torch, x) for x in vel]
+    forge_sph.check(forge_sph.lib().forge_apply_ops(ctypes.byref(sp), *(x.data_ptr() for x in p + v), n, 0, None))
+    torch.cuda.synchronize()
+    po, vo = [x.copy() for x in pos], [x.copy() for x in vel]
+    oracle.apply_ops(osp, po, vo)
+    for k in range(3):
+        np.testing.assert_allclose(host_f32(p[k]), po[k], rtol=0, atol=2e-6)
+        np.testing.assert_allclose(host_f32(v[k]), vo[k], rtol=1e-4, atol=2e-5)
+    assert (po[1] == np.float32(0.05)).sum() > 0, "no particle hit the ground plane"
