@@ -349,6 +349,19 @@ def reference_arm(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def sharded_roofline(cfg, phase_ms, n_own_max):
+    """Roofline of the dominant kernel of a sharded step: the force pass of the
+    busiest rank (boundary and interior zones; owned particles only), its
+    algorithmic bytes over the rank's force phase time (CUDA events)."""
+    fms = phase_ms.get("force")
+    if not fms:
+        return None
+    hbm, peak_kind = peaks()
+    achieved = alg_bytes(cfg)["force"] * n_own_max / (fms / 1e3) / 1e9
+    return {"bound": "hbm", "kernel": "force (busiest rank)", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+            "frac": achieved / hbm, "traffic": None, "peak_kind": peak_kind}
+
+
 def run_sharded(args, torch, dist, rank, world, local):
     """N > 1: x-slab decomposition of the workload over `world` GPUs (strong
     scaling: the total particle count is fixed). Halo, ghost-density and
@@ -455,6 +468,7 @@ def run_sharded(args, torch, dist, rank, world, local):
                            % every if every
                            else "uniform", "owned_per_rank_min_max": [n_min, n_max]},
                 "phases_ms_max_over_ranks": phase_ms,
+                "roofline": sharded_roofline(cfg, phase_ms, n_max),
                 "overlap_ms_after_prepare_max_over_ranks": side_ms,
                 "e2e": {"value": cfg.n * e2e_steps / (e2e_ms / 1e3), "unit": "particle-steps/s",
                         "h2d_bytes_per_step": tot_bytes, "d2h_bytes_per_step": tot_bytes},
