@@ -322,6 +322,29 @@ def cpu_threads():
     return oracle.max_threads()
 
 
+def cpu_variants(cfg, pos, vel, phase_ms):
+    """The reference's own CPU path is single-threaded (HashGrid::build,
+    hashgrid.rs:82-125): the oracle step on one thread, and the grid build
+    alone (stable counting sort) on one thread over the whole workload, beside
+    the GPU's grid build (sort + cell table phases)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    m1 = min(pos[0].size, 131_072)
+    p1, v1 = [x[:m1].copy() for x in pos], [x[:m1].copy() for x in vel]
+    t1 = min(cpu_steps(cfg, p1, v1, 1, 1))
+    full, _ = workloads.particles(cfg)
+    t0 = time.perf_counter()
+    oracle.grid_build(*full, cfg.cell_size, cfg.dims)
+    tg = time.perf_counter() - t0
+    gpu_ms = phase_ms["sort"] + phase_ms["cells_gather"]
+    return {"single_thread_step": {"value": m1 / t1, "unit": "particle-steps/s", "cores": 1,
+                                   "sample": f"first {m1} of {cfg.n} particles, 1 oracle step"},
+            "hashgrid_build_single_thread": {"value": cfg.n / tg, "unit": "particles/s", "cores": 1,
+                                             "sample": f"all {cfg.n} particles, one build"},
+            "hashgrid_build_gpu": {"value": cfg.n / (gpu_ms / 1e3), "unit": "particles/s",
+                                   "sample": "sort + cell-table phases of the timed steps"}}
+
+
 CPU_SAMPLE = {"sharded16m": 1_024_000, "dambreak1m": 262_144, "dambreak1m_h025": 131_072, "blobs4m": 262_144,
               "ref65k": 65_536}
 
@@ -560,6 +583,7 @@ def main():
         t = min(times)
         line["cpu_baseline"] = {"value": m / t, "unit": "particle-steps/s", "cores": th, "kind": "port",
                                 "sample": f"first {m} of {cfg.n} particles, 2 oracle steps, best of 2"}
+        line["cpu_baseline_variants"] = cpu_variants(cfg, cp, cv, phase_ms)
     if not args.no_extra and cfg.name != "dambreak1m":
         extra = {}
         c1 = workloads.config("dambreak1m")
