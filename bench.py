@@ -510,6 +510,8 @@ def main():
                     choices=["sharded16m", "dambreak1m", "dambreak1m_h025", "dambreak65k", "blobs4m", "ref65k"])
     ap.add_argument("--no-extra", action="store_true", help="skip the 1M dam-break and 2^28 sort extras")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
+    ap.add_argument("--sort-only", type=int, default=None, metavar="LOG2N",
+                    help="time only the standalone key/value sort of 2^LOG2N uniform pairs (for profiling)")
     ap.add_argument("--rebalance-every", type=int, default=None,
                     help="N>1: slab bounds at particle-count quantiles, rebalanced every K steps (0: uniform "
                          "slabs; default: 10 for blobs4m, uniform otherwise)")
@@ -528,6 +530,10 @@ def main():
     import torch
     import forge_sph
     torch.cuda.set_device(local)
+    if args.sort_only is not None:
+        r = sort_rate(torch, forge_sph, "uniform", 1 << args.sort_only, steps=args.steps, warmup=args.warmup)
+        print(json.dumps({"sort_only": f"2^{args.sort_only} uniform u32 pairs", **r}), flush=True)
+        return
     dist = None
     if world > 1:
         import torch.distributed as dist
