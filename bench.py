@@ -401,7 +401,7 @@ def run_sharded(args, torch, dist, rank, world, local):
     balance = args.rebalance_every > 0 if args.rebalance_every is not None else cfg.name == "blobs4m"
     every = (args.rebalance_every or 10) if balance else 0
     run = slab.SlabRun(dist, rank, world, cfg, pos, vel, be, dev, capacity=cap, comm=args.comm, forge_sph=forge_sph,
-                       balance=balance)
+                       balance=balance, halo_width=args.halo_width)
     del pos, vel
     count = [0]
 
@@ -486,7 +486,7 @@ def run_sharded(args, torch, dist, rank, world, local):
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic",
                 "config": {"workload": cfg.name, "particles": cfg.n, "cells": cfg.cells, "h": cfg.h,
                            "inputs_exceed_l2": True, "parallelism": f"x-slab over {world} GPUs (NCCL send/recv, exchange={args.comm})",
-                           "max_halo_particles_per_rank": halo,
+                           "max_halo_particles_per_rank": halo, "halo_width_h": args.halo_width,
                            "slab_bounds": "initial particle-count quantiles, rebalanced on the density-weighted x-histogram every %d steps"
                            % every if every
                            else "uniform", "owned_per_rank_min_max": [n_min, n_max]},
@@ -515,6 +515,8 @@ def main():
     ap.add_argument("--rebalance-every", type=int, default=None,
                     help="N>1: slab bounds at particle-count quantiles, rebalanced every K steps (0: uniform "
                          "slabs; default: 10 for blobs4m, uniform otherwise)")
+    ap.add_argument("--halo-width", type=float, choices=[1.0, 2.0], default=1.0,
+                    help="N>1: halo of h with a ghost-density round, or of 2h with ghost densities computed locally")
     ap.add_argument("--comm", choices=["nccl", "torch"], default="nccl",
                     help="N>1 exchange: in the library over NCCL, or in Python over torch.distributed")
     args = ap.parse_args()

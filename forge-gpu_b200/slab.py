@@ -425,10 +425,16 @@ class SlabRun:
 
     def __init__(self, dist, rank: int, world: int, cfg, pos, vel, backend, device: torch.device,
                  x_range=(0.0, 1.0), order_by_id: bool = False, comm_device=None, capacity: int | None = None,
-                 comm: str = "torch", forge_sph=None, balance: bool = False, hist_bins: int = 4096):
+                 comm: str = "torch", forge_sph=None, balance: bool = False, hist_bins: int = 4096,
+                 halo_width: float = 1.0):
         self.cfg, self.backend, self.device = cfg, backend, device
         self.dist, self.x_range, self.hist_bins = dist, x_range, hist_bins
-        self.reach = cfg.h * (1.0 + 1e-5)
+        # halo_width 2: ghosts within 2h of a face, so the ghosts within h get
+        # their exact densities locally and round 2 (ghost densities) is skipped
+        if halo_width not in (1.0, 2.0):
+            raise ValueError("halo_width is 1 (h, ghost densities exchanged) or 2 (2h, computed locally)")
+        self.reach = cfg.h * halo_width * (1.0 + 1e-5)
+        self.local_ghost_density = halo_width == 2.0
         self.geo = SlabGeometry(rank, world, x_range[0], x_range[1], cfg.h)
         if balance:  # initial bounds at the quantiles of the (identical on every rank) initial positions
             hist = np.histogram(np.asarray(pos[0], np.float64), bins=hist_bins, range=x_range)[0]
@@ -546,7 +552,8 @@ class SlabRun:
             rho = r
             C[:, perm] = C[:, :n].clone()
         self._mark("density")
-        self.comm.exchange_rho(rho)
+        if not self.local_ghost_density:
+            self.comm.exchange_rho(rho)
         self._mark("ghost_rho")
         self._note_work(C[0, :n_own], rho[:n_own])  # owned-then-ghost layout here in both modes
         if perm is not None:
@@ -596,7 +603,8 @@ class SlabRun:
             self._hp = torch.cuda.Stream(device=main.device, priority=-1)
         self._hp.wait_stream(main)
         with torch.cuda.stream(self._hp):
-            self.comm.exchange_rho(rho)
+            if not self.local_ghost_density:
+                self.comm.exchange_rho(rho)
             self._mark_side("ghost_rho_done")
             self.backend.force_step(cols6, rho, n, n_own, zone=(1,) + zones)
             self._mark_side("boundary_done")

@@ -69,14 +69,14 @@ class OracleBackend:
             a[3 + k][:n_update] = u
 
 
-def _rank_main(rank, world, port, out_path):
+def _rank_main(rank, world, port, out_path, halo_width=1.0):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         cfg = _cfg()
         pos, vel = _inputs(cfg)
         run = slab.SlabRun(dist, rank, world, cfg, pos, vel, OracleBackend(cfg), torch.device("cpu"),
-                           order_by_id=True)
+                           order_by_id=True, halo_width=halo_width)
         first_owner = run.ids().clone()
         halo = 0
         for _ in range(STEPS):
@@ -99,10 +99,13 @@ def _free_port():
     return p
 
 
-@pytest.mark.parametrize("world", [2, 3])
-def test_sharded_step_matches_single_process(tmp_path, world):
+@pytest.mark.parametrize("world,halo_width", [(2, 1.0), (3, 1.0), (3, 2.0)])
+def test_sharded_step_matches_single_process(tmp_path, world, halo_width):
+    """halo_width 2: a 2h halo, ghost densities computed locally (no density
+    round) -- the same trajectory bit for bit."""
     out = str(tmp_path / "states.npy")
-    mp.start_processes(_rank_main, args=(world, _free_port(), out), nprocs=world, join=True, start_method="spawn")
+    mp.start_processes(_rank_main, args=(world, _free_port(), out, halo_width), nprocs=world, join=True,
+                       start_method="spawn")
     states = np.load(out, allow_pickle=True)
     rows = np.concatenate([s[0] for s in states])
     assert sum(s[1] for s in states) > 0, "no particle migrated: the test does not exercise migration"
