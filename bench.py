@@ -322,6 +322,25 @@ def cpu_threads():
     return oracle.max_threads()
 
 
+PUBLISHED_DAM_BREAK_L40 = 3.04e8  # `forge run dam-break.toml`, particle-steps/s on an L40 (the reference's README)
+
+
+def dam_break_manifest(device):
+    """The reference's published workload through the `forge run` path
+    (manifest.py): 50K-particle dam break, 20,000 steps, timed end to end
+    like the reference's CLI (warm-up, graph capture and replays)."""
+    try:
+        import manifest
+        m = manifest.Manifest.from_file(os.path.join(ROOT, "forge-gpu_b200", "examples", "dam_break_50k.toml"))
+        r = manifest.run_manifest(m, device=device, seed=0)
+        return {"value": r.throughput, "unit": "particle-steps/s", "particles": r.count, "steps": r.steps,
+                "seconds": r.elapsed_secs, "published_l40": PUBLISHED_DAM_BREAK_L40,
+                "vs_published_l40": r.throughput / PUBLISHED_DAM_BREAK_L40,
+                "timing": "wall clock of run_manifest (warm-up + capture + replays), as the reference's CLI"}
+    except Exception as e:  # an extra: a failure here must not lose the bench line
+        return {"error": repr(e)[:300]}
+
+
 def cpu_variants(cfg, pos, vel, phase_ms):
     """The reference's own CPU path is single-threaded (HashGrid::build,
     hashgrid.rs:82-125): the oracle step on one thread, and the grid build
@@ -607,6 +626,8 @@ def main():
                                     "ms_per_step": ms2 / 20, "phases_ms": ph2,
                                     "l2_flushed_between_steps": r2.l2_flushed, "h": c2.h, "particles_per_cell": 125}
         del r2
+        torch.cuda.empty_cache()
+        extra["dam_break_50k_manifest"] = dam_break_manifest(local)
         torch.cuda.empty_cache()
         for kind in ("uniform", "morton"):
             extra["radix_sort_2^28_" + kind] = sort_rate(torch, forge_sph, kind, 1 << 28)
