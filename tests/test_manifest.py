@@ -137,3 +137,18 @@ def test_unfused_pipeline_order_and_rejections():
         manifest.build_pipeline(manifest.Manifest.from_toml(DAM + '\n[[forces]]\ntype = "custom"\nexpr = "v"\n'))
     with pytest.raises(manifest.ManifestError, match="springs"):
         manifest.build_pipeline(manifest.Manifest.from_toml(DAM + '\n[springs]\nstiffness = 1.0\ndamping = 0.1\n'))
+
+
+def test_example_dam_break_manifest():
+    """The shipped example (the reference's published 50K dam-break workload)
+    parses, validates and fuses into one forge_sph_step per substep."""
+    import os
+    path = os.path.join(os.path.dirname(manifest.__file__), "examples", "dam_break_50k.toml")
+    m = manifest.Manifest.from_file(path)
+    assert manifest.validate(m) == []
+    assert m.particle_count() == 50000 and m.total_steps() == 2000 and m.simulation["substeps"] == 10
+    p = manifest.build_pipeline(m)
+    assert [x.name() for x in p.modules] == ["sph_fused", "gravity", "integrate", "box_collider"]
+    assert p._fused_plan() is not None
+    sph = p.modules[0]
+    assert (sph.smoothing_radius, sph.cell_size, tuple(sph.grid_dims)) == (0.025, 0.05, (40, 60, 20))
