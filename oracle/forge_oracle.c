@@ -10,7 +10,9 @@
  * Parity: grid build / radix sort / find_cell_boundaries / query are pinned
  * by the reference's known-answer tests (tests/golden fixtures). SPH density
  * and force: parity unpinned by reference fixtures (the reference has no SPH
- * unit test); they restate the kernel strings cited per function.
+ * unit test); they restate the kernel strings cited per function and are
+ * cross-checked against fp64 all-pairs evaluations of the same formulas
+ * (tests/test_oracle.py).
  */
 #include "forge_oracle.h"
 
