@@ -71,9 +71,9 @@ def _free_port():
     return p
 
 
-def _sharded_rows(tmp_path, order_by_id, skewed=False):
+def _sharded_rows(tmp_path, order_by_id, skewed=False, world=2):
     out = str(tmp_path / "states.npy")
-    mp.start_processes(_rank_main, args=(2, _free_port(), out, order_by_id, skewed), nprocs=2, join=True,
+    mp.start_processes(_rank_main, args=(world, _free_port(), out, order_by_id, skewed), nprocs=world, join=True,
                        start_method="spawn")
     rows = np.concatenate(list(np.load(out, allow_pickle=True)))
     ids = rows[:, 6].copy().view(np.int32)
@@ -103,6 +103,20 @@ two_gpus = pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device
 def test_nccl_sharded_step_matches_single_gpu(cuda, tmp_path):
     """Test mode (local arrays in particle-id order each step): bit for bit."""
     assert np.array_equal(_sharded_rows(tmp_path, True), _single_gpu_rows())
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 4, reason="needs 4 GPUs")
+@pytest.mark.parametrize("order_by_id", [True, False])
+def test_nccl_four_ranks(cuda, tmp_path, order_by_id):
+    """Four ranks: the two middle ones exchange with both neighbours. Test
+    mode bit for bit; the overlapped production step within fp32 summation
+    order (as in the two-rank test)."""
+    got, want = _sharded_rows(tmp_path, order_by_id, world=4), _single_gpu_rows()
+    if order_by_id:
+        assert np.array_equal(got, want)
+    else:
+        np.testing.assert_allclose(got[:, :3], want[:, :3], rtol=0, atol=1e-5)
+        np.testing.assert_allclose(got[:, 3:], want[:, 3:], rtol=0, atol=1e-3)
 
 
 @two_gpus
