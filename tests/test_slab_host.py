@@ -68,3 +68,12 @@ def test_force_zones_guard_and_margin(rank, world):
     else:
         assert guard_hi == float(f32(g.hi) - f32(reach))
         assert inner_hi < guard_hi
+
+
+def test_halo_width_is_one_or_two():
+    import torch
+    import workloads
+    cfg = workloads.small("ref65k", 100, (8, 8, 8))
+    pos, vel = workloads.uniform_particles(cfg.n, seed=1)
+    with pytest.raises(ValueError, match="halo_width"):
+        slab.SlabRun(None, 0, 1, cfg, pos, vel, None, torch.device("cpu"), halo_width=1.5)
