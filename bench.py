@@ -10,8 +10,10 @@ workload is cfg3 (16,384,000 particles, 160^3 cells), the config the metric
 quotes at 1/2/4/8 GPUs; at N=1 the line also carries the 1M dam-break step
 rate and the 2^28-pair radix sort rate under "extra".
 
---impl reference times the reference algorithm's CPU implementation (the
-oracle port; the Rust reference cannot be built here) on the host cores.
+--impl reference times the reference's CPU path on the host cores: its own
+SPH and module kernels (CUDA C strings) built for the host by
+`make -C oracle ref`, or the oracle port of the same step where that build is
+absent (the Rust reference itself cannot be built here).
 """
 from __future__ import annotations
 
@@ -31,10 +33,13 @@ import numpy as np  # noqa: E402
 
 import workloads  # noqa: E402
 
-# DRAM bytes (read + write) per force+epilogue launch per particle, from the
-# ncu capture in profiles/sph_step_sharded16m_ncu.md (755 + 381 MB for 16,384,000
-# particles, cfg3); applied to cfg3-like workloads only.
-FORCE_TRAFFIC_B_PER_PARTICLE = 1136.0e6 / 16384000
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per particle of
+# one launch of the dominant kernel, from an ncu capture of
+# `bench.py --steps 2 --warmup 3 --no-extra --no-cpu` on a B200 (the kernel's
+# traffic grows with the particle count, so it is quoted per particle).
+# bench.py cannot read DRAM counters itself; the figure is refreshed with each
+# capture of a changed kernel.
+NCU_TRAFFIC_B_PER_PARTICLE = {("sharded16m", "force"): 1136.0e6 / 16384000}
 
 
 def peaks():
@@ -317,9 +322,42 @@ def cpu_steps(cfg, pos, vel, steps, threads):
 
 
 def cpu_threads():
+    """Every core this process may run on. Counted from the affinity mask,
+    not omp_get_max_threads(): torchrun sets OMP_NUM_THREADS=1 for its ranks,
+    and the CPU baseline must not inherit that."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def cpu_reference_steps(cfg, pos, vel, steps, threads):
+    """The timed CPU reference: the reference's own kernels built for the
+    host (oracle/_ref/libref.so: its unfused manifest step, threads in
+    parallel) where that library was built, else the oracle port of the same
+    step. Returns (per-step seconds, kind)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle
-    return oracle.max_threads()
+    import ref
+    if not ref.available():
+        return cpu_steps(cfg, pos, vel, steps, threads), "port"
+    run = ref.ManifestStep(cfg, pos[0].size)
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        run(pos, vel, threads)
+        times.append(time.perf_counter() - t0)
+    return times, "reference"
 
 
 PUBLISHED_DAM_BREAK_L40 = 3.04e8  # `forge run dam-break.toml`, particle-steps/s on an L40 (the reference's README)
@@ -375,18 +413,20 @@ def reference_arm(args, rank, world):
     m = CPU_SAMPLE.get(args.workload, 262_144)
     pos, vel, m = cpu_sample(cfg, m)
     th = cpu_threads()
-    cpu_steps(cfg, pos, vel, args.warmup, th)
-    times = cpu_steps(cfg, pos, vel, args.steps, th)
+    cpu_reference_steps(cfg, pos, vel, args.warmup, th)
+    times, kind = cpu_reference_steps(cfg, pos, vel, args.steps, th)
     t = sum(times) / len(times)
     val = m / t
-    sample = f"first {m} of {cfg.n} particles ({cfg.name}), oracle port of the manifest step, {th} OpenMP threads"
+    what = ("the reference's own kernels (unfused manifest step) built for the host" if kind == "reference"
+            else "oracle port of the manifest step")
+    sample = f"first {m} of {cfg.n} particles ({cfg.name}), {what}, {th} OpenMP threads on {cpu_model()}"
     line = {"metric": "SPH particle-steps/s", "value": val, "unit": "particle-steps/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "impl": "reference",
             "config": {"workload": cfg.name, "particles": cfg.n, "cells": cfg.cells, "h": cfg.h},
-            "cpu_baseline": {"value": val, "unit": "particle-steps/s", "cores": th, "kind": "port",
-                             "sample": sample},
+            "cpu_baseline": {"value": val, "unit": "particle-steps/s", "cores": th, "kind": kind,
+                             "cpu": cpu_model(), "sample": sample},
             "e2e": {"value": val, "unit": "particle-steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -419,7 +459,7 @@ def run_sharded(args, torch, dist, rank, world, local):
     # skewed workloads: bounds at particle-count quantiles, rebalanced every k steps
     balance = args.rebalance_every > 0 if args.rebalance_every is not None else cfg.name == "blobs4m"
     every = (args.rebalance_every or 10) if balance else 0
-    run = slab.SlabRun(dist, rank, world, cfg, pos, vel, be, dev, capacity=cap, comm=args.comm, forge_sph=forge_sph,
+    run = slab.SlabRun(dist, rank, world, cfg, pos, vel, be, dev, capacity=cap, comm="nccl", forge_sph=forge_sph,
                        balance=balance, halo_width=args.halo_width)
     del pos, vel
     count = [0]
@@ -504,7 +544,7 @@ def run_sharded(args, torch, dist, rank, world, local):
                 "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic",
                 "config": {"workload": cfg.name, "particles": cfg.n, "cells": cfg.cells, "h": cfg.h,
-                           "inputs_exceed_l2": True, "parallelism": f"x-slab over {world} GPUs (NCCL send/recv, exchange={args.comm})",
+                           "inputs_exceed_l2": True, "parallelism": f"x-slab over {world} GPUs (NCCL send/recv in the library)",
                            "max_halo_particles_per_rank": halo, "halo_width_h": args.halo_width,
                            "slab_bounds": "initial particle-count quantiles, rebalanced on the density-weighted x-histogram every %d steps"
                            % every if every
@@ -536,8 +576,6 @@ def main():
                          "slabs; default: 10 for blobs4m, uniform otherwise)")
     ap.add_argument("--halo-width", type=float, choices=[1.0, 2.0], default=1.0,
                     help="N>1: halo of h with a ghost-density round, or of 2h with ghost densities computed locally")
-    ap.add_argument("--comm", choices=["nccl", "torch"], default="nccl",
-                    help="N>1 exchange: in the library over NCCL, or in Python over torch.distributed")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -573,8 +611,8 @@ def main():
     dom = max(PHASES, key=lambda k: phase_ms[k])
     achieved = ab[dom] * cfg.n / (phase_ms[dom] / 1e3) / 1e9
     traffic = None
-    if dom == "force" and cfg.name == "sharded16m":
-        traffic = FORCE_TRAFFIC_B_PER_PARTICLE * cfg.n
+    if (cfg.name, dom) in NCU_TRAFFIC_B_PER_PARTICLE:
+        traffic = NCU_TRAFFIC_B_PER_PARTICLE[(cfg.name, dom)] * cfg.n
     pairs = lattice_pairs(cfg)
     phases = {k: {"ms": phase_ms[k], "alg_bytes_per_particle": ab[k],
                   "achieved_gbs": ab[k] * cfg.n / (phase_ms[k] / 1e3) / 1e9,
@@ -606,10 +644,12 @@ def main():
         m = CPU_SAMPLE.get(cfg.name, 262_144)
         cp, cv, m = cpu_sample(cfg, m)
         th = cpu_threads()
-        times = cpu_steps(cfg, cp, cv, 2, th)
+        times, kind = cpu_reference_steps(cfg, cp, cv, 2, th)
         t = min(times)
-        line["cpu_baseline"] = {"value": m / t, "unit": "particle-steps/s", "cores": th, "kind": "port",
-                                "sample": f"first {m} of {cfg.n} particles, 2 oracle steps, best of 2"}
+        what = "reference kernels built for the host" if kind == "reference" else "oracle port"
+        line["cpu_baseline"] = {"value": m / t, "unit": "particle-steps/s", "cores": th, "kind": kind,
+                                "cpu": cpu_model(),
+                                "sample": f"first {m} of {cfg.n} particles, 2 steps ({what}), best of 2"}
         line["cpu_baseline_variants"] = cpu_variants(cfg, cp, cv, phase_ms)
     if not args.no_extra and cfg.name != "dambreak1m":
         extra = {}

@@ -281,22 +281,58 @@ static __device__ __align__(256) uint32_t g_static_sort_scratch[kStaticWords];
 
 // Device address of g_static_sort_scratch per device ordinal. In host code the
 // symbol's name is only a host-side stand-in, so the address is looked up
-// with cudaGetSymbolAddress (once per device, with that device current).
+// with cudaGetSymbolAddress (with that device current). The lookup is cached
+// together with the unique id of the CUDA context it was made in: after a
+// cudaDeviceReset, or under another context, the module (and the array) may
+// be loaded again at another address, and the next call looks it up anew.
 std::mutex g_static_mu;
-uint32_t* g_static_addr[64] = {};
+struct StaticAddr {
+    uint32_t* addr = nullptr;
+    unsigned long long ctx_id = 0;
+};
+StaticAddr g_static_addr[64];
+
+// Unique id of the calling thread's current context (cuCtxGetCurrent +
+// cuCtxGetId through the runtime's driver entry points, so the library need
+// not link libcuda); 0 if unavailable.
+unsigned long long current_ctx_id() {
+    using GetCurrent = int (*)(void**);
+    using GetId = int (*)(void*, unsigned long long*);
+    static GetCurrent get_current = nullptr;
+    static GetId get_id = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<GetCurrent>(f);
+        f = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<GetId>(f);
+    });
+    void* ctx = nullptr;
+    unsigned long long id = 0;
+    if (get_current && get_id && get_current(&ctx) == 0 && ctx && get_id(ctx, &id) == 0) return id;
+    return 0;
+}
 
 int static_scratch(int dev, uint32_t** out) {
     if (dev < 0 || dev >= 64) return set_error(FORGE_ERR_INVALID_ARG, "forge_sort_pairs_static: device %d", dev);
+    const unsigned long long ctx = current_ctx_id();
     std::lock_guard<std::mutex> lock(g_static_mu);
-    if (!g_static_addr[dev]) {
+    StaticAddr& a = g_static_addr[dev];
+    if (!a.addr || ctx == 0 || a.ctx_id != ctx) {
         void* p = nullptr;
         cudaError_t e = cudaGetSymbolAddress(&p, g_static_sort_scratch);
         if (e != cudaSuccess)
             return set_error(FORGE_ERR_CUDA, "forge_sort_pairs_static: cudaGetSymbolAddress failed: %s",
                              cudaGetErrorString(e));
-        g_static_addr[dev] = static_cast<uint32_t*>(p);
+        a.addr = static_cast<uint32_t*>(p);
+        a.ctx_id = ctx;
     }
-    *out = g_static_addr[dev];
+    *out = a.addr;
     return FORGE_OK;
 }
 

@@ -226,7 +226,10 @@ __global__ void __launch_bounds__(128)
                 for (uint32_t s = b; s < e; ++s) {
                     const uint32_t j = sorted_idx[s];
                     const float ddx = px[j] - x, ddy = py[j] - y, ddz = pz[j] - z;
-                    const float d2 = ddx * ddx + ddy * ddy + ddz * ddz;
+                    // every product and sum rounded on its own, as hashgrid.rs:183-184
+                    // evaluates it (no FMA contraction), so d2 <= r2 is decided
+                    // exactly as the reference decides it, also at d2 == r2
+                    const float d2 = __fadd_rn(__fadd_rn(__fmul_rn(ddx, ddx), __fmul_rn(ddy, ddy)), __fmul_rn(ddz, ddz));
                     if (d2 <= r2) {
                         if (WRITE) hits[out + cnt] = j;
                         ++cnt;

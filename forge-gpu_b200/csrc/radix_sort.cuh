@@ -41,23 +41,6 @@ constexpr uint64_t kMaxN = (1ull << 29) - 1;
 
 constexpr int kHistThreads = 256;
 
-#ifdef FORGE_SORT_PHASES
-// Probe-only instrumentation: per-tile %globaltimer stamps at phase
-// boundaries (never compiled into the library).
-__device__ unsigned long long* g_phase_buf;
-#define FORGE_PHASE_MARK(tile, k)                                                          \
-    do {                                                                                   \
-        if (threadIdx.x == 0) {                                                            \
-            unsigned long long t_;                                                         \
-            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                         \
-            g_phase_buf[(size_t)(tile) * 8 + (k)] = t_;                                    \
-        }                                                                                  \
-    } while (0)
-#else
-#define FORGE_PHASE_MARK(tile, k) \
-    do {                          \
-    } while (0)
-#endif
 constexpr int kHistItems = 8;
 
 __host__ __device__ constexpr uint32_t num_tiles(uint64_t n) {
@@ -178,7 +161,6 @@ __global__ void __launch_bounds__(kThreads, 4)
     __syncthreads();
 
     const uint32_t tile = s_tile;
-    FORGE_PHASE_MARK(tile, 0);
     const uint32_t tile_start = tile * kTile;
     const uint32_t mask = (1u << bits) - 1u;
     const uint32_t warp_start = tile_start + warp * 32 * kItems;
@@ -195,7 +177,6 @@ __global__ void __launch_bounds__(kThreads, 4)
         else val[k] = ok ? vals_in[idx] : 0u;
     }
 
-    FORGE_PHASE_MARK(tile, 1);  // loads issued
     // Early counts: per-warp digit histograms from shared atomics (a warp
     // whose keys share one digit adds 32 once), so the tile aggregate is
     // published before the ranking and successors' look-backs do not wait
@@ -220,7 +201,6 @@ __global__ void __launch_bounds__(kThreads, 4)
     uint32_t cnt = 0;
 #pragma unroll
     for (int w = 0; w < kWarps; ++w) cnt += s_whist[w][tid];
-    FORGE_PHASE_MARK(tile, 2);  // counted
     uint32_t* my_status = status + (size_t)tile * kRadix + tid;
     const uint32_t par = parity ? kParityBit : 0u;
     st_relaxed_u32(my_status, par | (tile == 0 ? kFlagPre : kFlagAgg) | cnt);
@@ -259,7 +239,6 @@ __global__ void __launch_bounds__(kThreads, 4)
         if (ok) s_exchange[pos[k]] = key[k];
     }
 
-    FORGE_PHASE_MARK(tile, 3);  // aggregate published, scans done
     // Decoupled look-back for digit tid. The nearest inclusive prefix is
     // typically ~20 tiles back with every aggregate already published, so
     // kLookBatch status words are loaded per round trip and consumed in order
@@ -301,13 +280,9 @@ __global__ void __launch_bounds__(kThreads, 4)
             }
         }
         st_relaxed_u32(my_status, par | kFlagPre | ((excl + cnt) & kCountMask));
-#ifdef FORGE_SORT_PHASES
-        if (tid == 0) g_phase_buf[(size_t)tile * 8 + 6] = ((unsigned long long)spins << 32) | (uint32_t)((int)tile - 1 - t);
-#endif
     }
     s_base[tid] = hist_off + excl - tile_off;
     __syncthreads();
-    FORGE_PHASE_MARK(tile, 4);  // look-back done
 
     const uint32_t tile_n = min((uint32_t)kTile, n - tile_start);
     uint32_t dst[kItems];
@@ -332,7 +307,6 @@ __global__ void __launch_bounds__(kThreads, 4)
         if (j < tile_n) vals_out[dst[k]] = s_exchange[j];
     }
     __syncthreads();
-    FORGE_PHASE_MARK(tile, 5);  // written
 }
 
 }  // namespace radix

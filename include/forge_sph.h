@@ -105,8 +105,9 @@ FORGE_API int forge_sorter_sort_pairs(forge_sorter* s, uint32_t* keys, uint32_t*
  * Its scratch (look-back table, digit histograms, one alternate key/value
  * pair) is a fixed ~8.3 MiB array inside the library that every GPU which
  * loads the library holds until process exit. Runs on the calling thread's
- * current device. The first call on a device looks the array up (once per
- * device): make that first call before any stream capture. All calls share
+ * current device. The first call on a device (and the first after a
+ * cudaDeviceReset or under another CUDA context) looks the array up: make
+ * that first call before any stream capture. All calls share
  * the array, so calls whose work overlaps on the GPU (different streams, or
  * different host threads on one device) race; serialise them. A device-side
  * wait that gives up is not reported by this entry point (use the

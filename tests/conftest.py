@@ -9,7 +9,8 @@ import sys
 import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-for p in (os.path.join(ROOT, "forge-gpu_b200"), os.path.join(ROOT, "oracle"), ROOT):
+for p in (os.path.join(ROOT, "forge-gpu_b200"), os.path.join(ROOT, "oracle"), os.path.join(ROOT, "tests", "golden"),
+          ROOT):
     if p not in sys.path:
         sys.path.insert(0, p)
 

@@ -124,3 +124,30 @@ def test_build_is_deterministic(cuda):
     for _ in range(3):
         g.build(t)
         assert np.array_equal(host_u32(g.sorted_indices), a)
+
+
+def test_query_points_on_the_radius(cuda):
+    """Particles placed on spheres of the query radius around each query
+    point, so dist^2 lands within an ulp or two of r^2: the <= test must be
+    decided with every operation rounded, as hashgrid.rs:183-184 does (an
+    FMA-contracted dist^2 flips some of these)."""
+    rng = np.random.default_rng(77)
+    nq, per = 200, 64
+    cs, dims, radius = 0.05, (20, 20, 20), 0.05
+    q = rng.uniform(0.1, 0.9, (nq, 3)).astype(np.float32)
+    u = rng.normal(size=(nq, per, 3))
+    u /= np.linalg.norm(u, axis=2, keepdims=True)
+    p = (q[:, None, :].astype(np.float64) + radius * u).astype(np.float32).reshape(-1, 3)
+    pos = [np.ascontiguousarray(p[:, k]) for k in range(3)]
+    qs = [np.ascontiguousarray(q[:, k]) for k in range(3)]
+    g = forge_sph.HashGrid(cs, dims, (0, 0, 0), p.shape[0], 0)
+    g.build(tuple(dev(cuda, a) for a in pos))
+    counts, offsets, hits = g.query_batch(*(dev(cuda, a) for a in qs), radius)
+    counts, offsets, hits = host_u32(counts), host_u32(offsets), host_u32(hits)
+    ci, si, cst = oracle.grid_build(*pos, cs, dims)
+    on_edge = 0
+    for i in range(nq):
+        e = oracle.query(*pos, cst, si, cs, dims, (qs[0][i], qs[1][i], qs[2][i]), radius)
+        assert np.array_equal(hits[offsets[i]:offsets[i + 1]], e), i
+        on_edge += per - int(np.count_nonzero((e >= i * per) & (e < (i + 1) * per)))
+    assert 0 < on_edge < nq * per  # the case really straddles the radius

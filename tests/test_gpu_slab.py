@@ -15,6 +15,7 @@ import torch.multiprocessing as mp
 
 import forge_sph
 import slab
+import slab_cpu
 import workloads
 
 pytestmark = pytest.mark.gpu
@@ -40,7 +41,7 @@ def _rank_main(rank, world, port, out_path):
         pos, vel = _inputs(cfg)
         be = slab.GpuBackend(forge_sph, cfg, cfg.n, 0)
         run = slab.SlabRun(dist, rank, world, cfg, pos, vel, be, torch.device("cuda", 0), order_by_id=True,
-                           comm_device="cpu")
+                           comm=lambda r: slab_cpu.PyComm(r, dist, comm_device="cpu"))
         for _ in range(STEPS):
             run.step()
         be.grid.check()
@@ -92,13 +93,13 @@ def test_slab_classify_and_compact_match_torch(cuda, n):
     be = slab.GpuBackend(forge_sph, cfg, max(n, 1), 0)
     for flags in (1, 2, 3, 5, 6, 7, 13, 14, 15):
         got = be.classify(x, n, 0.25, 0.75, 0.05, flags)
-        want = slab.torch_classify(x, n, 0.25, 0.75, 0.05, flags)
+        want = slab_cpu.torch_classify(x, n, 0.25, 0.75, 0.05, flags)
         for a, b in zip(got, want):
             assert torch_.equal(a, b), flags
-    mig = slab.torch_classify(x, n, 0.25, 0.75, 0.05, 3)[0]
+    mig = slab_cpu.torch_classify(x, n, 0.25, 0.75, 0.05, 3)[0]
     cols = torch_.rand((7, n + 5), generator=g).cuda()
     ref = cols.clone()
     be.compact(cols, n, mig)
-    slab.torch_compact(ref, n, mig)
+    slab_cpu.torch_compact(ref, n, mig)
     keep = n - mig.numel()
     assert torch_.equal(cols[:, :keep], ref[:, :keep])

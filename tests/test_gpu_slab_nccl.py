@@ -40,7 +40,7 @@ def _skewed(cfg):
     return pos, [rng.normal(0.0, 1.0, n).astype(np.float32) for _ in range(3)]
 
 
-def _rank_main(rank, world, port, out_path, order_by_id=True, skewed=False):
+def _rank_main(rank, world, port, out_path, order_by_id=True, skewed=False, halo_width=1.0):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)  # plumbing: the NCCL id broadcast
     try:
@@ -49,7 +49,8 @@ def _rank_main(rank, world, port, out_path, order_by_id=True, skewed=False):
         pos, vel = _skewed(cfg) if skewed else _inputs(cfg)
         be = slab.GpuBackend(forge_sph, cfg, cfg.n, rank)
         run = slab.SlabRun(dist, rank, world, cfg, pos, vel, be, torch.device("cuda", rank), order_by_id=order_by_id,
-                           capacity=cfg.n + 8, comm="nccl", forge_sph=forge_sph, balance=skewed, hist_bins=256)
+                           capacity=cfg.n + 8, comm="nccl", forge_sph=forge_sph, balance=skewed, hist_bins=256,
+                           halo_width=halo_width)
         for s in range(STEPS):
             run.step()
             if skewed and s % 2 == 1:
@@ -71,9 +72,9 @@ def _free_port():
     return p
 
 
-def _sharded_rows(tmp_path, order_by_id, skewed=False, world=2):
+def _sharded_rows(tmp_path, order_by_id, skewed=False, world=2, halo_width=1.0):
     out = str(tmp_path / "states.npy")
-    mp.start_processes(_rank_main, args=(world, _free_port(), out, order_by_id, skewed), nprocs=world, join=True,
+    mp.start_processes(_rank_main, args=(world, _free_port(), out, order_by_id, skewed, halo_width), nprocs=world, join=True,
                        start_method="spawn")
     rows = np.concatenate(list(np.load(out, allow_pickle=True)))
     ids = rows[:, 6].copy().view(np.int32)
@@ -100,9 +101,12 @@ two_gpus = pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device
 
 
 @two_gpus
-def test_nccl_sharded_step_matches_single_gpu(cuda, tmp_path):
-    """Test mode (local arrays in particle-id order each step): bit for bit."""
-    assert np.array_equal(_sharded_rows(tmp_path, True), _single_gpu_rows())
+@pytest.mark.parametrize("halo_width", [1.0, 2.0])
+def test_nccl_sharded_step_matches_single_gpu(cuda, tmp_path, halo_width):
+    """Test mode (local arrays in particle-id order each step): bit for bit,
+    with the 1h halo + ghost-density round and with the 2h halo whose ghost
+    densities are computed locally."""
+    assert np.array_equal(_sharded_rows(tmp_path, True, halo_width=halo_width), _single_gpu_rows())
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 4, reason="needs 4 GPUs")
@@ -120,12 +124,13 @@ def test_nccl_four_ranks(cuda, tmp_path, order_by_id):
 
 
 @two_gpus
-def test_nccl_overlapped_step_close_to_single_gpu(cuda, tmp_path):
+@pytest.mark.parametrize("halo_width", [1.0, 2.0])
+def test_nccl_overlapped_step_close_to_single_gpu(cuda, tmp_path, halo_width):
     """The production path (both exchange rounds overlapped with the interior
     force on a second stream, local arrays in exchange order): the same
     particles, and trajectories equal up to fp32 summation order (neighbour
     order differs from the single-GPU run): |dx| <= 1e-5, |dv| <= 1e-3."""
-    got, want = _sharded_rows(tmp_path, False), _single_gpu_rows()
+    got, want = _sharded_rows(tmp_path, False, halo_width=halo_width), _single_gpu_rows()
     np.testing.assert_allclose(got[:, :3], want[:, :3], rtol=0, atol=1e-5)
     np.testing.assert_allclose(got[:, 3:], want[:, 3:], rtol=0, atol=1e-3)
 

@@ -15,6 +15,7 @@ import torch.multiprocessing as mp
 
 import oracle
 import slab
+import slab_cpu
 import workloads
 
 STEPS = 8
@@ -38,8 +39,8 @@ class OracleBackend:
         self.cfg = cfg
         self.p = oracle.SphParams(cfg.h, cfg.mass, cfg.gas_constant, cfg.rest_density, cfg.viscosity)
 
-    classify = staticmethod(slab.torch_classify)
-    compact = staticmethod(slab.torch_compact)
+    classify = staticmethod(slab_cpu.torch_classify)
+    compact = staticmethod(slab_cpu.torch_compact)
 
     def density(self, pos, n):
         c = self.cfg
@@ -76,7 +77,8 @@ def _rank_main(rank, world, port, out_path, halo_width=1.0):
         cfg = _cfg()
         pos, vel = _inputs(cfg)
         run = slab.SlabRun(dist, rank, world, cfg, pos, vel, OracleBackend(cfg), torch.device("cpu"),
-                           order_by_id=True, halo_width=halo_width)
+                           order_by_id=True, halo_width=halo_width,
+                           comm=lambda r: slab_cpu.PyComm(r, dist))
         first_owner = run.ids().clone()
         halo = 0
         for _ in range(STEPS):
@@ -142,7 +144,8 @@ def _balanced_rank_main(rank, world, port, out_path):
         cfg = _cfg()
         pos, vel = _skewed_inputs(cfg)
         run = slab.SlabRun(dist, rank, world, cfg, pos, vel, OracleBackend(cfg), torch.device("cpu"),
-                           order_by_id=True, balance=True, hist_bins=256)
+                           order_by_id=True, balance=True, hist_bins=256,
+                           comm=lambda r: slab_cpu.PyComm(r, dist))
         first = list(run.geo.bounds)
         loads = [run.n_own]
         moved = 0

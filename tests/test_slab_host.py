@@ -77,3 +77,30 @@ def test_halo_width_is_one_or_two():
     pos, vel = workloads.uniform_particles(cfg.n, seed=1)
     with pytest.raises(ValueError, match="halo_width"):
         slab.SlabRun(None, 0, 1, cfg, pos, vel, None, torch.device("cpu"), halo_width=1.5)
+
+
+@pytest.mark.parametrize("world,halo_width,ok", [(4, 1.0, True), (4, 2.0, False), (8, 1.0, False)])
+def test_uniform_slabs_narrower_than_two_reaches_are_rejected(world, halo_width, ok):
+    """h = 1/16: 4 slabs of 0.25 hold a 1h halo (2 * reach = 0.125) but not a
+    2h one (2 * reach = 0.25 + 1e-5 rounding margin); 8 slabs of 0.125 hold
+    neither. A halo never skips a rank, so too-narrow slabs must fail loudly."""
+    import torch
+    import workloads
+    cfg = workloads.small("ref65k", 200, (16, 16, 16))
+    pos, vel = workloads.uniform_particles(cfg.n, seed=3)
+    made = []
+
+    class _Comm:  # stands in for the exchange: only construction is tested
+        def __init__(self, run):
+            made.append(run)
+
+        def exchange(self, migrate):
+            pass
+
+    if ok:
+        slab.SlabRun(None, 1, world, cfg, pos, vel, None, torch.device("cpu"), halo_width=halo_width, comm=_Comm)
+        assert made
+    else:
+        with pytest.raises(ValueError, match="2 \\* reach"):
+            slab.SlabRun(None, 1, world, cfg, pos, vel, None, torch.device("cpu"), halo_width=halo_width,
+                         comm=_Comm)

@@ -1,5 +1,5 @@
 """Failure detection of the sharded step, on CPU ranks run as threads over
-an in-process mailbox transport (slab.MailboxHub) with injected delays,
+an in-process mailbox transport (slab_cpu.MailboxHub) with injected delays,
 dropped messages and a rank that dies: no GPU and no real process group.
 
 With random delays the trajectory is still the single-process one bit for
@@ -13,6 +13,7 @@ import torch
 
 import oracle
 import slab
+import slab_cpu
 import workloads
 from test_slab_gloo import OracleBackend, _cfg, _inputs
 
@@ -28,7 +29,7 @@ def _run_threads(world, hub, steps, die_at=None):
     def main(r):
         try:
             run = slab.SlabRun(hub.rank(r), r, world, cfg, pos, vel, OracleBackend(cfg), torch.device("cpu"),
-                               order_by_id=True)
+                               order_by_id=True, comm=lambda run: slab_cpu.PyComm(run, hub.rank(r)))
             for s in range(steps):
                 if die_at is not None and die_at == (r, s):
                     raise SystemExit(f"rank {r} stops at step {s}")
@@ -48,7 +49,7 @@ def _run_threads(world, hub, steps, die_at=None):
 
 
 def test_delayed_messages_keep_the_trajectory_exact():
-    hub = slab.MailboxHub(3, timeout=30.0, delay=(0.0, 0.003), seed=1)
+    hub = slab_cpu.MailboxHub(3, timeout=30.0, delay=(0.0, 0.003), seed=1)
     out, _ = _run_threads(3, hub, STEPS)
     for o in out:
         assert isinstance(o, np.ndarray), o
@@ -66,27 +67,27 @@ def test_delayed_messages_keep_the_trajectory_exact():
 
 def test_dropped_message_is_detected_by_timeout():
     # drop the 5th message rank 1 sends to rank 0 (mid-run: round 1 of step 1)
-    hub = slab.MailboxHub(3, timeout=1.0, drop=lambda src, dst, seq: (src, dst, seq) == (1, 0, 4))
+    hub = slab_cpu.MailboxHub(3, timeout=1.0, drop=lambda src, dst, seq: (src, dst, seq) == (1, 0, 4))
     out, took = _run_threads(3, hub, STEPS)
-    assert isinstance(out[0], slab.ExchangeTimeout), out[0]
+    assert isinstance(out[0], slab_cpu.ExchangeTimeout), out[0]
     assert "from rank 1" in str(out[0])
-    assert any(isinstance(o, slab.ExchangeTimeout) for o in out[1:]), "the failure did not propagate"
+    assert any(isinstance(o, slab_cpu.ExchangeTimeout) for o in out[1:]), "the failure did not propagate"
     assert took < 60
 
 
 def test_dead_rank_is_detected_by_its_neighbours():
-    hub = slab.MailboxHub(3, timeout=1.0)
+    hub = slab_cpu.MailboxHub(3, timeout=1.0)
     out, took = _run_threads(3, hub, STEPS, die_at=(2, 3))
     assert isinstance(out[2], SystemExit)
-    assert isinstance(out[1], slab.ExchangeTimeout) and "from rank 2" in str(out[1]), out[1]
-    assert isinstance(out[0], slab.ExchangeTimeout), out[0]  # rank 1 stopped answering too
+    assert isinstance(out[1], slab_cpu.ExchangeTimeout) and "from rank 2" in str(out[1]), out[1]
+    assert isinstance(out[0], slab_cpu.ExchangeTimeout), out[0]  # rank 1 stopped answering too
     assert took < 60
 
 
 def test_rebalance_all_reduce_over_mailbox():
     """The rebalancing all-reduce over the mailbox: every rank gets the same
     bounds; a missing rank turns into ExchangeTimeout."""
-    hub = slab.MailboxHub(2, timeout=1.0)
+    hub = slab_cpu.MailboxHub(2, timeout=1.0)
     got = [None, None]
 
     def main(r):
@@ -100,9 +101,9 @@ def test_rebalance_all_reduce_over_mailbox():
     for t in th:
         t.join()
     assert got == [[3.0] * 4, [3.0] * 4]
-    lone = slab.MailboxHub(2, timeout=0.5)
+    lone = slab_cpu.MailboxHub(2, timeout=0.5)
     try:
         lone.rank(0).all_reduce(torch.ones(2))
         raise AssertionError("expected ExchangeTimeout")
-    except slab.ExchangeTimeout:
+    except slab_cpu.ExchangeTimeout:
         pass
