@@ -43,6 +43,37 @@ __device__ __forceinline__ float4 ld_stream_f4(const float4* p) {
     return v;
 }
 
+// Unsigned division of n < 2^31 by a fixed divisor 1 <= d < 2^31 with one
+// 64-bit multiply and a shift: floor(n / d) == (n * m) >> s for
+// s = 31 + ceil(log2 d), m = floor(2^s / d) + 1 (m d - 2^s <= d <= 2^(s-31)).
+struct FastDiv {
+    uint64_t m;
+    uint32_t s;
+    uint32_t d;
+};
+
+__host__ __device__ inline FastDiv make_fastdiv(uint32_t d) {
+    uint32_t l = 0;
+    while ((1ull << l) < d) ++l;
+    FastDiv f;
+    f.d = d;
+    f.s = 31 + l;
+    f.m = (1ull << f.s) / d + 1;
+    return f;
+}
+
+__device__ __forceinline__ uint32_t fast_div(uint32_t n, const FastDiv& f) {
+    return (uint32_t)(((uint64_t)n * f.m) >> f.s);
+}
+
+// Hardware square root approximation (relative error ~2^-22; callers that
+// bound a search window add a margin for it).
+__device__ __forceinline__ float sqrt_approx(float x) {
+    float r;
+    asm("sqrt.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+
 // Exclusive scan of one uint32 per thread over a block of NT threads
 // (NT a multiple of 32, <= 1024). `warp_tot` is shared scratch of NT/32
 // words. Returns the exclusive prefix; *total receives the block sum.

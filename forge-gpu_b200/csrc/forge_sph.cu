@@ -611,8 +611,12 @@ sph::SphConsts make_consts(const forge_sph_params* p) {
 }
 
 sph::Geom geom_of(const forge_grid* g, float h) {
-    return sph::Geom{g->geom.ox, g->geom.oy, g->geom.oz, g->geom.cs, g->geom.nx, g->geom.ny, g->geom.nz,
-                     (int)g->sub_bits, g->geom.cs >= h ? 1 : 0};
+    sph::Geom G{g->geom.ox, g->geom.oy, g->geom.oz, g->geom.cs, g->geom.nx, g->geom.ny, g->geom.nz,
+                (int)g->sub_bits, g->geom.cs >= h ? 1 : 0};
+    G.inv_slice = (float)(1u << g->sub_bits) / g->geom.cs;
+    G.row_len = make_fastdiv((uint32_t)g->geom.nx << g->sub_bits);
+    G.ny_div = make_fastdiv((uint32_t)g->geom.ny);
+    return G;
 }
 
 constexpr uint32_t kSphThreads = 128;

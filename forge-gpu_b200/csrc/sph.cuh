@@ -55,6 +55,9 @@ struct Geom {
     int nx, ny, nz;
     int sub_bits;   // x-slices per cell = 2^sub_bits (keys are cell << sub_bits | slice)
     int pairable;   // cs >= h: a walk over a same-row neighbour's window adds only r >= h pairs
+    float inv_slice;   // 2^sub_bits / cs (rounded: window bounds carry a margin for it)
+    FastDiv row_len;   // nx << sub_bits: key -> (row, slice in row)
+    FastDiv ny_div;    // ny: row -> (cy, cz)
 };
 
 // Squared conservative gap: distance shrunk by a slack covering the rounding
@@ -79,17 +82,18 @@ __device__ __forceinline__ Frame make_frame(const float4& p, const Geom& g) {
     Frame f;
     const uint32_t key = __float_as_uint(p.w);
     const uint32_t S = 1u << g.sub_bits;
-    const uint32_t rowlen = (uint32_t)g.nx * S;
-    const uint32_t t = key / rowlen;
-    f.f_own = (int)(key - t * rowlen);
-    f.cy = (int)(t % (uint32_t)g.ny);
-    f.cz = (int)(t / (uint32_t)g.ny);
+    const uint32_t t = fast_div(key, g.row_len);
+    f.f_own = (int)(key - t * g.row_len.d);
+    const uint32_t tz = fast_div(t, g.ny_div);
+    f.cy = (int)(t - tz * g.ny_div.d);
+    f.cz = (int)tz;
     const int cx = f.f_own >> g.sub_bits;
     f.fx_lo = max(cx - 1, 0) * (int)S;
     f.fx_hi = (min(cx + 1, g.nx - 1) + 1) * (int)S - 1;
-    const float fx = (p.x - g.ox) / g.cs;
-    f.fxs = fx * (float)S;
-    f.slack = (4e-7f * (fabsf(fx) + 2.f)) * (float)S;
+    f.fxs = (p.x - g.ox) * g.inv_slice;
+    // rounding of the cell assignment and of r^2, plus 1e-3 slices for the
+    // rounded reciprocal and the approximate square root of row_window
+    f.slack = 4e-7f * (fabsf(f.fxs) + 2.f * (float)S) + 1e-3f;
     const float by = g.oy + (float)f.cy * g.cs, bz = g.oz + (float)f.cz * g.cs;
     const float sy = 4e-7f * (fabsf(p.y) + fabsf(by) + g.cs);
     const float sz = 4e-7f * (fabsf(p.z) + fabsf(bz) + g.cs);
@@ -111,7 +115,7 @@ __device__ __forceinline__ bool row_window(const Frame& f, int r, const Geom& g,
     if (z < 0 || z >= g.nz || y < 0 || y >= g.ny) return false;
     const float base = (dz < 0 ? f.gzl : (dz > 0 ? f.gzr : 0.f)) + (dy < 0 ? f.gyl : (dy > 0 ? f.gyr : 0.f));
     if (base > H) return false;
-    const float w = sqrtf(H - base) / g.cs * (float)(1 << g.sub_bits) + f.slack;
+    const float w = sqrt_approx(H - base) * g.inv_slice + f.slack;
     lo = max(min(floor_to_int_dev(f.fxs - w), f.f_own), f.fx_lo);
     hi = min(max(floor_to_int_dev(f.fxs + w), f.f_own), f.fx_hi);
     return true;
@@ -159,15 +163,23 @@ __device__ __forceinline__ void density_derived(float rho, const SphConsts& c, f
 // the sum equals the reference's branchy one. Writes 1/rho to vel4[s].w, aux[s]
 // and, if given, density_out[i] (original order).
 // ---------------------------------------------------------------------------
+// max(h^2 - r^2, 0) as three FMAs (h^2 - dx^2 - dy^2 - dz^2): the poly6
+// base of a pair, exactly +0 outside h. The sums below accumulate base^3 and
+// are scaled by m * poly6 once per particle (the reference scales each term;
+// the difference is fp32 rounding, inside the density tolerance).
+__device__ __forceinline__ float poly6_base(const float4& p, const float4& q, float h2) {
+    const float dx = p.x - q.x, dy = p.y - q.y, dz = p.z - q.z;
+    return fmaxf(fmaf(-dz, dz, fmaf(-dy, dy, fmaf(-dx, dx, h2))), 0.f);
+}
+
 // Poly6 contributions of candidates [b, e) to one or two particles.
 __device__ __forceinline__ void poly6_one(const float4* __restrict__ pos4, uint32_t b, uint32_t e, const float4& p,
                                           const SphConsts& c, float& rho) {
 #pragma unroll 4
     for (uint32_t j = b; j < e; ++j) {
         const float4 q = __ldg(pos4 + j);
-        const float dx = p.x - q.x, dy = p.y - q.y, dz = p.z - q.z;
-        const float d = fmaxf(c.h2 - (dx * dx + dy * dy + dz * dz), 0.f);
-        rho += c.mass_poly6 * d * d * d;
+        const float d = poly6_base(p, q, c.h2);
+        rho = fmaf(d * d, d, rho);
     }
 }
 
@@ -176,12 +188,10 @@ __device__ __forceinline__ void poly6_two(const float4* __restrict__ pos4, uint3
 #pragma unroll 2
     for (uint32_t j = b; j < e; ++j) {
         const float4 q = __ldg(pos4 + j);
-        const float ax = p0.x - q.x, ay = p0.y - q.y, az = p0.z - q.z;
-        const float bx = p1.x - q.x, by = p1.y - q.y, bz = p1.z - q.z;
-        const float d0 = fmaxf(c.h2 - (ax * ax + ay * ay + az * az), 0.f);
-        const float d1 = fmaxf(c.h2 - (bx * bx + by * by + bz * bz), 0.f);
-        rho0 += c.mass_poly6 * d0 * d0 * d0;
-        rho1 += c.mass_poly6 * d1 * d1 * d1;
+        const float d0 = poly6_base(p0, q, c.h2);
+        const float d1 = poly6_base(p1, q, c.h2);
+        rho0 = fmaf(d0 * d0, d0, rho0);
+        rho1 = fmaf(d1 * d1, d1, rho1);
     }
 }
 
@@ -230,6 +240,8 @@ __global__ void __launch_bounds__(128, FORGE_DENSITY_MIN_BLOCKS)
             for_each_range(p1, g, cell_start, c.h2_skip,
                            [&](uint32_t b, uint32_t e) { poly6_one(pos4, b, e, p1, c, rho1); });
     }
+    rho0 *= c.mass_poly6;
+    rho1 *= c.mass_poly6;
     float inv_rho;
     float2 a;
     density_derived(rho0, c, inv_rho, a);
@@ -522,7 +534,7 @@ __device__ __forceinline__ ForceAcc force_acc(const float4* __restrict__ pos4, c
 
 __device__ __forceinline__ uint32_t in_range_bit(const float4& p, const float4& q, const SphConsts& c, uint32_t k) {
     const float dx = p.x - q.x, dy = p.y - q.y, dz = p.z - q.z;
-    const float r2 = dx * dx + dy * dy + dz * dz;
+    const float r2 = fmaf(dz, dz, fmaf(dy, dy, dx * dx));
     return (r2 < c.h2 && r2 > 1e-12f) ? (1u << k) : 0u;
 }
 

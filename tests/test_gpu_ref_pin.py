@@ -60,6 +60,11 @@ def test_force_terms_vs_reference_kernels(cuda, name, terms):
     r = dev(cuda, rho)
     vo = [cuda.empty_like(x) for x in v]
     sp = forge_sph.SphParams(H, mass, K, RHO0, MU)
+    # builds the grid of these positions; the force pass then takes the
+    # reference's densities as the caller-supplied ones
+    scratch = cuda.empty(n, dtype=cuda.float32, device="cuda")
+    forge_sph.check(forge_sph.lib().forge_sph_density(g.handle, ctypes.byref(sp), *(x.data_ptr() for x in d), n,
+                                                      scratch.data_ptr(), None))
     forge_sph.check(forge_sph.lib().forge_sph_force(
         g.handle, ctypes.byref(sp), terms, *(x.data_ptr() for x in d), *(x.data_ptr() for x in v), r.data_ptr(), n,
         1.0, *(x.data_ptr() for x in vo), None, None, None, None))
