@@ -546,14 +546,16 @@ __device__ __forceinline__ void force_hits(const float4* __restrict__ pos4, cons
     while (hit) {
         const uint32_t j = j0 + (uint32_t)(__ffs(hit) - 1);
         hit &= hit - 1;
+        // all three loads issued together (one latency per hit)
         const float4 q = __ldg(pos4 + j);
         const float4 vj = __ldg(vel4 + j);
+        const float pjr = (TERMS & 1) ? __ldg(pj_over_rho + 2 * j) : 0.f;
         const float djx = A.p.x - q.x, djy = A.p.y - q.y, djz = A.p.z - q.z;
         const float r2 = __fadd_rn(__fadd_rn(__fmul_rn(djx, djx), __fmul_rn(djy, djy)), __fmul_rn(djz, djz));
         const float diff = c.h - sqrtf(r2);
         const float inv_rho_j = vj.w;
         if (TERMS & 1) {
-            const float pp = fmaf(A.pres, inv_rho_j, __ldg(pj_over_rho + 2 * j));
+            const float pp = fmaf(A.pres, inv_rho_j, pjr);
             const float f = c.kp * pp * (diff * diff) * rsqrtf(r2);
             A.pax = fmaf(f, djx, A.pax);
             A.pay = fmaf(f, djy, A.pay);
