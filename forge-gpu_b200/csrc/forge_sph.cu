@@ -481,6 +481,8 @@ extern "C" int forge_grid_create(float cell_size, uint32_t nx, uint32_t ny, uint
     g->geom.nx = (int)nx;
     g->geom.ny = (int)ny;
     g->geom.nz = (int)nz;
+    g->geom.cx0 = 0;
+    g->geom.nxw = (int)nx;
     g->C = (uint32_t)C;
     uint32_t kb = 1;
     while (kb < 32 && (1ull << kb) < C) ++kb;
@@ -534,6 +536,18 @@ extern "C" void forge_grid_destroy(forge_grid* g) {
 
 namespace {
 
+// Cells of the grid's x-window (the table's extent) and the key bits that
+// index them.
+uint32_t cells_w(const forge_grid* g) {
+    return (uint32_t)g->geom.nxw * (uint32_t)g->geom.ny * (uint32_t)g->geom.nz;
+}
+uint32_t key_bits_w(const forge_grid* g) {
+    const uint32_t C = cells_w(g);
+    uint32_t kb = 1;
+    while (kb < 32 && (1ull << kb) < C) ++kb;
+    return kb;
+}
+
 // Hash + sort + cell-start table (+ optional cell-ordered gather).
 // sub_bits > 0 (the SPH passes): keys are cell << sub_bits | x-slice, so the
 // cell-ordered arrays are also ordered by x-slice inside each cell and the
@@ -551,7 +565,7 @@ int grid_build_impl(forge_grid* g, const float* px, const float* py, const float
         grid::HashKeys src{px, py, pz, stride, g->geom, keys, sub_bits};
         int where = 0;
         int rc = run_onesweep(g->scratch, src, keys, nullptr, g->kb, g->vb, g->kc, g->vc, nn, 0,
-                              g->key_bits + sub_bits, st, &where);
+                              key_bits_w(g) + sub_bits, st, &where);
         if (rc != FORGE_OK) return rc;
         g->sorted_keys = where == 0 ? g->kb : g->kc;
         g->sorted_idx = where == 0 ? g->vb : g->vc;
@@ -561,7 +575,7 @@ int grid_build_impl(forge_grid* g, const float* px, const float* py, const float
     }
     prof_mark(g, 1, st);
     grid::GatherSrc gs{px, py, pz, stride, vx, vy, vz};
-    const uint32_t table = g->C << sub_bits;  // entries [0, table]
+    const uint32_t table = cells_w(g) << sub_bits;  // entries [0, table]
     grid::cell_start_gather_kernel<<<grid_blocks(n + 1, 256), 256, 0, st>>>(
         g->sorted_keys, g->sorted_idx, nn, table, g->cell_start, gs, gather_pos ? g->pos4 : nullptr,
         (gather_pos && vx) ? g->vel4 : nullptr, g->chunk_val);
@@ -582,7 +596,8 @@ int grid_export(forge_grid* g, uint32_t* sorted_idx, uint32_t* cell_start, cudaS
     if (sorted_idx && g->n)
         FORGE_CUDA(cudaMemcpyAsync(sorted_idx, g->sorted_idx, g->n * 4, cudaMemcpyDeviceToDevice, st));
     if (cell_start)
-        FORGE_CUDA(cudaMemcpyAsync(cell_start, g->cell_start, ((size_t)g->C + 1) * 4, cudaMemcpyDeviceToDevice, st));
+        FORGE_CUDA(cudaMemcpyAsync(cell_start, g->cell_start, ((size_t)cells_w(g) + 1) * 4, cudaMemcpyDeviceToDevice,
+                                   st));
     return FORGE_OK;
 }
 
@@ -611,10 +626,11 @@ sph::SphConsts make_consts(const forge_sph_params* p) {
 }
 
 sph::Geom geom_of(const forge_grid* g, float h) {
-    sph::Geom G{g->geom.ox, g->geom.oy, g->geom.oz, g->geom.cs, g->geom.nx, g->geom.ny, g->geom.nz,
+    sph::Geom G{g->geom.ox, g->geom.oy, g->geom.oz, g->geom.cs, g->geom.nxw, g->geom.ny, g->geom.nz,
                 (int)g->sub_bits, g->geom.cs >= h ? 1 : 0};
     G.inv_slice = (float)(1u << g->sub_bits) / g->geom.cs;
-    G.row_len = make_fastdiv((uint32_t)g->geom.nx << g->sub_bits);
+    G.x_off = (float)((uint32_t)g->geom.cx0 << g->sub_bits);
+    G.row_len = make_fastdiv((uint32_t)g->geom.nxw << g->sub_bits);
     G.ny_div = make_fastdiv((uint32_t)g->geom.ny);
     return G;
 }
@@ -637,7 +653,7 @@ constexpr double kPairMaxOccupancy = 8.0;
 template <int TERMS, int EPI>
 void launch_force_t(forge_grid* g, const sph::SphConsts& c, const sph::StepEpi& ep, const sph::ForceOut& o,
                     cudaStream_t st) {
-    if ((double)g->n / (double)g->C < kPairMaxOccupancy)
+    if ((double)g->n / (double)cells_w(g) < kPairMaxOccupancy)
         sph::force_kernel<TERMS, EPI, false><<<grid_blocks((g->n + 1) / 2, kSphThreads), kSphThreads, 0, st>>>(
             g->pos4, g->vel4, g->aux, g->cell_start, g->sorted_idx, (uint32_t)g->n, geom_of(g, c.h), c, ep, o, {});
     else
@@ -652,7 +668,7 @@ void launch_force_t(forge_grid* g, const sph::SphConsts& c, const sph::StepEpi& 
 int launch_force_zone(forge_grid* g, const sph::SphConsts& c, const sph::StepEpi& ep, const sph::ForceOut& o,
                       uint32_t list, cudaStream_t st) {
     const sph::ZoneList zl{g->zone_idx, g->zone_counts, list};
-    if ((double)g->n / (double)g->C < kPairMaxOccupancy)
+    if ((double)g->n / (double)cells_w(g) < kPairMaxOccupancy)
         sph::force_kernel<3, 1, true><<<grid_blocks((g->n + 1) / 2, kSphThreads), kSphThreads, 0, st>>>(
             g->pos4, g->vel4, g->aux, g->cell_start, g->sorted_idx, (uint32_t)g->n, geom_of(g, c.h), c, ep, o, zl);
     else
@@ -679,12 +695,12 @@ int zone_setup(forge_grid* g) {
 // [inner_lo, inner_hi). Ghosts fall in the boundary list (skipped there).
 int zone_classify(forge_grid* g, float inner_lo, float inner_hi, cudaStream_t st) {
     const grid::GridGeom& G = g->geom;
-    const uint32_t row_len = (uint32_t)G.nx << g->sub_bits;
+    const uint32_t row_len = (uint32_t)G.nxw << g->sub_bits;
     const double w = (double)G.cs / (double)(1u << g->sub_bits);  // slice width
     auto edge = [&](float x, bool up) -> uint32_t {
         if (std::isinf(x)) return x < 0 ? 0u : row_len;
         if (!(x == x)) return 0u;
-        const double f = ((double)x - (double)G.ox) / w;
+        const double f = ((double)x - (double)G.ox) / w - (double)((uint64_t)G.cx0 << g->sub_bits);
         const double e = up ? std::ceil(f) : std::floor(f);
         return (uint32_t)std::min<double>(std::max<double>(e, 0.0), (double)row_len);
     };
@@ -732,6 +748,8 @@ extern "C" int forge_grid_query(forge_grid* g, const float* px, const float* py,
     if (!g) return set_error(FORGE_ERR_INVALID_ARG, "forge_grid_query: grid is NULL");
     if (!g->built || g->sub_bits != 0)
         return set_error(FORGE_ERR_INVALID_ARG, "forge_grid_query: build the grid with forge_grid_build first");
+    if (g->geom.cx0 != 0 || g->geom.nxw != g->geom.nx)
+        return set_error(FORGE_ERR_INVALID_ARG, "forge_grid_query: the grid has an x-window; queries need the whole grid");
     if (nq > g->max_n)
         return set_error(FORGE_ERR_CAPACITY, "forge_grid_query: nq=%llu exceeds max_n=%llu",
                          (unsigned long long)nq, (unsigned long long)g->max_n);
@@ -960,6 +978,17 @@ extern "C" int forge_sph_step(forge_grid* g, const forge_sph_params* p, const fo
     FORGE_LAUNCHED();
     prof_mark(g, 4, st);
     prof_step_done(g);
+    return FORGE_OK;
+}
+
+extern "C" int forge_grid_set_x_window(forge_grid* g, uint32_t cx0, uint32_t nxw) {
+    if (!g) return set_error(FORGE_ERR_INVALID_ARG, "forge_grid_set_x_window: grid is NULL");
+    if (nxw == 0 || (uint64_t)cx0 + nxw > (uint64_t)g->geom.nx)
+        return set_error(FORGE_ERR_INVALID_ARG, "forge_grid_set_x_window: cells [%u, %u) outside the grid's %d",
+                         cx0, cx0 + nxw, g->geom.nx);
+    g->geom.cx0 = (int)cx0;
+    g->geom.nxw = (int)nxw;
+    g->built = false;  // the table of the last build no longer matches
     return FORGE_OK;
 }
 

@@ -12,6 +12,10 @@ struct GridGeom {
     float ox, oy, oz;  // origin (0 for the SPH modules)
     float cs;          // cell size
     int nx, ny, nz;
+    // x-window of the table: global cells [cx0, cx0 + nxw) (a shard's slab;
+    // the whole grid by default). Cells are assigned globally (the
+    // reference's floor and clamp), then shifted into the window.
+    int cx0, nxw;
 };
 
 // Saturating float -> int as Rust's `as i32` and CUDA's cvt.rzi.s32 do
@@ -29,7 +33,9 @@ __device__ __forceinline__ uint32_t cell_of(float x, float y, float z, const Gri
     cx = cx < 0 ? 0 : (cx >= g.nx ? g.nx - 1 : cx);
     cy = cy < 0 ? 0 : (cy >= g.ny ? g.ny - 1 : cy);
     cz = cz < 0 ? 0 : (cz >= g.nz ? g.nz - 1 : cz);
-    return (uint32_t)cx + (uint32_t)cy * (uint32_t)g.nx + (uint32_t)cz * (uint32_t)g.nx * (uint32_t)g.ny;
+    cx -= g.cx0;  // the caller keeps every particle inside the window; clamped for safety
+    cx = cx < 0 ? 0 : (cx >= g.nxw ? g.nxw - 1 : cx);
+    return (uint32_t)cx + (uint32_t)cy * (uint32_t)g.nxw + (uint32_t)cz * (uint32_t)g.nxw * (uint32_t)g.ny;
 }
 
 // Sub-slice of a position inside its (clamped) cell along x: the cell is cut

@@ -56,6 +56,7 @@ struct Geom {
     int sub_bits;   // x-slices per cell = 2^sub_bits (keys are cell << sub_bits | slice)
     int pairable;   // cs >= h: a walk over a same-row neighbour's window adds only r >= h pairs
     float inv_slice;   // 2^sub_bits / cs (rounded: window bounds carry a margin for it)
+    float x_off;       // first slice of the grid's x-window: cx0 << sub_bits (nx is the window's width)
     FastDiv row_len;   // nx << sub_bits: key -> (row, slice in row)
     FastDiv ny_div;    // ny: row -> (cy, cz)
 };
@@ -90,7 +91,7 @@ __device__ __forceinline__ Frame make_frame(const float4& p, const Geom& g) {
     const int cx = f.f_own >> g.sub_bits;
     f.fx_lo = max(cx - 1, 0) * (int)S;
     f.fx_hi = (min(cx + 1, g.nx - 1) + 1) * (int)S - 1;
-    f.fxs = (p.x - g.ox) * g.inv_slice;
+    f.fxs = (p.x - g.ox) * g.inv_slice - g.x_off;
     // rounding of the cell assignment and of r^2, plus 1e-3 slices for the
     // rounded reciprocal and the approximate square root of row_window
     f.slack = 4e-7f * (fabsf(f.fxs) + 2.f * (float)S) + 1e-3f;

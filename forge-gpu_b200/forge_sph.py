@@ -63,7 +63,7 @@ EXPORTED = (
     "forge_grid_create", "forge_grid_build", "forge_grid_build_aos", "forge_grid_query",
     "forge_grid_check", "forge_grid_destroy",
     "forge_sph_density", "forge_sph_force", "forge_sph_step",
-    "forge_grid_profile_enable", "forge_grid_profile_read",
+    "forge_grid_profile_enable", "forge_grid_profile_read", "forge_grid_set_x_window",
     "forge_sort_pairs_static",
     "forge_sph_force_step",
     "forge_slab_create", "forge_slab_destroy", "forge_slab_classify", "forge_slab_compact",
@@ -136,6 +136,7 @@ def lib() -> ctypes.CDLL:
         "forge_sph_step": (i32, [vp, ctypes.POINTER(SphParams), ctypes.POINTER(StepParams), vp, vp, vp, vp, vp,
                                  vp, vp, u64, vp]),
         "forge_grid_profile_enable": (i32, [vp, u32]),
+        "forge_grid_set_x_window": (i32, [vp, u32, u32]),
         "forge_sort_pairs_static": (i32, [vp, vp, u64, u32, u32, vp]),
         "forge_nccl_unique_id": (i32, [ctypes.c_char_p]),
         "forge_slab_comm_create": (i32, [ctypes.c_char_p, i32, i32, i32, u64, f32, f32, f32, pvp]),
@@ -290,6 +291,11 @@ class HashGrid:
     @property
     def handle(self):
         return self._h
+
+    def set_x_window(self, cx0: int, nxw: int) -> None:
+        """Index only global cells [cx0, cx0 + nxw) along x (a shard's slab);
+        every particle built must lie inside (forge_grid_set_x_window)."""
+        check(lib().forge_grid_set_x_window(self._h, int(cx0), int(nxw)))
 
     def num_cells(self) -> int:
         return self.dim_x * self.dim_y * self.dim_z

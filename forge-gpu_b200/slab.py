@@ -229,6 +229,7 @@ class SlabRun:
             self.geo.set_bounds(min_width_bounds(quantile_bounds(hist, x_range[0], x_range[1], world),
                                                  2.0 * self.reach))
         self.check_widths(self.geo.bounds)
+        self._set_window()
         self.order_by_id = order_by_id
         px = torch.as_tensor(pos[0])
         m = self.geo.owned_mask(px)
@@ -250,6 +251,16 @@ class SlabRun:
         # (exchange, set_bounds, exchange_rho) -- the tests' CPU-rank transport
         self.comm = NcclComm(self, dist, forge_sph) if comm == "nccl" else comm(self)
         self.comm.exchange(migrate=False)  # initial halo
+
+    def _set_window(self) -> None:
+        """Shrinks the backend's grid to this slab along x (owned particles,
+        ghosts within reach of a face, and one cell each side for the ghosts'
+        neighbours), so the cell table scales with the shard."""
+        if hasattr(self.backend, "set_window"):
+            g = self.geo
+            lo = -np.inf if g.first else g.lo - self.reach
+            hi = np.inf if g.last else g.hi + self.reach
+            self.backend.set_window(lo, hi)
 
     def check_widths(self, bounds) -> None:
         """Every slab must be at least 2 * reach wide: halo and migrant lists
@@ -293,6 +304,7 @@ class SlabRun:
             return False
         self.check_widths(new)
         self.geo.set_bounds(new)
+        self._set_window()
         self.comm.set_bounds(self.geo.lo, self.geo.hi)
         self.ng = 0  # ghosts of the old bounds
         self._work_hist = None
@@ -452,6 +464,14 @@ class GpuBackend:
         if h and self.f._lib is not None:
             self.f._lib.forge_slab_destroy(h)
             self.slab = None
+
+    def set_window(self, x_lo: float, x_hi: float) -> None:
+        """Grid x-window covering positions [x_lo, x_hi) plus one cell each
+        side (infinite bounds: to the grid's edge)."""
+        cs, nx = self.cfg.cell_size, self.cfg.dims[0]
+        c0 = 0 if not np.isfinite(x_lo) else max(0, int(np.floor(x_lo / cs)) - 1)
+        c1 = nx - 1 if not np.isfinite(x_hi) else min(nx - 1, int(np.floor(x_hi / cs)) + 1)
+        self.grid.set_x_window(c0, c1 - c0 + 1)
 
     def classify(self, x, n, lo, hi, reach, flags):
         """(A, L, R) ascending index lists from forge_slab_classify (one

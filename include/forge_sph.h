@@ -436,6 +436,17 @@ FORGE_API int forge_slab_exchange_end(forge_slab_comm* c, float* cols, uint64_t 
  * rho[] (indexed like the columns). No host synchronisation. */
 FORGE_API int forge_slab_exchange_rho(forge_slab_comm* c, float* rho, void* stream);
 
+/* x-window of a grid (no reference counterpart; for a shard of an x-slab
+ * decomposition): builds index only global cells [cx0, cx0 + nxw) along x,
+ * so the cell-start table and its build shrink with the shard. Cells are
+ * still assigned on the global grid (floor and clamp of hashgrid.rs:128-139
+ * / sph_fused.rs:91-99), then shifted; neighbour windows are clipped at the
+ * window's edges as at the grid's. The caller keeps every particle it builds
+ * inside the window (a shard's owned particles and ghosts, plus one cell of
+ * margin each side for the ghosts' neighbours). Resets the last build;
+ * forge_grid_query needs the whole grid. Default: the whole grid. */
+FORGE_API int forge_grid_set_x_window(forge_grid* g, uint32_t cx0, uint32_t nxw);
+
 /* ------------------------------------------------------------------------ */
 /* Benchmark aid (no reference counterpart; the reference only times the    */
 /* whole run with a wall clock, manifest_runner.rs:40-80).                  */
