@@ -249,18 +249,18 @@ def run_sph_single(torch, forge_sph, cfg, steps, warmup, rank_dev, clocks=True):
 
 def e2e_sph(torch, forge_sph, cfg, pos, vel, steps, warmup):
     """Same step through the public API with HOST buffers: every step copies the
-    particle state from pinned host memory to the device, steps, and reads the
-    new state back (pos, vel: 24 B/particle each way)."""
+    particle state from pinned host memory to the device (forge_io_upload),
+    steps, and reads the new state back (forge_io_download, which waits for
+    it): pos, vel, 24 B/particle each way."""
     run = SphRun(torch, forge_sph, cfg, pos, vel)
     hp = [torch.from_numpy(x.copy()).pin_memory() for x in pos + vel]
     dv = run.p + run.v
+    io = forge_sph.FieldIO(cfg.n, torch.cuda.current_device())
 
     def one():
-        for d, h in zip(dv, hp):
-            d.copy_(h, non_blocking=True)
+        io.upload(hp, dv)    # forge_io_upload: pinned host columns -> device
         run.step()
-        for d, h in zip(dv, hp):
-            h.copy_(d, non_blocking=True)
+        io.download(dv, hp)  # forge_io_download: back to the host (returns when there)
 
     for _ in range(warmup):
         one()

@@ -98,6 +98,11 @@ struct SortScratch {
     uint32_t* status = nullptr;  // tiles * 256 (+pad to uint4)
     uint32_t max_tiles = 0;
     int sms = 148;
+    // failure-detection test hook (forge_sorter_set_test_fault): the first
+    // pass skips tile ids below skip_tiles; look-back waits give up after
+    // spin_limit polls
+    uint32_t skip_tiles = 0;
+    uint32_t spin_limit = kSpinLimit;
 };
 
 int scratch_alloc(SortScratch& s, uint64_t max_n, int device) {
@@ -144,11 +149,13 @@ int run_onesweep(const SortScratch& s, Src src, const uint32_t* keys0, const uin
         if (p == 0 && vin == nullptr) {
             radix::onesweep_pass_kernel<true><<<tiles, radix::kThreads, 0, st>>>(
                 kin, nullptr, kout, vout, n, shift, bits, s.meta + p * radix::kRadix, s.status,
-                s.meta + kMetaCounters + p, p & 1u, s.meta + kMetaErr);
+                s.meta + kMetaCounters + p, p & 1u, s.meta + kMetaErr, p == 0 ? s.skip_tiles : 0u, s.spin_limit,
+                tiles);
         } else {
             radix::onesweep_pass_kernel<false><<<tiles, radix::kThreads, 0, st>>>(
                 kin, vin, kout, vout, n, shift, bits, s.meta + p * radix::kRadix, s.status,
-                s.meta + kMetaCounters + p, p & 1u, s.meta + kMetaErr);
+                s.meta + kMetaCounters + p, p & 1u, s.meta + kMetaErr, p == 0 ? s.skip_tiles : 0u, s.spin_limit,
+                tiles);
         }
         FORGE_LAUNCHED();
         kin = kout;
@@ -378,6 +385,14 @@ extern "C" int forge_sorter_check(forge_sorter* s, void* stream) {
     if (!s) return set_error(FORGE_ERR_INVALID_ARG, "forge_sorter_check: sorter is NULL");
     FORGE_DEVICE_SCOPE(s->device);
     return check_status_word(s->scratch.meta + kMetaErr, as_stream(stream), "radix sort");
+}
+
+extern "C" int forge_sorter_set_test_fault(forge_sorter* s, uint32_t skip_tiles, uint32_t spin_limit) {
+    if (!s) return set_error(FORGE_ERR_INVALID_ARG, "forge_sorter_set_test_fault: sorter is NULL");
+    if (skip_tiles > 1) return set_error(FORGE_ERR_INVALID_ARG, "forge_sorter_set_test_fault: skip_tiles is 0 or 1");
+    s->scratch.skip_tiles = skip_tiles;
+    s->scratch.spin_limit = spin_limit ? spin_limit : kSpinLimit;
+    return FORGE_OK;
 }
 
 extern "C" void forge_sorter_destroy(forge_sorter* s) {
@@ -1089,4 +1104,5 @@ extern "C" int forge_slab_compact(float* cols, uint64_t ld, uint32_t rows, uint6
     return FORGE_OK;
 }
 
+#include "field_io.cuh"
 #include "slab_comm.cuh"

@@ -146,7 +146,8 @@ __global__ void __launch_bounds__(kThreads, 4)
                          uint32_t n, uint32_t shift, uint32_t bits,
                          const uint32_t* __restrict__ pass_hist,  // [256] of this pass
                          uint32_t* status,                        // [tiles][256]
-                         uint32_t* tile_counter, uint32_t parity, uint32_t* err) {
+                         uint32_t* tile_counter, uint32_t parity, uint32_t* err,
+                         uint32_t tile_base, uint32_t spin_limit, uint32_t ntiles) {
     __shared__ uint32_t s_whist[kWarps][kRadix];  // per-warp digit counts, then offsets
     __shared__ uint32_t s_tile_off[kRadix];       // digit start inside the sorted tile
     __shared__ uint32_t s_base[kRadix];           // global dst = s_base[d] + tile position
@@ -155,12 +156,15 @@ __global__ void __launch_bounds__(kThreads, 4)
     __shared__ uint32_t s_tile;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    if (tid == 0) s_tile = atomicAdd(tile_counter, 1u);
+    // tile_base > 0 only under the failure-detection test hook: tile ids
+    // below it are never taken, so their successors' look-backs run out
+    if (tid == 0) s_tile = atomicAdd(tile_counter, 1u) + tile_base;
 #pragma unroll
     for (int w = 0; w < kWarps; ++w) s_whist[w][tid] = 0;
     __syncthreads();
 
     const uint32_t tile = s_tile;
+    if (tile >= ntiles) return;  // (only with tile_base > 0) the whole block
     const uint32_t tile_start = tile * kTile;
     const uint32_t mask = (1u << bits) - 1u;
     const uint32_t warp_start = tile_start + warp * 32 * kItems;
@@ -272,7 +276,7 @@ __global__ void __launch_bounds__(kThreads, 4)
             }
             t -= used;
             if (!done && used == 0) {
-                if (++spins > kSpinLimit) {
+                if (++spins > spin_limit) {
                     atomicOr(err, kDevTimeout);
                     break;
                 }

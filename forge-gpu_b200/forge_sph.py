@@ -26,6 +26,8 @@ import ctypes
 import os
 from dataclasses import dataclass, field
 
+import numpy as np
+
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.environ.get("FORGE_SPH_LIB") or os.path.join(_HERE, "libforge_sph.so")
 
@@ -59,11 +61,14 @@ _CODE_NAMES = {
 EXPORTED = (
     "forge_last_error", "forge_abi_version",
     "forge_sorter_create", "forge_sorter_sort_pairs", "forge_sorter_check", "forge_sorter_destroy",
+    "forge_sorter_set_test_fault",
     "forge_cell_bounds",
     "forge_grid_create", "forge_grid_build", "forge_grid_build_aos", "forge_grid_query",
     "forge_grid_check", "forge_grid_destroy",
     "forge_sph_density", "forge_sph_force", "forge_sph_step",
     "forge_grid_profile_enable", "forge_grid_profile_read", "forge_grid_set_x_window",
+    "forge_io_create", "forge_io_destroy", "forge_io_upload", "forge_io_download", "forge_io_upload_vec3",
+    "forge_io_download_vec3",
     "forge_sort_pairs_static",
     "forge_sph_force_step",
     "forge_slab_create", "forge_slab_destroy", "forge_slab_classify", "forge_slab_compact",
@@ -123,6 +128,7 @@ def lib() -> ctypes.CDLL:
         "forge_sorter_sort_pairs": (i32, [vp, vp, vp, vp, vp, u64, u32, u32, ctypes.POINTER(i32), vp]),
         "forge_sorter_check": (i32, [vp, vp]),
         "forge_sorter_destroy": (None, [vp]),
+        "forge_sorter_set_test_fault": (i32, [vp, u32, u32]),
         "forge_cell_bounds": (i32, [vp, vp, vp, u64, u64, vp]),
         "forge_grid_create": (i32, [f32, u32, u32, u32, ctypes.POINTER(f32), u64, i32, pvp]),
         "forge_grid_build": (i32, [vp, vp, vp, vp, u64, vp, vp, vp, vp]),
@@ -137,6 +143,12 @@ def lib() -> ctypes.CDLL:
                                  vp, vp, u64, vp]),
         "forge_grid_profile_enable": (i32, [vp, u32]),
         "forge_grid_set_x_window": (i32, [vp, u32, u32]),
+        "forge_io_create": (i32, [u64, i32, pvp]),
+        "forge_io_destroy": (None, [vp]),
+        "forge_io_upload": (i32, [vp, pvp, pvp, u32, u64, vp]),
+        "forge_io_download": (i32, [vp, pvp, pvp, u32, u64, vp]),
+        "forge_io_upload_vec3": (i32, [vp, vp, vp, vp, vp, u64, vp]),
+        "forge_io_download_vec3": (i32, [vp, vp, vp, vp, vp, u64, vp]),
         "forge_sort_pairs_static": (i32, [vp, vp, u64, u32, u32, vp]),
         "forge_nccl_unique_id": (i32, [ctypes.c_char_p]),
         "forge_slab_comm_create": (i32, [ctypes.c_char_p, i32, i32, i32, u64, f32, f32, f32, pvp]),
@@ -365,6 +377,68 @@ class HashGrid:
 
 
 # ---------------------------------------------------------------------------
+# Field I/O (manifest_runner.rs:192-269, :83-92)
+# ---------------------------------------------------------------------------
+def _host_ptrs(arrays):
+    """Host addresses of float32 numpy arrays or (pinned) CPU tensors."""
+    out = []
+    for a in arrays:
+        if hasattr(a, "data_ptr"):
+            if a.is_cuda or a.dtype != _torch().float32 or not a.is_contiguous():
+                raise ForgeError(FORGE_ERR_INVALID_ARG, "expected contiguous float32 host tensors")
+            out.append(a.data_ptr())
+        else:
+            if a.dtype != np.float32 or not a.flags["C_CONTIGUOUS"]:
+                raise ForgeError(FORGE_ERR_INVALID_ARG, "expected contiguous float32 numpy arrays")
+            out.append(a.ctypes.data)
+    return out
+
+
+class FieldIO:
+    """forge_io: host <-> device moves of particle fields through a pinned
+    staging buffer, with Vec3f AoS <-> SoA conversion on the GPU."""
+
+    def __init__(self, max_n: int, device: int = 0):
+        h = ctypes.c_void_p()
+        check(lib().forge_io_create(int(max_n), device, ctypes.byref(h)))
+        self._h, self.max_n, self.device = h, int(max_n), device
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h and _lib is not None:
+            _lib.forge_io_destroy(h)
+            self._h = None
+
+    @staticmethod
+    def _vp(ptrs):
+        return (ctypes.c_void_p * max(len(ptrs), 1))(*ptrs)
+
+    def upload(self, host, dev, stream=None) -> None:
+        """host[k] (float32 numpy / CPU tensor) -> dev[k] (CUDA tensor), asynchronous."""
+        n = len(dev[0]) if dev else 0
+        check(lib().forge_io_upload(self._h, self._vp(_host_ptrs(host)), self._vp([ptr(d) for d in dev]), len(dev),
+                                    n, _stream(stream)))
+
+    def download(self, dev, host, stream=None) -> None:
+        """dev[k] -> host[k]; returns when the data are on the host."""
+        n = len(dev[0]) if dev else 0
+        check(lib().forge_io_download(self._h, self._vp([ptr(d) for d in dev]), self._vp(_host_ptrs(host)),
+                                      len(dev), n, _stream(stream)))
+
+    def upload_vec3(self, xyz, x, y, z, stream=None) -> None:
+        """(n, 3) float32 host array -> x, y, z CUDA columns."""
+        (hp,) = _host_ptrs([xyz])
+        check(lib().forge_io_upload_vec3(self._h, hp, ptr(x), ptr(y), ptr(z), len(x), _stream(stream)))
+
+    def download_vec3(self, x, y, z, stream=None) -> np.ndarray:
+        """x, y, z CUDA columns -> new (n, 3) float32 numpy array."""
+        out = np.empty((len(x), 3), np.float32)
+        check(lib().forge_io_download_vec3(self._h, ptr(x), ptr(y), ptr(z), out.ctypes.data, len(x),
+                                           _stream(stream)))
+        return out
+
+
+# ---------------------------------------------------------------------------
 # Manifest modules (forge-manifest/src/modules)
 # ---------------------------------------------------------------------------
 class FieldSet:
@@ -376,11 +450,40 @@ class FieldSet:
         self.device = device
         self.f32_fields: dict = {}
         self.u32_fields: dict = {}
+        self._io = None
+
+    def io(self) -> FieldIO:
+        if self._io is None:
+            self._io = FieldIO(max(self.particle_count, 1), self.device)
+        return self._io
 
     def add_f32(self, name: str, data) -> None:
+        """Field `name` from host data (Array::from_vec): uploaded through
+        the field I/O handle."""
         torch = _torch()
-        self.f32_fields[name] = torch.as_tensor(data, dtype=torch.float32).to(
-            torch.device("cuda", self.device)).contiguous()
+        a = np.ascontiguousarray(np.asarray(data, dtype=np.float32))
+        t = torch.empty(a.shape, dtype=torch.float32, device=torch.device("cuda", self.device))
+        if a.size:
+            self.io().upload([a.reshape(-1)], [t.view(-1)])
+        self.f32_fields[name] = t
+
+    def add_vec3(self, base: str, xyz) -> None:
+        """Fields base_x/_y/_z from an (n, 3) Vec3f array, split on the GPU
+        (init_fields, manifest_runner.rs:205-213)."""
+        torch = _torch()
+        a = np.ascontiguousarray(np.asarray(xyz, dtype=np.float32).reshape(-1, 3))
+        cols = [torch.empty(a.shape[0], dtype=torch.float32, device=torch.device("cuda", self.device))
+                for _ in range(3)]
+        if a.shape[0]:
+            self.io().upload_vec3(a, *cols)
+        for c, t in zip("xyz", cols):
+            self.f32_fields[f"{base}_{c}"] = t
+
+    def positions(self) -> np.ndarray:
+        """pos_x/y/z interleaved into an (n, 3) array (the SimResult gather,
+        manifest_runner.rs:83-92)."""
+        f = self.f32_fields
+        return self.io().download_vec3(f["pos_x"], f["pos_y"], f["pos_z"])
 
     def add_f32_zeros(self, name: str, n: int) -> None:
         torch = _torch()

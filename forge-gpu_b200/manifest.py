@@ -185,6 +185,27 @@ def _vec3_init(n: int, init: dict | None, rng: np.random.Generator):
             (o[2] + (i // side).astype(np.float32) * sp).astype(np.float32)]
 
 
+def initial_vec3(m: Manifest, seed: int = 0) -> dict:
+    """The manifest's initial fields as the reference builds them on the host
+    (init_vec3 / init_f32, manifest_runner.rs:192-310): base name -> (n, 3)
+    Vec3f array for vec3f fields (position/velocity mapped to pos/vel), name
+    -> (n,) array for f32 fields; zero pos/vel added when absent."""
+    n = m.particle_count()
+    rng = np.random.Generator(np.random.PCG64(seed))
+    out = {}
+    for f in m.fields:
+        base = {"position": "pos", "pos": "pos", "velocity": "vel", "vel": "vel"}.get(f["name"], f["name"])
+        if f["type"] == "vec3f":
+            out[base] = np.stack(_vec3_init(n, f.get("init"), rng), axis=1)
+        elif f["type"] == "f32":
+            init = f.get("init")
+            v = float(init["value"][0]) if init is not None and init["type"] == "constant" else 0.0
+            out[f["name"]] = np.full(n, np.float32(v), np.float32)
+    for base in ("vel", "pos"):
+        out.setdefault(base, np.zeros((n, 3), np.float32))
+    return out
+
+
 def initial_fields(m: Manifest, seed: int = 0) -> dict:
     """init_fields (manifest_runner.rs:192-234): name -> float32 array, vec3
     fields split into _x/_y/_z with position/velocity mapped to pos/vel;
@@ -297,8 +318,11 @@ def run_manifest(m: Manifest, device: int = 0, seed: int = 0, capture: bool = Tr
     sub = max(int(m.simulation["substeps"]), 1)
     total = m.total_steps() if steps is None else int(steps)
     fields = forge_sph.FieldSet(n, device)
-    for name, arr in initial_fields(m, seed).items():
-        fields.add_f32(name, arr)
+    for name, arr in initial_vec3(m, seed).items():  # uploaded and split into SoA on the GPU
+        if arr.ndim == 2:
+            fields.add_vec3(name, arr)
+        else:
+            fields.add_f32(name, arr)
     pipe = build_pipeline(m)
     fused = pipe._fused_plan() is not None
     with torch.cuda.device(device):
@@ -328,7 +352,7 @@ def run_manifest(m: Manifest, device: int = 0, seed: int = 0, capture: bool = Tr
         grid = fields.u32_fields.get("_grid")
         if grid is not None:
             grid.check()
-    pos = np.stack([fields.f32_fields["pos_" + a].cpu().numpy() for a in "xyz"], axis=1)
+    pos = fields.positions()  # interleaved on the GPU, one copy back
     return SimResult(pos, n, count, elapsed, [mod.name() for mod in pipe.modules])
 
 

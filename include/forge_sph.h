@@ -121,6 +121,15 @@ FORGE_API int forge_sort_pairs_static(uint32_t* keys, uint32_t* vals, uint64_t n
  * (FORGE_ERR_TIMEOUT if a look-back wait gave up). Clears the status. */
 FORGE_API int forge_sorter_check(forge_sorter* s, void* stream);
 
+/* Test hook for failure detection (no reference counterpart; no GPU fault
+ * is involved). skip_tiles = 1 makes the first pass of the following sorts
+ * never take tile id 0, so the look-back of tile 1 waits on a status word
+ * that nothing writes; the wait gives up after spin_limit polls (0: the
+ * default, ~0.3 s), records the timeout and returns, the sort completes
+ * with unspecified output and forge_sorter_check reports FORGE_ERR_TIMEOUT.
+ * skip_tiles = 0 and spin_limit = 0 restore normal sorting. */
+FORGE_API int forge_sorter_set_test_fault(forge_sorter* s, uint32_t skip_tiles, uint32_t spin_limit);
+
 FORGE_API void forge_sorter_destroy(forge_sorter* s);
 
 /* find_cell_boundaries(sorted_ids, start, end, n, num_cells, ordinal)
@@ -435,6 +444,35 @@ FORGE_API int forge_slab_exchange_end(forge_slab_comm* c, float* cols, uint64_t 
 /* Round 2 (after density): every ghost receives its owner's density in
  * rho[] (indexed like the columns). No host synchronisation. */
 FORGE_API int forge_slab_exchange_rho(forge_slab_comm* c, float* rho, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Field I/O (manifest_runner.rs:192-269 init_fields, :83-92 the result     */
+/* gather). A handle owns a pinned host staging buffer (6 x max_n floats)   */
+/* and a device one (3 x max_n): pageable host arrays are copied through    */
+/* the pinned buffer, pinned ones are copied directly; Vec3f AoS <-> SoA    */
+/* conversion runs on the GPU. Uploads are asynchronous on `stream` (a      */
+/* pageable source may be reused when the call returns); downloads return   */
+/* once the data are in the host arrays. One handle per thread at a time.   */
+/* ------------------------------------------------------------------------ */
+typedef struct forge_io forge_io;
+FORGE_API int forge_io_create(uint64_t max_n, int device, forge_io** out);
+FORGE_API void forge_io_destroy(forge_io* io);
+/* nfields (<= 6) float columns of n values: host[f] -> dev[f]. Replaces the
+ * per-column Array::from_vec uploads of init_fields (manifest_runner.rs:205-213). */
+FORGE_API int forge_io_upload(forge_io* io, const float* const* host, float* const* dev, uint32_t nfields,
+                              uint64_t n, void* stream);
+/* dev[f] -> host[f]; returns when the host arrays hold the data
+ * (Array::to_vec, array.rs, as the result gather uses it). */
+FORGE_API int forge_io_download(forge_io* io, const float* const* dev, float* const* host, uint32_t nfields,
+                                uint64_t n, void* stream);
+/* Vec3f AoS host array (n x 3 floats, the layout init_vec3 produces,
+ * manifest_runner.rs:268-310) -> x, y, z device columns. */
+FORGE_API int forge_io_upload_vec3(forge_io* io, const float* xyz, float* x, float* y, float* z, uint64_t n,
+                                   void* stream);
+/* x, y, z device columns -> interleaved n x 3 host array (the SimResult
+ * positions of manifest_runner.rs:83-92); returns when the data are there. */
+FORGE_API int forge_io_download_vec3(forge_io* io, const float* x, const float* y, const float* z, float* xyz,
+                                     uint64_t n, void* stream);
 
 /* x-window of a grid (no reference counterpart; for a shard of an x-slab
  * decomposition): builds index only global cells [cx0, cx0 + nxw) along x,

@@ -154,3 +154,26 @@ def test_cell_bounds_vs_oracle(cuda, n, C):
     es, ee = oracle.cell_bounds(ids_np, C)
     assert np.array_equal(host_u32(start), es)
     assert np.array_equal(host_u32(end), ee)
+
+
+def test_lookback_wait_gives_up_and_is_reported(cuda):
+    """Failure detection without a GPU fault: the test hook makes the first
+    pass skip tile id 0, so tile 1's decoupled look-back waits on a status
+    word nothing writes. The wait is bounded (4096 polls here): the kernel
+    records the timeout and returns, forge_sorter_check reports
+    FORGE_ERR_TIMEOUT, and the same sorter then sorts correctly again."""
+    n = 5 * 4096 + 17
+    keys_np = oracle.uniform_u32(7, n)
+    s = forge_sph.RadixSorter(n, 0)
+    L = forge_sph.lib()
+    keys, vals = dev(cuda, keys_np), dev(cuda, np.arange(n, dtype=np.uint32))
+    forge_sph.check(L.forge_sorter_set_test_fault(s._h, 1, 1 << 12))
+    s.sort_pairs(keys, vals, n, 0, 32)
+    with pytest.raises(forge_sph.ForgeError, match="look-back"):
+        s.check()
+    forge_sph.check(L.forge_sorter_set_test_fault(s._h, 0, 0))
+    keys, vals = dev(cuda, keys_np), dev(cuda, np.arange(n, dtype=np.uint32))
+    s.sort_pairs(keys, vals, n, 0, 32)
+    s.check()
+    ek, ev = oracle.sort_pairs(keys_np, np.arange(n, dtype=np.uint32))
+    assert np.array_equal(host_u32(keys), ek) and np.array_equal(host_u32(vals), ev)
