@@ -397,13 +397,17 @@ class SlabRun:
     def _step_overlapped(self) -> None:
         """The step with both exchange rounds off the critical path.
 
-        main stream:  density -> prepare (gather, zone lists) -> interior
+        main stream:  density -> prepare (gather, zone lists) -> [wait for
+                      the ghost densities] -> boundary force -> interior
                       force -> [wait payload] finish round 1
-        side stream (high priority), after prepare: density round -> ghost
-                      densities re-read -> boundary force -> round 1 begin
-                      (selection, counts) -> payload (enqueued by the finish)
-        Interior particles have no ghost neighbours and are not in any
-        exchange list, so the interior force overlaps both rounds."""
+        side stream (high priority): density round (beside the prepare
+                      step), then, once the boundary force is done, round 1
+                      begin (selection, counts) and the payload (enqueued by
+                      the finish) -- beside the interior force.
+        The boundary force runs alone on the GPU (it is short and everything
+        after it waits for it); interior particles have no ghost neighbours
+        and are in no exchange list, so the interior force, the bulk of the
+        step, overlaps all of round 1."""
         C = self.cols
         self._mark("start")
         n_own, n = self.n, self.n + self.ng
@@ -412,23 +416,25 @@ class SlabRun:
         self._note_work(C[0, :n_own], rho[:n_own])
         cols6 = [C[k, :n] for k in range(6)]
         zones = self.geo.force_zones(self.reach)
-        self.backend.force_step(cols6, rho, n, n_own, zone=(3,) + zones)
-        self._mark("prepare")
         main = torch.cuda.current_stream()
         if self._hp is None:
             self._hp = torch.cuda.Stream(device=main.device, priority=-1)
+        if not self.local_ghost_density:
+            self._hp.wait_stream(main)
+            with torch.cuda.stream(self._hp):
+                self.comm.exchange_rho(rho)
+        self.backend.force_step(cols6, rho, n, n_own, zone=(3,) + zones)
+        self._mark("prepare")
+        main.wait_stream(self._hp)  # the ghosts' exact densities
+        self.backend.force_step(cols6, rho, n, n_own, zone=(1,) + zones)
+        self._mark("boundary")
         self._hp.wait_stream(main)
         with torch.cuda.stream(self._hp):
-            if not self.local_ghost_density:
-                self.comm.exchange_rho(rho)
-            self._mark_side("ghost_rho_done")
-            self.backend.force_step(cols6, rho, n, n_own, zone=(1,) + zones)
-            self._mark_side("boundary_done")
             self.comm.exchange_begin()
             self._mark_side("counts_done")
         self.backend.force_step(cols6, rho, n, n_own, zone=(2,) + zones)
         self._mark("force")
-        self.comm.exchange_end()  # the main stream waits for the payload, which followed the boundary zone
+        self.comm.exchange_end()  # the main stream waits for the payload
         with torch.cuda.stream(self._hp):
             self._mark_side("payload_done")
         self._mark("exchange")
