@@ -444,6 +444,38 @@ def sharded_roofline(cfg, phase_ms, n_own_max):
             "frac": achieved / hbm, "traffic": None, "peak_kind": peak_kind}
 
 
+def sharded_rate(args, torch, dist, rank, world, local, name, steps, warmup):
+    """The sharded step of workload `name` for `steps` timed steps (device
+    time, max over ranks): particle-steps/s and ms per step. Skewed
+    workloads start at particle-count quantiles and rebalance every 10 steps."""
+    import forge_sph
+    import slab
+    cfg = workloads.config(name)
+    pos, vel = workloads.particles(cfg)
+    cap = int(cfg.n / world * 1.3) + 4 * (cfg.n // cfg.dims[0]) + 1024
+    be = slab.GpuBackend(forge_sph, cfg, cap, local)
+    balance = cfg.name == "blobs4m"
+    run = slab.SlabRun(dist, rank, world, cfg, pos, vel, be, torch.device("cuda", local), capacity=cap, comm="nccl",
+                       forge_sph=forge_sph, balance=balance, halo_width=args.halo_width)
+    del pos, vel
+    count = [0]
+
+    def step():
+        run.step()
+        count[0] += 1
+        if balance and count[0] % 10 == 0:
+            run.rebalance()
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    ms = max_over_ranks(torch, dist, time_steps(torch, step, steps))
+    be.grid.check()
+    return {"value": cfg.n * steps / (ms / 1e3), "unit": "particle-steps/s", "ms_per_step": ms / steps,
+            "particles": cfg.n, "steps": steps, "rebalanced_every": 10 if balance else 0}
+
+
 def run_sharded(args, torch, dist, rank, world, local):
     """N > 1: x-slab decomposition of the workload over `world` GPUs (strong
     scaling: the total particle count is fixed). Halo, ghost-density and
@@ -507,6 +539,7 @@ def run_sharded(args, torch, dist, rank, world, local):
     # e2e: the same sharded step with the rank's particle state read from and
     # written back to pinned host memory every step.
     hbuf = torch.empty((run.cols.shape[0], cap), dtype=torch.float32).pin_memory()
+    io = forge_sph.FieldIO(cap, local)
     cur = run.n
     for k in range(hbuf.shape[0]):
         hbuf[k, :cur].copy_(run.cols[k, :cur])
@@ -514,13 +547,14 @@ def run_sharded(args, torch, dist, rank, world, local):
 
     def one():
         nonlocal cur
-        for k in range(hbuf.shape[0]):
-            run.cols[k, :cur].copy_(hbuf[k, :cur], non_blocking=True)
+        rows = range(hbuf.shape[0])
+        for r0 in (0, 6):  # forge_io_upload: pinned host rows -> device columns (6 per call)
+            io.upload([hbuf[k, :cur] for k in rows[r0:r0 + 6]], [run.cols[k, :cur] for k in rows[r0:r0 + 6]])
         run.n = cur
         step()
         cur = run.n
-        for k in range(hbuf.shape[0]):
-            hbuf[k, :cur].copy_(run.cols[k, :cur], non_blocking=True)
+        for r0 in (0, 6):  # forge_io_download: back to the host (returns when there)
+            io.download([run.cols[k, :cur] for k in rows[r0:r0 + 6]], [hbuf[k, :cur] for k in rows[r0:r0 + 6]])
         moved[0] += cur * hbuf.shape[0] * 4
 
     for _ in range(3):
@@ -556,6 +590,13 @@ def run_sharded(args, torch, dist, rank, world, local):
                         "h2d_bytes_per_step": tot_bytes, "d2h_bytes_per_step": tot_bytes},
                 "gpu_launches": sharded_kernels_per_step(cfg) * args.steps * world,
                 "clocks": clk}
+    if not args.no_extra and cfg.name != "blobs4m":
+        # cfg4 (skewed blobs) at this GPU count as well
+        torch.cuda.empty_cache()
+        ex = sharded_rate(args, torch, dist, rank, world, local, "blobs4m", 10, 3)
+        if rank == 0:
+            line["extra"] = {"blobs4m": ex}
+    if rank == 0:
         print(json.dumps(line), flush=True)
 
 
@@ -666,6 +707,12 @@ def main():
                                     "ms_per_step": ms2 / 20, "phases_ms": ph2,
                                     "l2_flushed_between_steps": r2.l2_flushed, "h": c2.h, "particles_per_cell": 125}
         del r2
+        torch.cuda.empty_cache()
+        c3 = workloads.config("blobs4m")
+        r3, ms3, ph3, _, _, _ = run_sph_single(torch, forge_sph, c3, 10, 3, local, clocks=False)
+        extra["blobs4m"] = {"value": c3.n / (ms3 / 10 / 1e3), "unit": "particle-steps/s", "ms_per_step": ms3 / 10,
+                            "phases_ms": ph3, "l2_flushed_between_steps": r3.l2_flushed, "h": c3.h}
+        del r3
         torch.cuda.empty_cache()
         extra["dam_break_50k_manifest"] = dam_break_manifest(local)
         torch.cuda.empty_cache()

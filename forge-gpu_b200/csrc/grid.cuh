@@ -70,6 +70,32 @@ struct HashKeys {
         keys_out[i] = c;
         return c;
     }
+    // keys of particles i0 .. i0+7 (i0 a multiple of 8; missing ones 0):
+    // 16-byte loads and stores for aligned SoA columns
+    __device__ __forceinline__ void load8(uint32_t i0, uint32_t n, uint32_t (&k)[8]) const {
+        const uintptr_t al = reinterpret_cast<uintptr_t>(px) | reinterpret_cast<uintptr_t>(py) |
+                             reinterpret_cast<uintptr_t>(pz) | reinterpret_cast<uintptr_t>(keys_out);
+        if (stride == 1 && i0 + 8 <= n && (al & 15u) == 0) {
+            float x[8], y[8], z[8];
+            *reinterpret_cast<float4*>(x) = __ldg(reinterpret_cast<const float4*>(px + i0));
+            *reinterpret_cast<float4*>(x + 4) = __ldg(reinterpret_cast<const float4*>(px + i0) + 1);
+            *reinterpret_cast<float4*>(y) = __ldg(reinterpret_cast<const float4*>(py + i0));
+            *reinterpret_cast<float4*>(y + 4) = __ldg(reinterpret_cast<const float4*>(py + i0) + 1);
+            *reinterpret_cast<float4*>(z) = __ldg(reinterpret_cast<const float4*>(pz + i0));
+            *reinterpret_cast<float4*>(z + 4) = __ldg(reinterpret_cast<const float4*>(pz + i0) + 1);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                uint32_t c = cell_of(x[j], y[j], z[j], g);
+                if (sub_bits) c = (c << sub_bits) | slice_of(x[j], g, sub_bits);
+                k[j] = c;
+            }
+            reinterpret_cast<uint4*>(keys_out + i0)[0] = make_uint4(k[0], k[1], k[2], k[3]);
+            reinterpret_cast<uint4*>(keys_out + i0)[1] = make_uint4(k[4], k[5], k[6], k[7]);
+            return;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) k[j] = i0 + j < n ? (*this)(i0 + j) : 0u;
+    }
 };
 
 // Fill value `v` into table[a..b] (inclusive, empty if a > b) with the whole

@@ -72,24 +72,38 @@ __device__ __forceinline__ uint32_t digit_of(uint32_t key, uint32_t shift, uint3
 struct KeysFromArray {
     const uint32_t* __restrict__ keys;
     __device__ __forceinline__ uint32_t operator()(uint32_t i) const { return keys[i]; }
+    // keys i0 .. i0+7 (i0 a multiple of 8; missing keys read as 0): two
+    // 16-byte loads when the array is 16-byte aligned
+    __device__ __forceinline__ void load8(uint32_t i0, uint32_t n, uint32_t (&k)[8]) const {
+        if (i0 + 8 <= n && (reinterpret_cast<uintptr_t>(keys) & 15u) == 0) {
+            const uint4 a = __ldg(reinterpret_cast<const uint4*>(keys + i0));
+            const uint4 b = __ldg(reinterpret_cast<const uint4*>(keys + i0) + 1);
+            k[0] = a.x, k[1] = a.y, k[2] = a.z, k[3] = a.w, k[4] = b.x, k[5] = b.y, k[6] = b.z, k[7] = b.w;
+            return;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) k[j] = i0 + j < n ? keys[i0 + j] : 0u;
+    }
 };
 
 // ---------------------------------------------------------------------------
 // Up-front histogram: hist[p*256 + d] += #keys whose pass-p digit is d, for
 // every pass p. Also zeroes the look-back status table used by the passes.
-// Each warp keeps its own shared histograms; a warp whose 32 keys share a
-// digit (common for cell keys of spatially ordered particles) adds 32 once
-// instead of serialising 32 atomics on one shared address.
+// Each thread takes runs of kHistItems consecutive keys and counts each
+// pass's digits run-length (a change of digit flushes the run with one
+// shared atomic), so spatially ordered cell keys -- long runs of one digit
+// in the upper passes -- cost one atomic per run, and random keys one per
+// key, with no warp-wide votes. Each warp keeps its own shared histograms.
 // ---------------------------------------------------------------------------
 template <class Src>
 __global__ void __launch_bounds__(kHistThreads)
     digit_histogram_kernel(Src src, uint32_t n, uint32_t begin_bit, uint32_t end_bit,
                            uint32_t passes, uint32_t* __restrict__ hist,
                            uint4* __restrict__ status, uint32_t status_vec4) {
+    static_assert(kHistItems == 8, "load8 runs");
     constexpr int kW = kHistThreads / 32;
-    // Per-warp histograms: a warp's shared atomics only contend with itself.
     __shared__ uint32_t s_hist[kW][kMaxPasses * kRadix];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int warp = threadIdx.x >> 5;
     for (uint32_t j = threadIdx.x; j < kW * kMaxPasses * kRadix; j += kHistThreads) (&s_hist[0][0])[j] = 0;
 
     const uint32_t stride = gridDim.x * kHistThreads;
@@ -99,33 +113,36 @@ __global__ void __launch_bounds__(kHistThreads)
     __syncthreads();
 
     uint32_t* wh = s_hist[warp];
-    // kHistItems independent loads per thread in flight before any counting.
-    for (uint32_t base = blockIdx.x * kHistThreads * kHistItems; base < n; base += stride * kHistItems) {
+    uint32_t cur[kMaxPasses], cnt[kMaxPasses];
+#pragma unroll
+    for (int p = 0; p < kMaxPasses; ++p) cur[p] = 0, cnt[p] = 0;
+    for (uint32_t i0 = (blockIdx.x * kHistThreads + threadIdx.x) * kHistItems; i0 < n;
+         i0 += stride * kHistItems) {
         uint32_t key[kHistItems];
+        src.load8(i0, n, key);
+        const uint32_t m = min((uint32_t)kHistItems, n - i0);
 #pragma unroll
         for (int k = 0; k < kHistItems; ++k) {
-            const uint32_t i = base + k * kHistThreads + threadIdx.x;
-            key[k] = i < n ? src(i) : 0u;
-        }
+            if ((uint32_t)k >= m) break;
 #pragma unroll
-        for (int k = 0; k < kHistItems; ++k) {
-            const bool valid = base + k * kHistThreads + threadIdx.x < n;
-            for (uint32_t p = 0; p < passes; ++p) {
+            for (int p = 0; p < kMaxPasses; ++p) {
+                if ((uint32_t)p >= passes) break;
                 const uint32_t shift = begin_bit + p * kRadixBits;
                 const uint32_t bits = min((uint32_t)kRadixBits, end_bit - shift);
                 const uint32_t d = digit_of(key[k], shift, (1u << bits) - 1u);
-                // Spatially ordered cell keys often give a whole warp one digit:
-                // one add of 32 instead of 32 conflicting atomics.
-                const uint32_t d0 = __shfl_sync(0xffffffffu, d, 0);
-                if (__all_sync(0xffffffffu, valid && d == d0)) {
-                    if (lane == 0) wh[p * kRadix + d0] += 32u;
-                } else if (valid) {
-                    atomicAdd(&wh[p * kRadix + d], 1u);
+                if (d != cur[p]) {
+                    if (cnt[p]) atomicAdd(&wh[p * kRadix + cur[p]], cnt[p]);
+                    cur[p] = d;
+                    cnt[p] = 1;
+                } else {
+                    ++cnt[p];
                 }
-                __syncwarp();
             }
         }
     }
+#pragma unroll
+    for (int p = 0; p < kMaxPasses; ++p)
+        if (cnt[p]) atomicAdd(&wh[p * kRadix + cur[p]], cnt[p]);
     __syncthreads();
     for (uint32_t j = threadIdx.x; j < passes * kRadix; j += kHistThreads) {
         uint32_t c = 0;
@@ -139,8 +156,11 @@ __global__ void __launch_bounds__(kHistThreads)
 // One Onesweep pass. IOTA: the input values are the element indices (first
 // pass of the grid build), vals_in is not read.
 // ---------------------------------------------------------------------------
+#ifndef FORGE_SORT_MIN_BLOCKS
+#define FORGE_SORT_MIN_BLOCKS 5  // 51 registers (spills): 5 CTAs per SM, the shared-memory limit
+#endif
 template <bool IOTA>
-__global__ void __launch_bounds__(kThreads, 4)
+__global__ void __launch_bounds__(kThreads, FORGE_SORT_MIN_BLOCKS)
     onesweep_pass_kernel(const uint32_t* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
                          uint32_t* __restrict__ keys_out, uint32_t* __restrict__ vals_out,
                          uint32_t n, uint32_t shift, uint32_t bits,
@@ -152,7 +172,8 @@ __global__ void __launch_bounds__(kThreads, 4)
     __shared__ uint32_t s_tile_off[kRadix];       // digit start inside the sorted tile
     __shared__ uint32_t s_base[kRadix];           // global dst = s_base[d] + tile position
     __shared__ uint32_t s_scan[kWarps + 1];
-    __shared__ uint32_t s_exchange[kTile];
+    __shared__ uint32_t s_exchange[kTile];  // the tile's keys, in sorted order
+    __shared__ uint32_t s_vals[kTile];      // its values: input order (staged), then sorted order
     __shared__ uint32_t s_tile;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -170,16 +191,22 @@ __global__ void __launch_bounds__(kThreads, 4)
     const uint32_t warp_start = tile_start + warp * 32 * kItems;
 
     // Load: warp-striped so each load instruction is 128 contiguous bytes and
-    // (item, lane) order equals input order.
-    uint32_t key[kItems], val[kItems];
+    // (item, lane) order equals input order. The values go straight to
+    // shared memory (cp.async, no registers held through the ranking); they
+    // are needed only once every key has its tile position.
+    uint32_t key[kItems];
+    const uint32_t wbase = (uint32_t)warp * 32u * kItems;  // this warp's first tile slot
 #pragma unroll
     for (int k = 0; k < kItems; ++k) {
         const uint32_t idx = warp_start + k * 32 + lane;
         const bool ok = idx < n;
         key[k] = ok ? keys_in[idx] : 0u;
-        if (IOTA) val[k] = idx;
-        else val[k] = ok ? vals_in[idx] : 0u;
+        if (!IOTA && ok) {
+            const uint32_t sa = (uint32_t)__cvta_generic_to_shared(&s_vals[wbase + k * 32 + lane]);
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(sa), "l"(vals_in + idx) : "memory");
+        }
     }
+    if (!IOTA) asm volatile("cp.async.commit_group;" ::: "memory");
 
     // Early counts: per-warp digit histograms from shared atomics (a warp
     // whose keys share one digit adds 32 once), so the tile aggregate is
@@ -286,31 +313,37 @@ __global__ void __launch_bounds__(kThreads, 4)
         st_relaxed_u32(my_status, par | kFlagPre | ((excl + cnt) & kCountMask));
     }
     s_base[tid] = hist_off + excl - tile_off;
-    __syncthreads();
 
-    const uint32_t tile_n = min((uint32_t)kTile, n - tile_start);
-    uint32_t dst[kItems];
+    // Values to their tile positions: read this thread's staged values
+    // (input order), then, after a barrier, write them sorted.
+    uint32_t val[kItems];
+    if (IOTA) {
 #pragma unroll
-    for (int k = 0; k < kItems; ++k) {
-        const uint32_t j = tid + k * kThreads;
-        dst[k] = 0xffffffffu;
-        if (j < tile_n) {
-            const uint32_t kk = s_exchange[j];
-            dst[k] = s_base[digit_of(kk, shift, mask)] + j;
-            keys_out[dst[k]] = kk;
-        }
+        for (int k = 0; k < kItems; ++k) val[k] = warp_start + k * 32 + lane;
+    } else {
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        __syncthreads();  // every thread's copies landed
+#pragma unroll
+        for (int k = 0; k < kItems; ++k) val[k] = s_vals[wbase + k * 32 + lane];
     }
     __syncthreads();
 #pragma unroll
     for (int k = 0; k < kItems; ++k)
-        if (pos[k] != 0xffffffffu) s_exchange[pos[k]] = val[k];
+        if (pos[k] != 0xffffffffu) s_vals[pos[k]] = val[k];
     __syncthreads();
+
+    // Coalesced scatter of the sorted tile: runs of one digit are contiguous.
+    const uint32_t tile_n = min((uint32_t)kTile, n - tile_start);
 #pragma unroll
     for (int k = 0; k < kItems; ++k) {
         const uint32_t j = tid + k * kThreads;
-        if (j < tile_n) vals_out[dst[k]] = s_exchange[j];
+        if (j < tile_n) {
+            const uint32_t kk = s_exchange[j];
+            const uint32_t dst = s_base[digit_of(kk, shift, mask)] + j;
+            keys_out[dst] = kk;
+            vals_out[dst] = s_vals[j];
+        }
     }
-    __syncthreads();
 }
 
 }  // namespace radix
