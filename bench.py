@@ -256,11 +256,30 @@ def e2e_sph(torch, forge_sph, cfg, pos, vel, steps, warmup):
     hp = [torch.from_numpy(x.copy()).pin_memory() for x in pos + vel]
     dv = run.p + run.v
     io = forge_sph.FieldIO(cfg.n, torch.cuda.current_device())
+    # The state goes through host memory every step, in chunks: chunk c of
+    # step k's result is read back (copy engine D2H) and, as soon as it is
+    # on the host, sent again as step k+1's input (copy engine H2D), so the
+    # two directions overlap; the step itself waits for every chunk.
+    main = torch.cuda.current_stream()
+    s_down, s_up = torch.cuda.Stream(), torch.cuda.Stream()
+    chunks = 8
+    bounds = [cfg.n * c // chunks for c in range(chunks + 1)]
+    up_done = torch.cuda.Event()
+    io.upload(hp, dv, stream=main)
 
     def one():
-        io.upload(hp, dv)    # forge_io_upload: pinned host columns -> device
         run.step()
-        io.download(dv, hp)  # forge_io_download: back to the host (returns when there)
+        step_done = torch.cuda.Event()
+        step_done.record(main)
+        s_down.wait_event(step_done)
+        for a, b in zip(bounds[:-1], bounds[1:]):
+            io.download([d[a:b] for d in dv], [h[a:b] for h in hp], stream=s_down)  # pinned: asynchronous
+            landed = torch.cuda.Event()
+            landed.record(s_down)
+            s_up.wait_event(landed)
+            io.upload([h[a:b] for h in hp], [d[a:b] for d in dv], stream=s_up)
+        up_done.record(s_up)
+        main.wait_event(up_done)
 
     for _ in range(warmup):
         one()

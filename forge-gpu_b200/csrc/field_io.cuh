@@ -134,14 +134,21 @@ extern "C" int forge_io_download(forge_io* io, const float* const* dev, float* c
     if (n == 0 || nfields == 0) return FORGE_OK;
     FORGE_DEVICE_SCOPE(io->device);
     cudaStream_t st = as_stream(stream);
-    int rc = io_reuse(io);
-    if (rc != FORGE_OK) return rc;
     bool any_staged = false;
     for (uint32_t f = 0; f < nfields; ++f) {
         if (!host[f] || !dev[f]) return set_error(FORGE_ERR_INVALID_ARG, "forge_io_download: field %u is NULL", f);
+        any_staged |= !host_pinned(host[f]);
+    }
+    if (!any_staged) {  // all pinned: DMA straight into them, asynchronously
+        for (uint32_t f = 0; f < nfields; ++f)
+            FORGE_CUDA(cudaMemcpyAsync(host[f], dev[f], n * sizeof(float), cudaMemcpyDeviceToHost, st));
+        return FORGE_OK;
+    }
+    int rc = io_reuse(io);
+    if (rc != FORGE_OK) return rc;
+    for (uint32_t f = 0; f < nfields; ++f) {
         const bool direct = host_pinned(host[f]);
         float* dst = direct ? host[f] : io->pinned + (size_t)f * io->max_n;
-        any_staged |= !direct;
         FORGE_CUDA(cudaMemcpyAsync(dst, dev[f], n * sizeof(float), cudaMemcpyDeviceToHost, st));
     }
     FORGE_CUDA(cudaEventRecord(io->ev, st));

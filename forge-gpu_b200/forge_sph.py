@@ -420,7 +420,9 @@ class FieldIO:
                                     n, _stream(stream)))
 
     def download(self, dev, host, stream=None) -> None:
-        """dev[k] -> host[k]; returns when the data are on the host."""
+        """dev[k] -> host[k]: enqueued on `stream` when every host array is
+        pinned (synchronise before reading them), else returns when the data
+        are on the host."""
         n = len(dev[0]) if dev else 0
         check(lib().forge_io_download(self._h, self._vp([ptr(d) for d in dev]), self._vp(_host_ptrs(host)),
                                       len(dev), n, _stream(stream)))

@@ -461,8 +461,11 @@ FORGE_API void forge_io_destroy(forge_io* io);
  * per-column Array::from_vec uploads of init_fields (manifest_runner.rs:205-213). */
 FORGE_API int forge_io_upload(forge_io* io, const float* const* host, float* const* dev, uint32_t nfields,
                               uint64_t n, void* stream);
-/* dev[f] -> host[f]; returns when the host arrays hold the data
- * (Array::to_vec, array.rs, as the result gather uses it). */
+/* dev[f] -> host[f] (Array::to_vec, array.rs, as the result gather uses
+ * it). If every host array is page-locked the copies are only enqueued on
+ * `stream` (the caller synchronises, and can overlap them with uploads on
+ * another stream); otherwise the call returns when the host arrays hold the
+ * data. */
 FORGE_API int forge_io_download(forge_io* io, const float* const* dev, float* const* host, uint32_t nfields,
                                 uint64_t n, void* stream);
 /* Vec3f AoS host array (n x 3 floats, the layout init_vec3 produces,
