@@ -652,18 +652,27 @@ sph::Geom geom_of(const forge_grid* g, float h) {
 
 constexpr uint32_t kSphThreads = 128;
 
-int launch_density(forge_grid* g, const forge_sph_params* p, float* density, cudaStream_t st) {
-    if (g->n == 0) return FORGE_OK;
-    sph::density_pair_kernel<<<grid_blocks((g->n + 1) / 2, kSphThreads), kSphThreads, 0, st>>>(
-        g->pos4, g->cell_start, g->sorted_idx, (uint32_t)g->n, geom_of(g, p->h), make_consts(p), g->vel4, g->aux, density);
-    FORGE_LAUNCHED();
-    return FORGE_OK;
-}
-
 // Two particles per thread pay off when cells are sparse (the candidate scan
 // dominates); with dense cells the per-hit work dominates and one particle
 // per thread diverges less. Mean occupancy n / C selects the kernel.
 constexpr double kPairMaxOccupancy = 8.0;
+
+int launch_density(forge_grid* g, const forge_sph_params* p, float* density, cudaStream_t st) {
+    if (g->n == 0) return FORGE_OK;
+    // Four particles per thread share each neighbour load where cells hold a
+    // few particles (cfg3: 1.41 -> 1.25 ms); with dense cells the union of
+    // four windows adds more evaluations than it saves loads: two per thread.
+    if ((double)g->n / (double)cells_w(g) < kPairMaxOccupancy)
+        sph::density_multi_kernel<4><<<grid_blocks((g->n + 3) / 4, kSphThreads), kSphThreads, 0, st>>>(
+            g->pos4, g->cell_start, g->sorted_idx, (uint32_t)g->n, geom_of(g, p->h), make_consts(p), g->vel4, g->aux,
+            density);
+    else
+        sph::density_pair_kernel<<<grid_blocks((g->n + 1) / 2, kSphThreads), kSphThreads, 0, st>>>(
+            g->pos4, g->cell_start, g->sorted_idx, (uint32_t)g->n, geom_of(g, p->h), make_consts(p), g->vel4, g->aux,
+            density);
+    FORGE_LAUNCHED();
+    return FORGE_OK;
+}
 
 template <int TERMS, int EPI>
 void launch_force_t(forge_grid* g, const sph::SphConsts& c, const sph::StepEpi& ep, const sph::ForceOut& o,

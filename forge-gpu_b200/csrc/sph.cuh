@@ -261,6 +261,77 @@ __global__ void __launch_bounds__(128, FORGE_DENSITY_MIN_BLOCKS)
     }
 }
 
+// Density, P consecutive cell-ordered particles per thread: when all lie in
+// one grid row (and cell size >= h), one walk over the union of their
+// windows feeds P pair evaluations per neighbour load (extra candidates add
+// exactly +0, as in the two-particle kernel); otherwise P single walks.
+template <int P>
+__global__ void __launch_bounds__(128)
+    density_multi_kernel(const float4* __restrict__ pos4, const uint32_t* __restrict__ cell_start,
+                         const uint32_t* __restrict__ sorted_idx, uint32_t n, Geom g, SphConsts c,
+                         float4* __restrict__ vel4, float2* __restrict__ aux, float* __restrict__ density_out) {
+    const uint32_t s0 = P * (blockIdx.x * blockDim.x + threadIdx.x);
+    if (s0 >= n) return;
+    const uint32_t np = min((uint32_t)P, n - s0);
+    float4 p[P];
+    float rho[P];
+    bool together = g.pairable != 0;
+    const Frame f0 = make_frame(p[0] = pos4[s0], g);
+#pragma unroll
+    for (int k = 1; k < P; ++k) {
+        p[k] = (uint32_t)k < np ? pos4[s0 + k] : p[0];
+        const Frame fk = make_frame(p[k], g);
+        together = together && fk.cy == f0.cy && fk.cz == f0.cz;
+    }
+#pragma unroll
+    for (int k = 0; k < P; ++k) rho[k] = 0.f;
+    if (together) {
+#pragma unroll 1
+        for (int r = 0; r < 9; ++r) {
+            int lo = 0x7fffffff, hi = -1;
+#pragma unroll
+            for (int k = 0; k < P; ++k) {
+                int l, h;
+                if (row_window(make_frame(p[k], g), r, g, c.h2_skip, l, h)) {
+                    lo = min(lo, l);
+                    hi = max(hi, h);
+                }
+            }
+            if (lo > hi) continue;
+            const uint32_t row = row_base(g, f0, r);
+            const uint32_t b = __ldg(cell_start + row + lo), e = __ldg(cell_start + row + hi + 1);
+#pragma unroll 2
+            for (uint32_t j = b; j < e; ++j) {
+                const float4 q = __ldg(pos4 + j);
+#pragma unroll
+                for (int k = 0; k < P; ++k) {
+                    const float d = poly6_base(p[k], q, c.h2);
+                    rho[k] = fmaf(d * d, d, rho[k]);
+                }
+            }
+        }
+    } else {
+#pragma unroll
+        for (int k = 0; k < P; ++k)
+            if ((uint32_t)k < np)
+                for_each_range(p[k], g, cell_start, c.h2_skip,
+                               [&](uint32_t b, uint32_t e) { poly6_one(pos4, b, e, p[k], c, rho[k]); });
+    }
+#pragma unroll
+    for (int k = 0; k < P; ++k) {
+        if ((uint32_t)k >= np) break;
+        const float r = rho[k] * c.mass_poly6;
+        float inv_rho;
+        float2 a;
+        density_derived(r, c, inv_rho, a);
+        if (vel4 != nullptr) {
+            vel4[s0 + k].w = inv_rho;
+            aux[s0 + k] = a;
+        }
+        if (density_out != nullptr) density_out[sorted_idx[s0 + k]] = r;
+    }
+}
+
 // vel4[s] = (vx[i], vy[i], vz[i], 1/rho[i]), aux[s] = (p/rho, rho), i = svals[s]
 // (forge_sph_force with a caller-supplied density).
 __global__ void __launch_bounds__(256)
