@@ -110,6 +110,8 @@ class Clocks:
 
 
 PHASES = ("sort", "cells_gather", "density", "force")
+WALKS = {"auto": 0, "thread": 1, "group4": 2, "group8": 3, "group16": 4}  # forge_grid_set_walk
+WALK = 0
 
 
 def kernels_per_step(cfg):
@@ -165,6 +167,7 @@ class SphRun:
         self.v = [torch.from_numpy(x).to(dev) for x in vel]
         self.rho = torch.empty(cfg.n, dtype=torch.float32, device=dev)
         self.grid = forge_sph.HashGrid(cfg.cell_size, cfg.dims, (0, 0, 0), cfg.n, dev.index)
+        self.grid.set_walk(WALK)
         self.sp = sph_params(forge_sph, cfg)
         self.stp = step_params(forge_sph, cfg)
         self.args = [x.data_ptr() for x in self.p] + [x.data_ptr() for x in self.v] + [self.rho.data_ptr()]
@@ -506,7 +509,7 @@ def run_sharded(args, torch, dist, rank, world, local):
     pos, vel = workloads.particles(cfg)
     cap = int(cfg.n / world * 1.3) + 4 * (cfg.n // cfg.dims[0]) + 1024
     dev = torch.device("cuda", local)
-    be = slab.GpuBackend(forge_sph, cfg, cap, local)
+    be = slab.GpuBackend(forge_sph, cfg, cap, local, walk=WALK)
     # skewed workloads: bounds at particle-count quantiles, rebalanced every k steps
     balance = args.rebalance_every > 0 if args.rebalance_every is not None else cfg.name == "blobs4m"
     every = (args.rebalance_every or 10) if balance else 0
@@ -628,6 +631,8 @@ def main():
     ap.add_argument("--workload", default="sharded16m",
                     choices=["sharded16m", "dambreak1m", "dambreak1m_h025", "dambreak65k", "blobs4m", "ref65k"])
     ap.add_argument("--no-extra", action="store_true", help="skip the 1M dam-break and 2^28 sort extras")
+    ap.add_argument("--walk", choices=list(WALKS), default="auto",
+                    help="neighbour-pass kernel family (auto: group walks below 2^18 particles)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
     ap.add_argument("--sort-only", type=int, default=None, metavar="LOG2N",
                     help="time only the standalone key/value sort of 2^LOG2N uniform pairs (for profiling)")
@@ -638,6 +643,8 @@ def main():
                     help="N>1: halo of h with a ghost-density round, or of 2h with ghost densities computed locally")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    global WALK
+    WALK = WALKS[args.walk]
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

@@ -15,6 +15,7 @@
 #include "grid.cuh"
 #include "radix_sort.cuh"
 #include "sph.cuh"
+#include "sph_group.cuh"
 #include "slab.cuh"
 
 using namespace forge;
@@ -435,6 +436,7 @@ struct forge_grid {
     uint32_t* cell_start = nullptr;  // (C << kSphSubBits) + 1
     uint32_t* chunk_val = nullptr;   // marks of whole table chunks to fill (grid::kFillChunk entries each)
     uint32_t sub_bits = 0;           // x-slices of the last build (0: plain cells)
+    int walk = FORGE_WALK_AUTO;      // neighbour-pass kernel family (forge_grid_set_walk)
     float4* pos4 = nullptr;          // cell-ordered (x, y, z, key)
     float4* vel4 = nullptr;          // cell-ordered (vx, vy, vz, 1/rho)
     float2* aux = nullptr;           // cell-ordered (p/rho, rho)
@@ -657,47 +659,102 @@ constexpr uint32_t kSphThreads = 128;
 // per thread diverges less. Mean occupancy n / C selects the kernel.
 constexpr double kPairMaxOccupancy = 8.0;
 
+// Neighbour-pass kernel family of a build. Per-thread walks (one, two or
+// four particles per thread) need many particles to fill the GPU: below
+// kGroupMaxN particles, warp-cooperative group walks (sph_group.cuh) give
+// every particle 4 lanes instead, G = 8 particles per warp.
+#ifndef FORGE_GROUP_MAX_N
+#define FORGE_GROUP_MAX_N (1u << 18)
+#endif
+constexpr uint64_t kGroupMaxN = FORGE_GROUP_MAX_N;
+
+int walk_of(const forge_grid* g) {
+    if (g->walk != FORGE_WALK_AUTO) return g->walk;
+    return g->n < kGroupMaxN ? FORGE_WALK_GROUP8 : FORGE_WALK_THREAD;
+}
+
+template <int G>
+uint32_t group_blocks(uint64_t n) {
+    return grid_blocks((n + G - 1) / G * 32, kSphThreads);
+}
+
 int launch_density(forge_grid* g, const forge_sph_params* p, float* density, cudaStream_t st) {
     if (g->n == 0) return FORGE_OK;
-    // Four particles per thread share each neighbour load where cells hold a
-    // few particles (cfg3: 1.41 -> 1.25 ms); with dense cells the union of
-    // four windows adds more evaluations than it saves loads: two per thread.
-    if ((double)g->n / (double)cells_w(g) < kPairMaxOccupancy)
-        sph::density_multi_kernel<4><<<grid_blocks((g->n + 3) / 4, kSphThreads), kSphThreads, 0, st>>>(
-            g->pos4, g->cell_start, g->sorted_idx, (uint32_t)g->n, geom_of(g, p->h), make_consts(p), g->vel4, g->aux,
-            density);
-    else
-        sph::density_pair_kernel<<<grid_blocks((g->n + 1) / 2, kSphThreads), kSphThreads, 0, st>>>(
-            g->pos4, g->cell_start, g->sorted_idx, (uint32_t)g->n, geom_of(g, p->h), make_consts(p), g->vel4, g->aux,
-            density);
+    const sph::Geom G = geom_of(g, p->h);
+    const sph::SphConsts c = make_consts(p);
+    const uint32_t n = (uint32_t)g->n;
+    switch (walk_of(g)) {
+        case FORGE_WALK_GROUP4:
+            sph::density_group_kernel<4><<<group_blocks<4>(n), kSphThreads, 0, st>>>(
+                g->pos4, g->cell_start, g->sorted_idx, n, G, c, g->vel4, g->aux, density);
+            break;
+        case FORGE_WALK_GROUP8:
+            sph::density_group_kernel<8><<<group_blocks<8>(n), kSphThreads, 0, st>>>(
+                g->pos4, g->cell_start, g->sorted_idx, n, G, c, g->vel4, g->aux, density);
+            break;
+        case FORGE_WALK_GROUP16:
+            sph::density_group_kernel<16><<<group_blocks<16>(n), kSphThreads, 0, st>>>(
+                g->pos4, g->cell_start, g->sorted_idx, n, G, c, g->vel4, g->aux, density);
+            break;
+        default:
+            // Four particles per thread share each neighbour load where cells
+            // hold a few particles (cfg3: 1.41 -> 1.25 ms); with dense cells
+            // the union of four windows adds more evaluations than it saves
+            // loads: two per thread.
+            if ((double)n / (double)cells_w(g) < kPairMaxOccupancy)
+                sph::density_multi_kernel<4><<<grid_blocks((n + 3) / 4, kSphThreads), kSphThreads, 0, st>>>(
+                    g->pos4, g->cell_start, g->sorted_idx, n, G, c, g->vel4, g->aux, density);
+            else
+                sph::density_pair_kernel<<<grid_blocks((n + 1) / 2, kSphThreads), kSphThreads, 0, st>>>(
+                    g->pos4, g->cell_start, g->sorted_idx, n, G, c, g->vel4, g->aux, density);
+    }
     FORGE_LAUNCHED();
     return FORGE_OK;
+}
+
+// One force pass over all particles (LIST false) or a zone list (the grid
+// covers an upper bound of the list; warps past its end leave at once).
+template <int TERMS, int EPI, bool LIST>
+void launch_force_k(forge_grid* g, const sph::SphConsts& c, const sph::StepEpi& ep, const sph::ForceOut& o,
+                    const sph::ZoneList& zl, cudaStream_t st) {
+    const sph::Geom G = geom_of(g, c.h);
+    const uint32_t n = (uint32_t)g->n;
+    switch (walk_of(g)) {
+        case FORGE_WALK_GROUP4:
+            sph::force_group_kernel<TERMS, EPI, 4, LIST><<<group_blocks<4>(n), kSphThreads, 0, st>>>(
+                g->pos4, g->vel4, g->aux, g->cell_start, g->sorted_idx, n, G, c, ep, o, zl);
+            break;
+        case FORGE_WALK_GROUP8:
+            sph::force_group_kernel<TERMS, EPI, 8, LIST><<<group_blocks<8>(n), kSphThreads, 0, st>>>(
+                g->pos4, g->vel4, g->aux, g->cell_start, g->sorted_idx, n, G, c, ep, o, zl);
+            break;
+        case FORGE_WALK_GROUP16:
+            sph::force_group_kernel<TERMS, EPI, 16, LIST><<<group_blocks<16>(n), kSphThreads, 0, st>>>(
+                g->pos4, g->vel4, g->aux, g->cell_start, g->sorted_idx, n, G, c, ep, o, zl);
+            break;
+        default:
+            if ((double)n / (double)cells_w(g) < kPairMaxOccupancy)
+                sph::force_kernel<TERMS, EPI, LIST><<<grid_blocks((n + 1) / 2, kSphThreads), kSphThreads, 0, st>>>(
+                    g->pos4, g->vel4, g->aux, g->cell_start, g->sorted_idx, n, G, c, ep, o, zl);
+            else
+                sph::force_single_kernel<TERMS, EPI, LIST><<<grid_blocks(n, kSphThreads), kSphThreads, 0, st>>>(
+                    g->pos4, g->vel4, g->aux, g->cell_start, g->sorted_idx, n, G, c, ep, o, zl);
+    }
 }
 
 template <int TERMS, int EPI>
 void launch_force_t(forge_grid* g, const sph::SphConsts& c, const sph::StepEpi& ep, const sph::ForceOut& o,
                     cudaStream_t st) {
-    if ((double)g->n / (double)cells_w(g) < kPairMaxOccupancy)
-        sph::force_kernel<TERMS, EPI, false><<<grid_blocks((g->n + 1) / 2, kSphThreads), kSphThreads, 0, st>>>(
-            g->pos4, g->vel4, g->aux, g->cell_start, g->sorted_idx, (uint32_t)g->n, geom_of(g, c.h), c, ep, o, {});
-    else
-        sph::force_single_kernel<TERMS, EPI, false><<<grid_blocks(g->n, kSphThreads), kSphThreads, 0, st>>>(
-            g->pos4, g->vel4, g->aux, g->cell_start, g->sorted_idx, (uint32_t)g->n, geom_of(g, c.h), c, ep, o, {});
+    launch_force_k<TERMS, EPI, false>(g, c, ep, o, {}, st);
 }
 
-// One zone of a zoned force step: the same kernels over a zone list. The
-// list size is known only on the device, so the grid covers n (blocks past
-// the list leave at once); short-lived blocks leave room for concurrent
-// work (the other zone, the exchange kernels, NCCL).
+// One zone of a zoned force step: the same kernels over a zone list; short-
+// lived blocks leave room for concurrent work (the other zone, the exchange
+// kernels, NCCL).
 int launch_force_zone(forge_grid* g, const sph::SphConsts& c, const sph::StepEpi& ep, const sph::ForceOut& o,
                       uint32_t list, cudaStream_t st) {
     const sph::ZoneList zl{g->zone_idx, g->zone_counts, list};
-    if ((double)g->n / (double)cells_w(g) < kPairMaxOccupancy)
-        sph::force_kernel<3, 1, true><<<grid_blocks((g->n + 1) / 2, kSphThreads), kSphThreads, 0, st>>>(
-            g->pos4, g->vel4, g->aux, g->cell_start, g->sorted_idx, (uint32_t)g->n, geom_of(g, c.h), c, ep, o, zl);
-    else
-        sph::force_single_kernel<3, 1, true><<<grid_blocks(g->n, kSphThreads), kSphThreads, 0, st>>>(
-            g->pos4, g->vel4, g->aux, g->cell_start, g->sorted_idx, (uint32_t)g->n, geom_of(g, c.h), c, ep, o, zl);
+    launch_force_k<3, 1, true>(g, c, ep, o, zl, st);
     FORGE_LAUNCHED();
     return FORGE_OK;
 }
@@ -1002,6 +1059,14 @@ extern "C" int forge_sph_step(forge_grid* g, const forge_sph_params* p, const fo
     FORGE_LAUNCHED();
     prof_mark(g, 4, st);
     prof_step_done(g);
+    return FORGE_OK;
+}
+
+extern "C" int forge_grid_set_walk(forge_grid* g, int walk) {
+    if (!g) return set_error(FORGE_ERR_INVALID_ARG, "forge_grid_set_walk: grid is NULL");
+    if (walk < FORGE_WALK_AUTO || walk > FORGE_WALK_GROUP16)
+        return set_error(FORGE_ERR_INVALID_ARG, "forge_grid_set_walk: unknown walk %d", walk);
+    g->walk = walk;
     return FORGE_OK;
 }
 

@@ -40,6 +40,8 @@ FORGE_ERR_NCCL = -5
 FORGE_ERR_DEVICE = -6
 
 OP_GRAVITY, OP_DRAG, OP_INTEGRATE, OP_GROUND, OP_SPHERE, OP_BOX = 1, 2, 3, 4, 5, 6
+# neighbour-pass kernel families (forge_grid_set_walk)
+WALK_AUTO, WALK_THREAD, WALK_GROUP4, WALK_GROUP8, WALK_GROUP16 = 0, 1, 2, 3, 4
 STEP_MAX_OPS = 8
 
 TERM_PRESSURE = 1
@@ -66,7 +68,7 @@ EXPORTED = (
     "forge_grid_create", "forge_grid_build", "forge_grid_build_aos", "forge_grid_query",
     "forge_grid_check", "forge_grid_destroy",
     "forge_sph_density", "forge_sph_force", "forge_sph_step",
-    "forge_grid_profile_enable", "forge_grid_profile_read", "forge_grid_set_x_window",
+    "forge_grid_profile_enable", "forge_grid_profile_read", "forge_grid_set_x_window", "forge_grid_set_walk",
     "forge_io_create", "forge_io_destroy", "forge_io_upload", "forge_io_download", "forge_io_upload_vec3",
     "forge_io_download_vec3",
     "forge_sort_pairs_static",
@@ -143,6 +145,7 @@ def lib() -> ctypes.CDLL:
                                  vp, vp, u64, vp]),
         "forge_grid_profile_enable": (i32, [vp, u32]),
         "forge_grid_set_x_window": (i32, [vp, u32, u32]),
+        "forge_grid_set_walk": (i32, [vp, i32]),
         "forge_io_create": (i32, [u64, i32, pvp]),
         "forge_io_destroy": (None, [vp]),
         "forge_io_upload": (i32, [vp, pvp, pvp, u32, u64, vp]),
@@ -303,6 +306,10 @@ class HashGrid:
     @property
     def handle(self):
         return self._h
+
+    def set_walk(self, walk: int) -> None:
+        """Neighbour-pass kernel family (WALK_*; WALK_AUTO by particle count)."""
+        check(lib().forge_grid_set_walk(self._h, walk))
 
     def set_x_window(self, cx0: int, nxw: int) -> None:
         """Index only global cells [cx0, cx0 + nxw) along x (a shard's slab);

@@ -444,9 +444,10 @@ class SlabRun:
 class GpuBackend:
     """Per-rank compute through libforge_sph (sm_100a kernels)."""
 
-    def __init__(self, forge_sph, cfg, capacity: int, device: int):
+    def __init__(self, forge_sph, cfg, capacity: int, device: int, walk: int = 0):
         self.f, self.cfg = forge_sph, cfg
         self.grid = forge_sph.HashGrid(cfg.cell_size, cfg.dims, (0.0, 0.0, 0.0), capacity, device)
+        self.grid.set_walk(walk)  # neighbour-pass kernel family (0: by particle count)
         self.sp = forge_sph.SphParams(cfg.h, cfg.mass, cfg.gas_constant, cfg.rest_density, cfg.viscosity)
         stp = forge_sph.StepParams()
         stp.dt = cfg.dt

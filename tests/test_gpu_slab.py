@@ -39,7 +39,9 @@ def _rank_main(rank, world, port, out_path):
         torch.cuda.set_device(0)
         cfg = _cfg()
         pos, vel = _inputs(cfg)
-        be = slab.GpuBackend(forge_sph, cfg, cfg.n, 0)
+        # per-thread walks on both sides: bit-for-bit comparison (see
+        # test_gpu_slab_nccl.py)
+        be = slab.GpuBackend(forge_sph, cfg, cfg.n, 0, walk=forge_sph.WALK_THREAD)
         run = slab.SlabRun(dist, rank, world, cfg, pos, vel, be, torch.device("cuda", 0), order_by_id=True,
                            comm=lambda r: slab_cpu.PyComm(r, dist, comm_device="cpu"))
         for _ in range(STEPS):
@@ -75,6 +77,7 @@ def test_two_rank_sharded_step_matches_single_gpu(cuda, tmp_path):
     v = [torch.from_numpy(x.copy()).cuda() for x in vel]
     rho = torch.empty(cfg.n, dtype=torch.float32, device="cuda")
     g = forge_sph.HashGrid(cfg.cell_size, cfg.dims, (0, 0, 0), cfg.n, 0)
+    g.set_walk(forge_sph.WALK_THREAD)
     be = slab.GpuBackend(forge_sph, cfg, 1, 0)
     L = forge_sph.lib()
     for _ in range(STEPS):

@@ -47,7 +47,10 @@ def _rank_main(rank, world, port, out_path, order_by_id=True, skewed=False, halo
         torch.cuda.set_device(rank)
         cfg = _cfg()
         pos, vel = _skewed(cfg) if skewed else _inputs(cfg)
-        be = slab.GpuBackend(forge_sph, cfg, cfg.n, rank)
+        # test mode compares bit for bit with one GPU: both sides use the
+        # per-thread walks, whose per-particle sums do not depend on which
+        # particles share a thread (group walks agree to fp32 rounding only)
+        be = slab.GpuBackend(forge_sph, cfg, cfg.n, rank, walk=forge_sph.WALK_THREAD if order_by_id else 0)
         run = slab.SlabRun(dist, rank, world, cfg, pos, vel, be, torch.device("cuda", rank), order_by_id=order_by_id,
                            capacity=cfg.n + 8, comm="nccl", forge_sph=forge_sph, balance=skewed, hist_bins=256,
                            halo_width=halo_width)
@@ -82,13 +85,14 @@ def _sharded_rows(tmp_path, order_by_id, skewed=False, world=2, halo_width=1.0):
     return rows[np.argsort(ids), :6]
 
 
-def _single_gpu_rows(skewed=False):
+def _single_gpu_rows(skewed=False, walk=None):
     cfg = _cfg()
     pos, vel = _skewed(cfg) if skewed else _inputs(cfg)
     p = [torch.from_numpy(x.copy()).cuda() for x in pos]
     v = [torch.from_numpy(x.copy()).cuda() for x in vel]
     rho = torch.empty(cfg.n, dtype=torch.float32, device="cuda")
     g = forge_sph.HashGrid(cfg.cell_size, cfg.dims, (0, 0, 0), cfg.n, 0)
+    g.set_walk(forge_sph.WALK_THREAD if walk is None else walk)
     be = slab.GpuBackend(forge_sph, cfg, 1, 0)
     L = forge_sph.lib()
     for _ in range(STEPS):
@@ -115,7 +119,7 @@ def test_nccl_four_ranks(cuda, tmp_path, order_by_id):
     """Four ranks: the two middle ones exchange with both neighbours. Test
     mode bit for bit; the overlapped production step within fp32 summation
     order (as in the two-rank test)."""
-    got, want = _sharded_rows(tmp_path, order_by_id, world=4), _single_gpu_rows()
+    got, want = _sharded_rows(tmp_path, order_by_id, world=4), _single_gpu_rows(walk=None if order_by_id else 0)
     if order_by_id:
         assert np.array_equal(got, want)
     else:
@@ -130,7 +134,7 @@ def test_nccl_overlapped_step_close_to_single_gpu(cuda, tmp_path, halo_width):
     force on a second stream, local arrays in exchange order): the same
     particles, and trajectories equal up to fp32 summation order (neighbour
     order differs from the single-GPU run): |dx| <= 1e-5, |dv| <= 1e-3."""
-    got, want = _sharded_rows(tmp_path, False, halo_width=halo_width), _single_gpu_rows()
+    got, want = _sharded_rows(tmp_path, False, halo_width=halo_width), _single_gpu_rows(walk=0)
     np.testing.assert_allclose(got[:, :3], want[:, :3], rtol=0, atol=1e-5)
     np.testing.assert_allclose(got[:, 3:], want[:, 3:], rtol=0, atol=1e-3)
 

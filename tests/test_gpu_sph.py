@@ -324,13 +324,14 @@ def test_fused_epilogue_ops_vs_oracle(cuda):
     assert (po[1] == np.float32(0.05)).sum() > 0, "no particle hit the ground plane"
 
 
-def _force_step_run(torch, cfg, pos, vel, n_update, zones):
+def _force_step_run(torch, cfg, pos, vel, n_update, zones, walk=forge_sph.WALK_THREAD):
     """forge_sph_density + forge_sph_force_step (zones None) or the split
     forge_sph_force_step_zone calls (zones = [(mode, inner_lo, inner_hi,
     guard_lo, guard_hi), ...])."""
     L = forge_sph.lib()
     sp, _ = make_step(cfg)
     g = forge_sph.HashGrid(cfg.cell_size, cfg.dims, (0, 0, 0), cfg.n, 0)
+    g.set_walk(walk)
     p, v = [dev(torch, x) for x in pos], [dev(torch, x) for x in vel]
     rho = torch.empty(cfg.n, dtype=torch.float32, device="cuda")
     forge_sph.check(L.forge_sph_density(g.handle, ctypes.byref(gparams(cfg)), *(x.data_ptr() for x in p), cfg.n,
@@ -345,25 +346,34 @@ def _force_step_run(torch, cfg, pos, vel, n_update, zones):
     return g, [host_f32(t) for t in p + v]
 
 
-@pytest.mark.parametrize("name", ["ref65k", "dambreak65k"])
-def test_zoned_force_step_equals_whole_pass(cuda, name):
+@pytest.mark.parametrize("name,walk", [("ref65k", forge_sph.WALK_THREAD), ("dambreak65k", forge_sph.WALK_THREAD),
+                                       ("dambreak65k", forge_sph.WALK_GROUP8)])
+def test_zoned_force_step_equals_whole_pass(cuda, name, walk):
     """Boundary zone then interior zone (the split a sharded step overlaps
-    its exchange with) updates every particle exactly once and equals the
-    single forge_sph_force_step bit for bit, ghosts (i >= n_update) untouched;
-    covers both force kernels (pair and single-particle)."""
+    its exchange with) updates every particle exactly once, ghosts
+    (i >= n_update) untouched. Per-thread walks (pair and single-particle
+    force kernels) equal the single forge_sph_force_step bit for bit; a group
+    walk splits a particle's candidates over lanes by the particles that
+    share its warp, which differ between a zone list and the whole cell
+    order, so it agrees to fp32 rounding."""
     cfg = workloads.config(name)
     pos, vel = workloads.particles(cfg)
     n_upd = cfg.n - 1000
     zones = (0.31, 0.59, 0.25, 0.65)  # interior: x-slices 50..93 (cs/4 = 0.00625 wide) inside [0.31, 0.59)
-    g0, want = _force_step_run(cuda, cfg, pos, vel, n_upd, None)
-    g1, got = _force_step_run(cuda, cfg, pos, vel, n_upd, [(1,) + zones, (2,) + zones])
+    g0, want = _force_step_run(cuda, cfg, pos, vel, n_upd, None, walk)
+    g1, got = _force_step_run(cuda, cfg, pos, vel, n_upd, [(1,) + zones, (2,) + zones], walk)
     g1.check()
     for a, b in zip(got, want):
-        assert np.array_equal(a, b)
+        if walk == forge_sph.WALK_THREAD:
+            assert np.array_equal(a, b)
+        else:
+            np.testing.assert_allclose(a, b, rtol=1e-5, atol=1e-7)
     for a, b in zip(got, pos + vel):
         assert np.array_equal(a[n_upd:], b[n_upd:])
+    if walk != forge_sph.WALK_THREAD:
+        return
     # the boundary pass alone leaves the interior particles as they were
-    _, half = _force_step_run(cuda, cfg, pos, vel, n_upd, [(1,) + zones])
+    _, half = _force_step_run(cuda, cfg, pos, vel, n_upd, [(1,) + zones], walk)
     fx = pos[0] / np.float32(cfg.cell_size)  # the kernels' slice of x: cell * 4 + floor(4 * frac)
     cx = np.clip(np.floor(fx), 0, cfg.dims[0] - 1)
     k = cx * 4 + np.clip(np.floor((fx - cx.astype(np.float32)) * np.float32(4)), 0, 3)
@@ -405,6 +415,7 @@ def test_zoned_prepare_then_late_ghost_densities(cuda):
 
     def run(split):
         g = forge_sph.HashGrid(cfg.cell_size, cfg.dims, (0, 0, 0), cfg.n, 0)
+        g.set_walk(forge_sph.WALK_THREAD)  # bit-for-bit comparison (see the zoned test above)
         p, v = [dev(torch, x) for x in pos], [dev(torch, x) for x in vel]
         rho = torch.empty(cfg.n, dtype=torch.float32, device="cuda")
         forge_sph.check(L.forge_sph_density(g.handle, ctypes.byref(gparams(cfg)), *(x.data_ptr() for x in p), cfg.n,

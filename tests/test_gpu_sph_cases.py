@@ -1,6 +1,7 @@
-"""GPU parity of the neighbour passes against the oracle on sparse,
-lattice, dense, skewed, ragged and out-of-grid inputs and with cell size < h
-(no shared walk of two particles across cells).
+"""GPU parity of every neighbour-pass kernel family (forge_grid_set_walk:
+per-thread walks; warp-cooperative group walks of 4, 8 and 16 particles per
+warp) against the oracle, on sparse, lattice, dense, skewed, ragged and
+out-of-grid inputs and with cell size < h (no shared walk across cells).
 
 Tolerances as in test_gpu_sph.py: density 1e-5 relative; accelerations
 |a_gpu - a_cpu| <= 1e-4 * sum_j |term_j| / rho_i."""
@@ -48,6 +49,8 @@ def _case(name):
 
 
 CASES = ["sparse", "lattice", "dense", "blobs", "ragged", "small_cells"]
+WALKS = {"auto": forge_sph.WALK_AUTO, "thread": forge_sph.WALK_THREAD, "group4": forge_sph.WALK_GROUP4,
+         "group8": forge_sph.WALK_GROUP8, "group16": forge_sph.WALK_GROUP16}
 
 
 def _params(mod, cfg):
@@ -65,8 +68,9 @@ def _oracle(cfg, pos, vel, terms):
     return rho, a, scale
 
 
-def _gpu(torch, cfg, pos, vel, terms):
+def _gpu(torch, cfg, pos, vel, terms, walk=forge_sph.WALK_AUTO):
     g = forge_sph.HashGrid(cfg.cell_size, cfg.dims, (0, 0, 0), cfg.n, 0)
+    g.set_walk(walk)
     d, v = [dev(torch, x) for x in pos], [dev(torch, x) for x in vel]
     rho = torch.empty(cfg.n, dtype=torch.float32, device="cuda")
     L = forge_sph.lib()
@@ -83,28 +87,31 @@ def _gpu(torch, cfg, pos, vel, terms):
 
 
 @pytest.mark.parametrize("case", CASES)
-def test_density_and_force_vs_oracle(cuda, case):
+@pytest.mark.parametrize("walk", list(WALKS))
+def test_density_and_force_vs_oracle(cuda, case, walk):
     cfg, pos, vel = _case(case)
     rho, a, scale = _oracle(cfg, pos, vel, 3)
-    rg, ag = _gpu(cuda, cfg, pos, vel, 3)
+    rg, ag = _gpu(cuda, cfg, pos, vel, 3, WALKS[walk])
     np.testing.assert_allclose(rg, rho, rtol=1e-5, atol=0)
     assert_force_close(ag, a, scale)
 
 
 @pytest.mark.parametrize("terms", [1, 2])
 @pytest.mark.parametrize("case", ["dense", "blobs"])
-def test_single_terms(cuda, terms, case):
+@pytest.mark.parametrize("walk", ["thread", "group8"])
+def test_single_terms(cuda, terms, case, walk):
     cfg, pos, vel = _case(case)
     _, a, scale = _oracle(cfg, pos, vel, terms)
-    _, ag = _gpu(cuda, cfg, pos, vel, terms)
+    _, ag = _gpu(cuda, cfg, pos, vel, terms, WALKS[walk])
     assert_force_close(ag, a, scale)
 
 
 @pytest.mark.parametrize("case", ["lattice", "blobs"])
-def test_passes_are_deterministic(cuda, case):
+@pytest.mark.parametrize("walk", ["thread", "group8"])
+def test_passes_are_deterministic(cuda, case, walk):
     cfg, pos, vel = _case(case)
-    r1, a1 = _gpu(cuda, cfg, pos, vel, 3)
-    r2, a2 = _gpu(cuda, cfg, pos, vel, 3)
+    r1, a1 = _gpu(cuda, cfg, pos, vel, 3, WALKS[walk])
+    r2, a2 = _gpu(cuda, cfg, pos, vel, 3, WALKS[walk])
     assert np.array_equal(r1, r2)
     for x, y in zip(a1, a2):
         assert np.array_equal(x, y)
