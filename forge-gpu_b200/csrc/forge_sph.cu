@@ -107,7 +107,9 @@ struct SortScratch {
 };
 
 int scratch_alloc(SortScratch& s, uint64_t max_n, int device) {
-    s.max_tiles = radix::num_tiles(max_n > 0 ? max_n : 1);
+    const uint64_t m = max_n > 0 ? max_n : 1;
+    s.max_tiles = std::max(radix::num_tiles(m), radix::num_tiles(std::min<uint64_t>(m, radix::kSmallN),
+                                                                 radix::kSmallTile));
     FORGE_CUDA(dalloc(&s.meta, kMetaWords));
     FORGE_CUDA(cudaMemset(s.meta, 0, kMetaWords * sizeof(uint32_t)));
     FORGE_CUDA(dalloc(&s.status, (size_t)s.max_tiles * radix::kRadix));
@@ -131,7 +133,8 @@ int run_onesweep(const SortScratch& s, Src src, const uint32_t* keys0, const uin
                  uint32_t* va, uint32_t* kb, uint32_t* vb, uint32_t n, uint32_t begin_bit, uint32_t end_bit,
                  cudaStream_t st, int* where) {
     const uint32_t passes = (end_bit - begin_bit + radix::kRadixBits - 1) / radix::kRadixBits;
-    const uint32_t tiles = radix::num_tiles(n);
+    const bool small = n <= radix::kSmallN && s.max_tiles >= radix::num_tiles(n, radix::kSmallTile);
+    const uint32_t tiles = small ? radix::num_tiles(n, radix::kSmallTile) : radix::num_tiles(n);
     FORGE_CUDA(cudaMemsetAsync(s.meta, 0, kMetaErr * sizeof(uint32_t), st));
     const uint32_t status_vec4 = (uint32_t)(((size_t)tiles * radix::kRadix + 3) / 4);
     const uint32_t hblocks =
@@ -147,17 +150,27 @@ int run_onesweep(const SortScratch& s, Src src, const uint32_t* keys0, const uin
         uint32_t* vout = (p % 2 == 0) ? va : vb;
         const uint32_t shift = begin_bit + p * radix::kRadixBits;
         const uint32_t bits = std::min((uint32_t)radix::kRadixBits, end_bit - shift);
-        if (p == 0 && vin == nullptr) {
+        const uint32_t skip = p == 0 ? s.skip_tiles : 0u;
+        uint32_t* hist = s.meta + p * radix::kRadix;
+        uint32_t* counter = s.meta + kMetaCounters + p;
+        uint32_t* err = s.meta + kMetaErr;
+        const bool iota = p == 0 && vin == nullptr;
+        if (small && iota)
+            radix::onesweep_pass_kernel<true, radix::kSmallItems><<<tiles, radix::kThreads, 0, st>>>(
+                kin, nullptr, kout, vout, n, shift, bits, hist, s.status, counter, p & 1u, err, skip, s.spin_limit,
+                tiles);
+        else if (small)
+            radix::onesweep_pass_kernel<false, radix::kSmallItems><<<tiles, radix::kThreads, 0, st>>>(
+                kin, vin, kout, vout, n, shift, bits, hist, s.status, counter, p & 1u, err, skip, s.spin_limit,
+                tiles);
+        else if (iota)
             radix::onesweep_pass_kernel<true><<<tiles, radix::kThreads, 0, st>>>(
-                kin, nullptr, kout, vout, n, shift, bits, s.meta + p * radix::kRadix, s.status,
-                s.meta + kMetaCounters + p, p & 1u, s.meta + kMetaErr, p == 0 ? s.skip_tiles : 0u, s.spin_limit,
+                kin, nullptr, kout, vout, n, shift, bits, hist, s.status, counter, p & 1u, err, skip, s.spin_limit,
                 tiles);
-        } else {
+        else
             radix::onesweep_pass_kernel<false><<<tiles, radix::kThreads, 0, st>>>(
-                kin, vin, kout, vout, n, shift, bits, s.meta + p * radix::kRadix, s.status,
-                s.meta + kMetaCounters + p, p & 1u, s.meta + kMetaErr, p == 0 ? s.skip_tiles : 0u, s.spin_limit,
+                kin, vin, kout, vout, n, shift, bits, hist, s.status, counter, p & 1u, err, skip, s.spin_limit,
                 tiles);
-        }
         FORGE_LAUNCHED();
         kin = kout;
         vin = vout;
@@ -646,7 +659,7 @@ sph::Geom geom_of(const forge_grid* g, float h) {
     sph::Geom G{g->geom.ox, g->geom.oy, g->geom.oz, g->geom.cs, g->geom.nxw, g->geom.ny, g->geom.nz,
                 (int)g->sub_bits, g->geom.cs >= h ? 1 : 0};
     G.inv_slice = (float)(1u << g->sub_bits) / g->geom.cs;
-    G.x_off = (float)((uint32_t)g->geom.cx0 << g->sub_bits);
+    G.x_off = (int)((uint32_t)g->geom.cx0 << g->sub_bits);
     G.row_len = make_fastdiv((uint32_t)g->geom.nxw << g->sub_bits);
     G.ny_div = make_fastdiv((uint32_t)g->geom.ny);
     return G;

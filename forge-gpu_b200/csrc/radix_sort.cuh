@@ -43,9 +43,16 @@ constexpr int kHistThreads = 256;
 
 constexpr int kHistItems = 8;
 
-__host__ __device__ constexpr uint32_t num_tiles(uint64_t n) {
-    return (uint32_t)((n + kTile - 1) / kTile);
+__host__ __device__ constexpr uint32_t num_tiles(uint64_t n, uint32_t tile = kTile) {
+    return (uint32_t)((n + tile - 1) / tile);
 }
+
+// Small sorts (at most kSmallN keys) take tiles of kSmallItems keys per
+// thread: four times the CTAs, so a 50,000-key sort still spreads over the
+// GPU instead of running 13 long tiles one after another.
+constexpr int kSmallItems = 4;
+constexpr uint32_t kSmallTile = kThreads * kSmallItems;
+constexpr uint32_t kSmallN = 1u << 20;
 
 // Lanes of the warp holding the same 8-bit digit as this lane, from eight
 // ballots (bit slicing); cheaper than the MATCH instruction on this part.
@@ -153,13 +160,14 @@ __global__ void __launch_bounds__(kHistThreads)
 }
 
 // ---------------------------------------------------------------------------
-// One Onesweep pass. IOTA: the input values are the element indices (first
-// pass of the grid build), vals_in is not read.
+// One Onesweep pass over tiles of kThreads * ITEMS keys. IOTA: the input
+// values are the element indices (first pass of the grid build), vals_in is
+// not read.
 // ---------------------------------------------------------------------------
 #ifndef FORGE_SORT_MIN_BLOCKS
 #define FORGE_SORT_MIN_BLOCKS 5  // 51 registers (spills): 5 CTAs per SM, the shared-memory limit
 #endif
-template <bool IOTA>
+template <bool IOTA, int ITEMS = kItems>
 __global__ void __launch_bounds__(kThreads, FORGE_SORT_MIN_BLOCKS)
     onesweep_pass_kernel(const uint32_t* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
                          uint32_t* __restrict__ keys_out, uint32_t* __restrict__ vals_out,
@@ -172,8 +180,9 @@ __global__ void __launch_bounds__(kThreads, FORGE_SORT_MIN_BLOCKS)
     __shared__ uint32_t s_tile_off[kRadix];       // digit start inside the sorted tile
     __shared__ uint32_t s_base[kRadix];           // global dst = s_base[d] + tile position
     __shared__ uint32_t s_scan[kWarps + 1];
-    __shared__ uint32_t s_exchange[kTile];  // the tile's keys, in sorted order
-    __shared__ uint32_t s_vals[kTile];      // its values: input order (staged), then sorted order
+    constexpr uint32_t TILE = kThreads * ITEMS;
+    __shared__ uint32_t s_exchange[TILE];  // the tile's keys, in sorted order
+    __shared__ uint32_t s_vals[TILE];      // its values: input order (staged), then sorted order
     __shared__ uint32_t s_tile;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -186,18 +195,18 @@ __global__ void __launch_bounds__(kThreads, FORGE_SORT_MIN_BLOCKS)
 
     const uint32_t tile = s_tile;
     if (tile >= ntiles) return;  // (only with tile_base > 0) the whole block
-    const uint32_t tile_start = tile * kTile;
+    const uint32_t tile_start = tile * TILE;
     const uint32_t mask = (1u << bits) - 1u;
-    const uint32_t warp_start = tile_start + warp * 32 * kItems;
+    const uint32_t warp_start = tile_start + warp * 32 * ITEMS;
 
     // Load: warp-striped so each load instruction is 128 contiguous bytes and
     // (item, lane) order equals input order. The values go straight to
     // shared memory (cp.async, no registers held through the ranking); they
     // are needed only once every key has its tile position.
-    uint32_t key[kItems];
-    const uint32_t wbase = (uint32_t)warp * 32u * kItems;  // this warp's first tile slot
+    uint32_t key[ITEMS];
+    const uint32_t wbase = (uint32_t)warp * 32u * ITEMS;  // this warp's first tile slot
 #pragma unroll
-    for (int k = 0; k < kItems; ++k) {
+    for (int k = 0; k < ITEMS; ++k) {
         const uint32_t idx = warp_start + k * 32 + lane;
         const bool ok = idx < n;
         key[k] = ok ? keys_in[idx] : 0u;
@@ -213,7 +222,7 @@ __global__ void __launch_bounds__(kThreads, FORGE_SORT_MIN_BLOCKS)
     // published before the ranking and successors' look-backs do not wait
     // for it.
 #pragma unroll
-    for (int k = 0; k < kItems; ++k) {
+    for (int k = 0; k < ITEMS; ++k) {
         const uint32_t idx = warp_start + k * 32 + lane;
         const bool ok = idx < n;
         const uint32_t d = digit_of(key[k], shift, mask);
@@ -254,9 +263,9 @@ __global__ void __launch_bounds__(kThreads, FORGE_SORT_MIN_BLOCKS)
     // Stable warp-level ranking straight to tile positions: item-major,
     // lane-minor order is the input order.
     const uint32_t lt = lanemask_lt();
-    uint32_t pos[kItems];
+    uint32_t pos[ITEMS];
 #pragma unroll
-    for (int k = 0; k < kItems; ++k) {
+    for (int k = 0; k < ITEMS; ++k) {
         const uint32_t idx = warp_start + k * 32 + lane;
         const bool ok = idx < n;
         const uint32_t d = digit_of(key[k], shift, mask);
@@ -316,26 +325,26 @@ __global__ void __launch_bounds__(kThreads, FORGE_SORT_MIN_BLOCKS)
 
     // Values to their tile positions: read this thread's staged values
     // (input order), then, after a barrier, write them sorted.
-    uint32_t val[kItems];
+    uint32_t val[ITEMS];
     if (IOTA) {
 #pragma unroll
-        for (int k = 0; k < kItems; ++k) val[k] = warp_start + k * 32 + lane;
+        for (int k = 0; k < ITEMS; ++k) val[k] = warp_start + k * 32 + lane;
     } else {
         asm volatile("cp.async.wait_all;" ::: "memory");
         __syncthreads();  // every thread's copies landed
 #pragma unroll
-        for (int k = 0; k < kItems; ++k) val[k] = s_vals[wbase + k * 32 + lane];
+        for (int k = 0; k < ITEMS; ++k) val[k] = s_vals[wbase + k * 32 + lane];
     }
     __syncthreads();
 #pragma unroll
-    for (int k = 0; k < kItems; ++k)
+    for (int k = 0; k < ITEMS; ++k)
         if (pos[k] != 0xffffffffu) s_vals[pos[k]] = val[k];
     __syncthreads();
 
     // Coalesced scatter of the sorted tile: runs of one digit are contiguous.
-    const uint32_t tile_n = min((uint32_t)kTile, n - tile_start);
+    const uint32_t tile_n = min((uint32_t)TILE, n - tile_start);
 #pragma unroll
-    for (int k = 0; k < kItems; ++k) {
+    for (int k = 0; k < ITEMS; ++k) {
         const uint32_t j = tid + k * kThreads;
         if (j < tile_n) {
             const uint32_t kk = s_exchange[j];

@@ -56,7 +56,7 @@ struct Geom {
     int sub_bits;   // x-slices per cell = 2^sub_bits (keys are cell << sub_bits | slice)
     int pairable;   // cs >= h: a walk over a same-row neighbour's window adds only r >= h pairs
     float inv_slice;   // 2^sub_bits / cs (rounded: window bounds carry a margin for it)
-    float x_off;       // first slice of the grid's x-window: cx0 << sub_bits (nx is the window's width)
+    int x_off;         // first slice of the grid's x-window: cx0 << sub_bits (nx is the window's width)
     FastDiv row_len;   // nx << sub_bits: key -> (row, slice in row)
     FastDiv ny_div;    // ny: row -> (cy, cz)
 };
@@ -74,7 +74,8 @@ struct Frame {
     int cy, cz;
     int fx_lo, fx_hi;   // x-slice range of the reference window: cells cx-1..cx+1, clamped to the grid
     int f_own;          // own x-slice index in the row
-    float fxs;          // (x - ox) / cs * 2^sub_bits   (slice coordinate)
+    float fxs;          // (x - ox) / cs * 2^sub_bits   (global slice coordinate: windows round
+                        // the same whatever the grid's x-window)
     float slack;        // slice-units rounding slack
     float gyl, gyr, gzl, gzr;  // squared gaps to the neighbouring rows
 };
@@ -91,7 +92,7 @@ __device__ __forceinline__ Frame make_frame(const float4& p, const Geom& g) {
     const int cx = f.f_own >> g.sub_bits;
     f.fx_lo = max(cx - 1, 0) * (int)S;
     f.fx_hi = (min(cx + 1, g.nx - 1) + 1) * (int)S - 1;
-    f.fxs = (p.x - g.ox) * g.inv_slice - g.x_off;
+    f.fxs = (p.x - g.ox) * g.inv_slice;
     // rounding of the cell assignment and of r^2, plus 1e-3 slices for the
     // rounded reciprocal and the approximate square root of row_window
     f.slack = 4e-7f * (fabsf(f.fxs) + 2.f * (float)S) + 1e-3f;
@@ -117,8 +118,8 @@ __device__ __forceinline__ bool row_window(const Frame& f, int r, const Geom& g,
     const float base = (dz < 0 ? f.gzl : (dz > 0 ? f.gzr : 0.f)) + (dy < 0 ? f.gyl : (dy > 0 ? f.gyr : 0.f));
     if (base > H) return false;
     const float w = sqrt_approx(H - base) * g.inv_slice + f.slack;
-    lo = max(min(floor_to_int_dev(f.fxs - w), f.f_own), f.fx_lo);
-    hi = min(max(floor_to_int_dev(f.fxs + w), f.f_own), f.fx_hi);
+    lo = max(min(floor_to_int_dev(f.fxs - w) - g.x_off, f.f_own), f.fx_lo);
+    hi = min(max(floor_to_int_dev(f.fxs + w) - g.x_off, f.f_own), f.fx_hi);
     return true;
 }
 
