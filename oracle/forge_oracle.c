@@ -301,10 +301,11 @@ static inline void sph_cell(float x, float y, float z, float cs, uint32_t nx, ui
     *cz = c;
 }
 
-/* sph_density.rs:401-461. */
-void orc_density(const orc_sph_params* p, const float* px, const float* py, const float* pz, uint64_t n, float cs,
-                 uint32_t nx, uint32_t ny, uint32_t nz, const uint32_t* cell_start, const uint32_t* sorted_idx,
-                 float* density, int threads) {
+/* sph_density.rs:401-461, for particles idx[0..count) (all n when idx is
+ * NULL); out[k] is the density of particle idx[k]. */
+static void density_of(const orc_sph_params* p, const float* px, const float* py, const float* pz, float cs,
+                       uint32_t nx, uint32_t ny, uint32_t nz, const uint32_t* cell_start, const uint32_t* sorted_idx,
+                       const uint32_t* idx, uint64_t count, float* density, int threads) {
     const float h = p->h, mass = p->mass;
     const float h2 = h * h;
     const float h9 = h2 * h2 * h2 * h2 * h;
@@ -312,8 +313,8 @@ void orc_density(const orc_sph_params* p, const float* px, const float* py, cons
 #ifdef _OPENMP
 #pragma omp parallel for schedule(dynamic, 256) num_threads(threads > 0 ? threads : 1)
 #endif
-    for (int64_t ii = 0; ii < (int64_t)n; ++ii) {
-        const uint64_t i = (uint64_t)ii;
+    for (int64_t kk = 0; kk < (int64_t)count; ++kk) {
+        const uint64_t i = idx ? idx[kk] : (uint64_t)kk;
         const float xi = px[i], yi = py[i], zi = pz[i];
         float rho = 0.0f;
         int cx, cy, cz;
@@ -340,18 +341,30 @@ void orc_density(const orc_sph_params* p, const float* px, const float* py, cons
                 }
             }
         }
-        density[i] = rho;
+        density[kk] = rho;
     }
     (void)threads;
 }
 
+void orc_density(const orc_sph_params* p, const float* px, const float* py, const float* pz, uint64_t n, float cs,
+                 uint32_t nx, uint32_t ny, uint32_t nz, const uint32_t* cell_start, const uint32_t* sorted_idx,
+                 float* density, int threads) {
+    density_of(p, px, py, pz, cs, nx, ny, nz, cell_start, sorted_idx, NULL, n, density, threads);
+}
+
+void orc_density_at(const orc_sph_params* p, const float* px, const float* py, const float* pz, float cs,
+                    uint32_t nx, uint32_t ny, uint32_t nz, const uint32_t* cell_start, const uint32_t* sorted_idx,
+                    const uint32_t* idx, uint64_t m, float* density, int threads) {
+    density_of(p, px, py, pz, cs, nx, ny, nz, cell_start, sorted_idx, idx, m, density, threads);
+}
+
 /* Fused pressure + viscosity, sph_fused.rs:542-638 (terms per
  * sph_pressure.rs:28-112 / sph_viscosity.rs:27-106), Jacobi velocities. */
-void orc_force(const orc_sph_params* p, uint32_t terms, const float* px, const float* py, const float* pz,
-               const float* vx, const float* vy, const float* vz, const float* density, uint64_t n, float cs,
-               uint32_t nx, uint32_t ny, uint32_t nz, const uint32_t* cell_start, const uint32_t* sorted_idx,
-               float dt, float* vx_out, float* vy_out, float* vz_out, float* ax_out, float* ay_out, float* az_out,
-               int threads) {
+static void force_of(const orc_sph_params* p, uint32_t terms, const float* px, const float* py, const float* pz,
+                     const float* vx, const float* vy, const float* vz, const float* density, float cs, uint32_t nx,
+                     uint32_t ny, uint32_t nz, const uint32_t* cell_start, const uint32_t* sorted_idx,
+                     const uint32_t* idx, uint64_t count, float dt, float* vx_out, float* vy_out, float* vz_out,
+                     float* ax_out, float* ay_out, float* az_out, int threads) {
     const float h = p->h, mass = p->mass, gas_constant = p->gas_constant, rest_density = p->rest_density,
                 visc_coeff = p->viscosity;
     const float h2 = h * h;
@@ -361,8 +374,8 @@ void orc_force(const orc_sph_params* p, uint32_t terms, const float* px, const f
 #ifdef _OPENMP
 #pragma omp parallel for schedule(dynamic, 256) num_threads(threads > 0 ? threads : 1)
 #endif
-    for (int64_t ii = 0; ii < (int64_t)n; ++ii) {
-        const uint64_t i = (uint64_t)ii;
+    for (int64_t kk = 0; kk < (int64_t)count; ++kk) {
+        const uint64_t i = idx ? idx[kk] : (uint64_t)kk;
         const float xi = px[i], yi = py[i], zi = pz[i];
         const float vxi = vx[i], vyi = vy[i], vzi = vz[i];
         const float rho_i = density[i];
@@ -442,16 +455,36 @@ void orc_force(const orc_sph_params* p, uint32_t terms, const float* px, const f
                 az = vaz / rho_i;
             }
         }
-        vx_out[i] = valid ? vxi + ax * dt : vxi;
-        vy_out[i] = valid ? vyi + ay * dt : vyi;
-        vz_out[i] = valid ? vzi + az * dt : vzi;
+        vx_out[kk] = valid ? vxi + ax * dt : vxi;
+        vy_out[kk] = valid ? vyi + ay * dt : vyi;
+        vz_out[kk] = valid ? vzi + az * dt : vzi;
         if (ax_out) {
-            ax_out[i] = ax;
-            ay_out[i] = ay;
-            az_out[i] = az;
+            ax_out[kk] = ax;
+            ay_out[kk] = ay;
+            az_out[kk] = az;
         }
     }
     (void)threads;
+}
+
+void orc_force(const orc_sph_params* p, uint32_t terms, const float* px, const float* py, const float* pz,
+               const float* vx, const float* vy, const float* vz, const float* density, uint64_t n, float cs,
+               uint32_t nx, uint32_t ny, uint32_t nz, const uint32_t* cell_start, const uint32_t* sorted_idx,
+               float dt, float* vx_out, float* vy_out, float* vz_out, float* ax_out, float* ay_out, float* az_out,
+               int threads) {
+    force_of(p, terms, px, py, pz, vx, vy, vz, density, cs, nx, ny, nz, cell_start, sorted_idx, NULL, n, dt, vx_out,
+             vy_out, vz_out, ax_out, ay_out, az_out, threads);
+}
+
+/* The force of particles idx[0..m) only (outputs indexed by k), against
+ * all particles as neighbours: sampled checks of large configs. */
+void orc_force_at(const orc_sph_params* p, uint32_t terms, const float* px, const float* py, const float* pz,
+                  const float* vx, const float* vy, const float* vz, const float* density, float cs, uint32_t nx,
+                  uint32_t ny, uint32_t nz, const uint32_t* cell_start, const uint32_t* sorted_idx,
+                  const uint32_t* idx, uint64_t m, float dt, float* vx_out, float* vy_out, float* vz_out,
+                  float* ax_out, float* ay_out, float* az_out, int threads) {
+    force_of(p, terms, px, py, pz, vx, vy, vz, density, cs, nx, ny, nz, cell_start, sorted_idx, idx, m, dt, vx_out,
+             vy_out, vz_out, ax_out, ay_out, az_out, threads);
 }
 
 /* One per-particle module after the SPH module:

@@ -93,6 +93,16 @@ void orc_density(const orc_sph_params* p, const float* px, const float* py, cons
  * velocities: reads v_in, writes v_out and accel (nullable). terms | 4
  * accumulates |term| instead of term (the per-particle magnitude scale the
  * force tolerance is stated against). */
+/* density / force of the particles idx[0..m) only, against all n as
+ * neighbours (outputs indexed 0..m): sampled checks of large configs */
+void orc_density_at(const orc_sph_params* p, const float* px, const float* py, const float* pz, float cs,
+                    uint32_t nx, uint32_t ny, uint32_t nz, const uint32_t* cell_start, const uint32_t* sorted_idx,
+                    const uint32_t* idx, uint64_t m, float* density, int threads);
+void orc_force_at(const orc_sph_params* p, uint32_t terms, const float* px, const float* py, const float* pz,
+                  const float* vx, const float* vy, const float* vz, const float* density, float cs, uint32_t nx,
+                  uint32_t ny, uint32_t nz, const uint32_t* cell_start, const uint32_t* sorted_idx,
+                  const uint32_t* idx, uint64_t m, float dt, float* vx_out, float* vy_out, float* vz_out,
+                  float* ax_out, float* ay_out, float* az_out, int threads);
 void orc_force(const orc_sph_params* p, uint32_t terms, const float* px, const float* py, const float* pz,
                const float* vx, const float* vy, const float* vz, const float* density, uint64_t n,
                float cs, uint32_t nx, uint32_t ny, uint32_t nz, const uint32_t* cell_start,

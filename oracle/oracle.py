@@ -65,6 +65,10 @@ def lib():
                                 _u, _u, f32, _f, _f, _f, vp, vp, vp, i32]
         L.orc_step.argtypes = [ctypes.POINTER(SphParams), ctypes.POINTER(StepParams), _f, _f, _f, _f, _f, _f, vp,
                                u64, f32, u32, u32, u32, _u, i32]
+        L.orc_density_at.argtypes = [ctypes.POINTER(SphParams), _f, _f, _f, f32, u32, u32, u32, _u, _u, _u, u64,
+                                     _f, i32]
+        L.orc_force_at.argtypes = [ctypes.POINTER(SphParams), u32, _f, _f, _f, _f, _f, _f, _f, f32, u32, u32, u32,
+                                   _u, _u, _u, u64, f32, _f, _f, _f, vp, vp, vp, i32]
         L.orc_apply_ops.argtypes = [ctypes.POINTER(StepParams), _f, _f, _f, _f, _f, _f, u64]
         L.orc_max_threads.restype = i32
         _lib = L
@@ -181,6 +185,27 @@ def force(p: SphParams, terms, px, py, pz, vx, vy, vz, rho, cs, dims, cell_start
     ac = [np.empty(n, np.float32) for _ in range(3)]
     lib().orc_force(ctypes.byref(p), terms, px, py, pz, vx, vy, vz, rho, n, cs, *dims, cell_start, sorted_idx, dt,
                     *vo, *(a.ctypes.data for a in ac), threads)
+    return vo, ac
+
+
+def density_at(p: SphParams, px, py, pz, cs, dims, cell_start, sorted_idx, idx, threads=1):
+    """Densities of particles idx only (all particles as neighbours)."""
+    idx = np.ascontiguousarray(idx, np.uint32)
+    out = np.empty(idx.size, np.float32)
+    lib().orc_density_at(ctypes.byref(p), px, py, pz, cs, *dims, cell_start, sorted_idx, idx, idx.size, out,
+                         threads)
+    return out
+
+
+def force_at(p: SphParams, terms, px, py, pz, vx, vy, vz, rho, cs, dims, cell_start, sorted_idx, idx, dt,
+             threads=1):
+    """(velocities, accelerations) of particles idx only."""
+    idx = np.ascontiguousarray(idx, np.uint32)
+    m = idx.size
+    vo = [np.empty(m, np.float32) for _ in range(3)]
+    ac = [np.empty(m, np.float32) for _ in range(3)]
+    lib().orc_force_at(ctypes.byref(p), terms, px, py, pz, vx, vy, vz, rho, cs, *dims, cell_start, sorted_idx, idx,
+                       m, dt, *vo, *(a.ctypes.data for a in ac), threads)
     return vo, ac
 
 

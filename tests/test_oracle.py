@@ -171,3 +171,21 @@ def test_force_matches_brute_force_fp64():
     scale = ((np.abs(fp)[:, :, None] * np.abs(d)).sum(1) + (np.abs(fv)[:, :, None] * np.abs(dv)).sum(1)) / R[:, None]
     got = np.stack(acc, 1).astype(np.float64)
     assert (np.abs(got - a_ref) <= 1e-4 * scale + 1e-30).all(), np.max(np.abs(got - a_ref) / (scale + 1e-30))
+
+
+def test_sampled_density_and_force_equal_the_full_passes():
+    """orc_density_at / orc_force_at (the sampled checks of the full-size
+    configs) give, bit for bit, the full passes' values of the sampled
+    particles."""
+    import workloads
+    cfg = workloads.small("ref65k", 6000, (12, 12, 12))
+    pos, vel = workloads.uniform_particles(cfg.n, seed=12)
+    ci, si, cst = oracle.grid_build(*pos, cfg.cell_size, cfg.dims)
+    p = oracle.SphParams(cfg.h, cfg.mass, cfg.gas_constant, cfg.rest_density, cfg.viscosity)
+    rho = oracle.density(p, *pos, cfg.cell_size, cfg.dims, cst, si)
+    idx = np.random.default_rng(3).choice(cfg.n, 700, replace=False).astype(np.uint32)
+    assert np.array_equal(oracle.density_at(p, *pos, cfg.cell_size, cfg.dims, cst, si, idx), rho[idx])
+    vo, a = oracle.force(p, 3, *pos, *vel, rho, cfg.cell_size, cfg.dims, cst, si, 1e-4)
+    vs, as_ = oracle.force_at(p, 3, *pos, *vel, rho, cfg.cell_size, cfg.dims, cst, si, idx, 1e-4)
+    for k in range(3):
+        assert np.array_equal(vs[k], vo[k][idx]) and np.array_equal(as_[k], a[k][idx])
