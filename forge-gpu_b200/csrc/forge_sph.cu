@@ -1128,8 +1128,10 @@ extern "C" int forge_grid_profile_read(forge_grid* g, float* out, uint32_t cap_s
 // ===========================================================================
 struct forge_slab {
     int device = 0;
+    int sms = 148;
     uint64_t max_n = 0;
     uint32_t* tile_counts = nullptr;
+    uint32_t* hist_acc = nullptr;  // 2 x kHistMaxBins words: 64-bit fixed-point bins of forge_slab_x_hist
 };
 
 extern "C" int forge_slab_create(uint64_t max_n, int device, forge_slab** out) {
@@ -1140,8 +1142,11 @@ extern "C" int forge_slab_create(uint64_t max_n, int device, forge_slab** out) {
     forge_slab* h = new forge_slab;
     h->device = device;
     h->max_n = max_n;
+    h->sms = num_sms(device);
     const size_t tiles = (max_n + slab::kTile - 1) / slab::kTile + 1;
-    if (dalloc(&h->tile_counts, tiles * slab::kLists) != cudaSuccess) {
+    if (dalloc(&h->tile_counts, tiles * slab::kLists) != cudaSuccess ||
+        dalloc(&h->hist_acc, 2 * (size_t)slab::kHistMaxBins) != cudaSuccess) {
+        cudaFree(h->tile_counts);
         delete h;
         return set_error(FORGE_ERR_CUDA, "forge_slab_create: cudaMalloc failed");
     }
@@ -1153,6 +1158,7 @@ extern "C" void forge_slab_destroy(forge_slab* h) {
     if (!h) return;
     DeviceScope scope(h->device);
     cudaFree(h->tile_counts);
+    cudaFree(h->hist_acc);
     delete h;
 }
 
@@ -1177,6 +1183,25 @@ extern "C" int forge_slab_classify(forge_slab* h, const float* x, uint64_t n, fl
     slab::classify_write_kernel<<<tiles, slab::kThreads, 0, st>>>(slab::XMember{x, a}, (uint32_t)n,
                                                                   nullptr, h->tile_counts,
                                                                   counts, idx_out);
+    FORGE_LAUNCHED();
+    return FORGE_OK;
+}
+
+extern "C" int forge_slab_x_hist(forge_slab* h, const float* x, const float* w, uint64_t n, float lo, float hi,
+                                 uint32_t bins, double* out, void* stream) {
+    if (!h || !out || (n && !x)) return set_error(FORGE_ERR_INVALID_ARG, "forge_slab_x_hist: NULL argument");
+    if (bins == 0 || bins > slab::kHistMaxBins || !(lo < hi) || n >= 0xffffffffull)
+        return set_error(FORGE_ERR_INVALID_ARG, "forge_slab_x_hist: bins in [1, %u], lo < hi", slab::kHistMaxBins);
+    FORGE_DEVICE_SCOPE(h->device);
+    cudaStream_t st = as_stream(stream);
+    unsigned long long* acc = reinterpret_cast<unsigned long long*>(h->hist_acc);
+    FORGE_CUDA(cudaMemsetAsync(acc, 0, bins * sizeof(unsigned long long), st));
+    if (n) {
+        const uint32_t blocks = std::min(grid_blocks(n, 256), (uint32_t)h->sms * 2u);
+        slab::x_hist_kernel<<<blocks, 256, 0, st>>>(x, w, (uint32_t)n, (double)lo,
+                                                    (double)bins / ((double)hi - (double)lo), bins, acc);
+    }
+    slab::x_hist_finish_kernel<<<grid_blocks(bins, 256), 256, 0, st>>>(acc, bins, out);
     FORGE_LAUNCHED();
     return FORGE_OK;
 }

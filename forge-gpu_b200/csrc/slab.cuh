@@ -160,6 +160,36 @@ __global__ void __launch_bounds__(1024)
 namespace forge {
 namespace slab {
 
+// x-histogram for load balancing: out[b] += weight of each particle whose x
+// falls in bin b of [lo, hi) (clamped to the end bins; weight 1 when w is
+// NULL). Weights are summed as fixed point (2^-16 units) in 64-bit
+// integers, so the result does not depend on the order of the atomics and
+// every rank computes the same bounds from the same all-reduced histogram.
+constexpr uint32_t kHistMaxBins = 4096;
+constexpr double kHistScale = 65536.0;
+
+__global__ void __launch_bounds__(256)
+    x_hist_kernel(const float* __restrict__ x, const float* __restrict__ w, uint32_t n, double lo, double scale,
+                  uint32_t bins, unsigned long long* __restrict__ acc) {
+    __shared__ unsigned long long s[kHistMaxBins];
+    for (uint32_t b = threadIdx.x; b < bins; b += blockDim.x) s[b] = 0ull;
+    __syncthreads();
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const double f = floor(((double)x[i] - lo) * scale);
+        const uint32_t b = f < 0.0 ? 0u : (f >= (double)(bins - 1) ? bins - 1 : (uint32_t)f);
+        const unsigned long long q = w ? (unsigned long long)((double)fmaxf(w[i], 0.f) * kHistScale + 0.5) : 65536ull;
+        atomicAdd(&s[b], q);
+    }
+    __syncthreads();
+    for (uint32_t b = threadIdx.x; b < bins; b += blockDim.x)
+        if (s[b]) atomicAdd(&acc[b], s[b]);
+}
+
+__global__ void x_hist_finish_kernel(const unsigned long long* __restrict__ acc, uint32_t bins, double* __restrict__ out) {
+    for (uint32_t b = blockIdx.x * blockDim.x + threadIdx.x; b < bins; b += gridDim.x * blockDim.x)
+        out[b] = (double)acc[b] / kHistScale;
+}
+
 }  // namespace slab
 }  // namespace forge
 

@@ -73,7 +73,7 @@ EXPORTED = (
     "forge_io_download_vec3",
     "forge_sort_pairs_static",
     "forge_sph_force_step",
-    "forge_slab_create", "forge_slab_destroy", "forge_slab_classify", "forge_slab_compact",
+    "forge_slab_create", "forge_slab_destroy", "forge_slab_classify", "forge_slab_compact", "forge_slab_x_hist",
     "forge_nccl_unique_id", "forge_slab_comm_create", "forge_slab_comm_destroy", "forge_slab_exchange",
     "forge_apply_ops", "forge_slab_exchange_rho", "forge_slab_comm_set_bounds", "forge_slab_comm_set_timeout", "forge_sph_force_step_zone", "forge_slab_exchange_begin", "forge_slab_exchange_end",
 )
@@ -165,6 +165,7 @@ def lib() -> ctypes.CDLL:
         "forge_slab_destroy": (None, [vp]),
         "forge_slab_classify": (i32, [vp, vp, u64, f32, f32, f32, u32, vp, vp, vp]),
         "forge_slab_compact": (i32, [vp, u64, u32, u64, vp, u64, vp]),
+        "forge_slab_x_hist": (i32, [vp, vp, vp, u64, f32, f32, u32, vp, vp]),
         "forge_sph_force_step": (i32, [vp, ctypes.POINTER(SphParams), ctypes.POINTER(StepParams), vp, vp, vp, vp,
                                        vp, vp, vp, u64, u64, vp]),
         "forge_sph_force_step_zone": (i32, [vp, ctypes.POINTER(SphParams), ctypes.POINTER(StepParams), vp, vp, vp,

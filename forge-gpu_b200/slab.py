@@ -274,10 +274,10 @@ class SlabRun:
                              f"halo width {self.reach / self.cfg.h:.3g} h): use fewer ranks or halo_width 1")
 
     def _x_hist(self, x: torch.Tensor, w: torch.Tensor | None) -> torch.Tensor:
+        """hist_bins-bin histogram of x over x_range (weights w, or counts),
+        computed by the backend (forge_slab_x_hist on GPU ranks)."""
         lo, hi = self.x_range
-        nb = self.hist_bins
-        idx = ((x.double() - lo) * (nb / (hi - lo))).floor().clamp_(0, nb - 1).long()
-        return torch.bincount(idx, weights=None if w is None else w.double(), minlength=nb).double()
+        return self.backend.x_hist(x, w, lo, hi, self.hist_bins)
 
     def _note_work(self, x: torch.Tensor, rho: torch.Tensor) -> None:
         """Work histogram of the owned particles at density time (balancing
@@ -488,6 +488,13 @@ class GpuBackend:
         a, l, r = self.counts.tolist()
         flat = self.idx[:a + l + r].long()
         return flat[:a], flat[a:a + l], flat[a + l:]
+
+    def x_hist(self, x, w, lo, hi, bins):
+        """forge_slab_x_hist: fixed-point, order-independent x-histogram."""
+        out = torch.empty(bins, dtype=torch.float64, device=x.device)
+        self.f.check(self.L.forge_slab_x_hist(self.slab, x.data_ptr(), None if w is None else w.data_ptr(),
+                                              x.numel(), lo, hi, bins, out.data_ptr(), self._st()))
+        return out
 
     def compact(self, cols, n, gone):
         if gone.numel() == 0:

@@ -376,6 +376,15 @@ FORGE_API void forge_slab_destroy(forge_slab* h);
 FORGE_API int forge_slab_classify(forge_slab* h, const float* x, uint64_t n, float lo, float hi, float reach,
                                   uint32_t flags, uint32_t* idx_out, uint32_t* counts, void* stream);
 
+/* x-histogram of n particles for load balancing (no reference
+ * counterpart): out[b] (bins doubles, device) = sum of w[i] (1 when w is
+ * NULL; negative weights count 0) over the particles whose x lies in bin b
+ * of [lo, hi), x below/above in the end bins. Summed in 2^-16 fixed point
+ * with 64-bit integer atomics: the same inputs give the same histogram
+ * bit for bit. bins <= 4096. */
+FORGE_API int forge_slab_x_hist(forge_slab* h, const float* x, const float* w, uint64_t n, float lo, float hi,
+                                uint32_t bins, double* out, void* stream);
+
 /* Remove the k columns gone[] (ascending, < n) from a row-major rows x ld
  * float buffer holding n live columns: surviving columns among the last k
  * move into the holes, so the live columns become [0, n - k). */

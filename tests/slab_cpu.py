@@ -247,3 +247,9 @@ def torch_compact(cols, n, gone):
     tail = torch.arange(keep, n, device=cols.device)
     fillers = tail[~torch.isin(tail, gone)]
     cols[:, gone[:fillers.numel()]] = cols[:, fillers]
+
+
+def torch_x_hist(x, w, lo, hi, bins):
+    """forge_slab_x_hist with torch ops (CPU ranks in tests)."""
+    idx = ((x.double() - lo) * (bins / (hi - lo))).floor().clamp_(0, bins - 1).long()
+    return torch.bincount(idx, weights=None if w is None else w.double().clamp(min=0), minlength=bins).double()

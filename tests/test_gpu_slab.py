@@ -106,3 +106,21 @@ def test_slab_classify_and_compact_match_torch(cuda, n):
     slab_cpu.torch_compact(ref, n, mig)
     keep = n - mig.numel()
     assert torch_.equal(cols[:, :keep], ref[:, :keep])
+
+
+@pytest.mark.parametrize("n", [0, 1, 1000, 300_001])
+def test_x_hist_matches_torch_and_is_deterministic(cuda, n):
+    """forge_slab_x_hist (the load-balancing histogram): counts equal the
+    torch restatement exactly; density weights within the 2^-16 fixed-point
+    quantisation; two runs give the same bits."""
+    g = cuda.Generator().manual_seed(n + 1)
+    x = (cuda.rand(n, generator=g) * 1.4 - 0.2).cuda()
+    w = (cuda.rand(n, generator=g) * 2000.0).cuda()
+    be = slab.GpuBackend(forge_sph, _cfg(), max(n, 1), 0)
+    c = be.x_hist(x, None, 0.0, 1.0, 256)
+    assert cuda.equal(c.cpu(), slab_cpu.torch_x_hist(x.cpu(), None, 0.0, 1.0, 256))
+    h1 = be.x_hist(x, w, 0.0, 1.0, 4096)
+    h2 = be.x_hist(x, w, 0.0, 1.0, 4096)
+    assert cuda.equal(h1, h2)
+    want = slab_cpu.torch_x_hist(x.cpu(), w.cpu(), 0.0, 1.0, 4096)
+    assert cuda.allclose(h1.cpu(), want, rtol=1e-6, atol=1e-3)

@@ -41,6 +41,7 @@ class OracleBackend:
 
     classify = staticmethod(slab_cpu.torch_classify)
     compact = staticmethod(slab_cpu.torch_compact)
+    x_hist = staticmethod(slab_cpu.torch_x_hist)
 
     def density(self, pos, n):
         c = self.cfg
