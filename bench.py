@@ -110,7 +110,7 @@ class Clocks:
 
 
 PHASES = ("sort", "cells_gather", "density", "force")
-WALKS = {"auto": 0, "thread": 1, "group4": 2, "group8": 3, "group16": 4}  # forge_grid_set_walk
+WALKS = {"auto": 0, "thread": 1, "group4": 2, "group8": 3, "group16": 4, "rows": 5}  # forge_grid_set_walk
 WALK = 0
 
 
@@ -632,7 +632,7 @@ def main():
                     choices=["sharded16m", "dambreak1m", "dambreak1m_h025", "dambreak65k", "blobs4m", "ref65k"])
     ap.add_argument("--no-extra", action="store_true", help="skip the 1M dam-break and 2^28 sort extras")
     ap.add_argument("--walk", choices=list(WALKS), default="auto",
-                    help="neighbour-pass kernel family (auto: group walks below 2^18 particles)")
+                    help="neighbour-pass kernel family (auto: row walks below 2^18 particles)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
     ap.add_argument("--sort-only", type=int, default=None, metavar="LOG2N",
                     help="time only the standalone key/value sort of 2^LOG2N uniform pairs (for profiling)")

@@ -8,6 +8,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include "forge_sph.h"
@@ -16,6 +17,7 @@
 #include "radix_sort.cuh"
 #include "sph.cuh"
 #include "sph_group.cuh"
+#include "sph_rows.cuh"
 #include "slab.cuh"
 
 using namespace forge;
@@ -78,6 +80,25 @@ cudaError_t dalloc(T** p, size_t count) {
 
 uint32_t grid_blocks(uint64_t work, uint32_t threads) { return (uint32_t)((work + threads - 1) / threads); }
 
+// Launches a kernel of a step chain with programmatic dependent launch: its
+// launch overlaps the previous kernel's drain, and its CTAs wait in
+// pdl_enter() (common.cuh) until that kernel has completed. Errors
+// surface through cudaGetLastError like a <<<>>> launch.
+template <typename... KArgs, typename... Args>
+void launch_pdl(void (*kernel)(KArgs...), uint32_t grid, uint32_t block, cudaStream_t st, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 int num_sms(int device) {
     int v = 148;
     cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device);
@@ -139,7 +160,7 @@ int run_onesweep(const SortScratch& s, Src src, const uint32_t* keys0, const uin
     const uint32_t status_vec4 = (uint32_t)(((size_t)tiles * radix::kRadix + 3) / 4);
     const uint32_t hblocks =
         std::max(1u, std::min(grid_blocks(n, radix::kHistThreads * radix::kHistItems), (uint32_t)s.sms * 8u));
-    radix::digit_histogram_kernel<Src><<<hblocks, radix::kHistThreads, 0, st>>>(
+    launch_pdl(radix::digit_histogram_kernel<Src>, hblocks, radix::kHistThreads, st,
         src, n, begin_bit, end_bit, passes, s.meta, reinterpret_cast<uint4*>(s.status), status_vec4);
     FORGE_LAUNCHED();
     const uint32_t* kin = keys0;
@@ -156,19 +177,19 @@ int run_onesweep(const SortScratch& s, Src src, const uint32_t* keys0, const uin
         uint32_t* err = s.meta + kMetaErr;
         const bool iota = p == 0 && vin == nullptr;
         if (small && iota)
-            radix::onesweep_pass_kernel<true, radix::kSmallItems><<<tiles, radix::kThreads, 0, st>>>(
+            launch_pdl(radix::onesweep_pass_kernel<true, radix::kSmallItems>, tiles, radix::kThreads, st,
                 kin, nullptr, kout, vout, n, shift, bits, hist, s.status, counter, p & 1u, err, skip, s.spin_limit,
                 tiles);
         else if (small)
-            radix::onesweep_pass_kernel<false, radix::kSmallItems><<<tiles, radix::kThreads, 0, st>>>(
+            launch_pdl(radix::onesweep_pass_kernel<false, radix::kSmallItems>, tiles, radix::kThreads, st,
                 kin, vin, kout, vout, n, shift, bits, hist, s.status, counter, p & 1u, err, skip, s.spin_limit,
                 tiles);
         else if (iota)
-            radix::onesweep_pass_kernel<true><<<tiles, radix::kThreads, 0, st>>>(
+            launch_pdl(radix::onesweep_pass_kernel<true>, tiles, radix::kThreads, st,
                 kin, nullptr, kout, vout, n, shift, bits, hist, s.status, counter, p & 1u, err, skip, s.spin_limit,
                 tiles);
         else
-            radix::onesweep_pass_kernel<false><<<tiles, radix::kThreads, 0, st>>>(
+            launch_pdl(radix::onesweep_pass_kernel<false>, tiles, radix::kThreads, st,
                 kin, vin, kout, vout, n, shift, bits, hist, s.status, counter, p & 1u, err, skip, s.spin_limit,
                 tiles);
         FORGE_LAUNCHED();
@@ -606,12 +627,12 @@ int grid_build_impl(forge_grid* g, const float* px, const float* py, const float
     prof_mark(g, 1, st);
     grid::GatherSrc gs{px, py, pz, stride, vx, vy, vz};
     const uint32_t table = cells_w(g) << sub_bits;  // entries [0, table]
-    grid::cell_start_gather_kernel<<<grid_blocks(n + 1, 256), 256, 0, st>>>(
+    launch_pdl(grid::cell_start_gather_kernel, grid_blocks(n + 1, 256), 256, st,
         g->sorted_keys, g->sorted_idx, nn, table, g->cell_start, gs, gather_pos ? g->pos4 : nullptr,
         (gather_pos && vx) ? g->vel4 : nullptr, g->chunk_val);
     const uint32_t chunks = table / grid::kFillChunk;  // whole chunks below entry `table`
     if (chunks)
-        grid::fill_chunks_kernel<<<std::min(chunks, (uint32_t)g->scratch.sms * 8u), 256, 0, st>>>(g->cell_start,
+        launch_pdl(grid::fill_chunks_kernel, std::min(chunks, (uint32_t)g->scratch.sms * 8u), 256, st, g->cell_start,
                                                                                                 g->chunk_val, chunks);
     FORGE_LAUNCHED();
     prof_mark(g, 2, st);
@@ -674,21 +695,27 @@ constexpr double kPairMaxOccupancy = 8.0;
 
 // Neighbour-pass kernel family of a build. Per-thread walks (one, two or
 // four particles per thread) need many particles to fill the GPU: below
-// kGroupMaxN particles, warp-cooperative group walks (sph_group.cuh) give
-// every particle 4 lanes instead, G = 8 particles per warp.
-#ifndef FORGE_GROUP_MAX_N
-#define FORGE_GROUP_MAX_N (1u << 18)
+// kSmallWalkMaxN particles, row-parallel walks (sph_rows.cuh) give every
+// particle nine threads instead, one per neighbour row (the reference's 50K
+// dam break: 101 -> 60 us per step against the group walks; 65,536 uniform
+// particles: 0.16 -> 0.10 ms against per-thread walks).
+#ifndef FORGE_SMALL_WALK_MAX_N
+#define FORGE_SMALL_WALK_MAX_N (1u << 18)
 #endif
-constexpr uint64_t kGroupMaxN = FORGE_GROUP_MAX_N;
+constexpr uint64_t kSmallWalkMaxN = FORGE_SMALL_WALK_MAX_N;
 
 int walk_of(const forge_grid* g) {
     if (g->walk != FORGE_WALK_AUTO) return g->walk;
-    return g->n < kGroupMaxN ? FORGE_WALK_GROUP8 : FORGE_WALK_THREAD;
+    return g->n < kSmallWalkMaxN ? FORGE_WALK_ROWS : FORGE_WALK_THREAD;
 }
 
 template <int G>
 uint32_t group_blocks(uint64_t n) {
     return grid_blocks((n + G - 1) / G * 32, kSphThreads);
+}
+
+uint32_t rows_blocks(uint64_t n) {
+    return (uint32_t)((n + sph::kRowsParticles - 1) / sph::kRowsParticles);
 }
 
 int launch_density(forge_grid* g, const forge_sph_params* p, float* density, cudaStream_t st) {
@@ -698,15 +725,19 @@ int launch_density(forge_grid* g, const forge_sph_params* p, float* density, cud
     const uint32_t n = (uint32_t)g->n;
     switch (walk_of(g)) {
         case FORGE_WALK_GROUP4:
-            sph::density_group_kernel<4><<<group_blocks<4>(n), kSphThreads, 0, st>>>(
+            launch_pdl(sph::density_group_kernel<4>, group_blocks<4>(n), kSphThreads, st,
                 g->pos4, g->cell_start, g->sorted_idx, n, G, c, g->vel4, g->aux, density);
             break;
         case FORGE_WALK_GROUP8:
-            sph::density_group_kernel<8><<<group_blocks<8>(n), kSphThreads, 0, st>>>(
+            launch_pdl(sph::density_group_kernel<8>, group_blocks<8>(n), kSphThreads, st,
                 g->pos4, g->cell_start, g->sorted_idx, n, G, c, g->vel4, g->aux, density);
             break;
         case FORGE_WALK_GROUP16:
-            sph::density_group_kernel<16><<<group_blocks<16>(n), kSphThreads, 0, st>>>(
+            launch_pdl(sph::density_group_kernel<16>, group_blocks<16>(n), kSphThreads, st,
+                g->pos4, g->cell_start, g->sorted_idx, n, G, c, g->vel4, g->aux, density);
+            break;
+        case FORGE_WALK_ROWS:
+            launch_pdl(sph::density_rows_kernel, rows_blocks(n), sph::kRowsThreads, st,
                 g->pos4, g->cell_start, g->sorted_idx, n, G, c, g->vel4, g->aux, density);
             break;
         default:
@@ -715,10 +746,10 @@ int launch_density(forge_grid* g, const forge_sph_params* p, float* density, cud
             // the union of four windows adds more evaluations than it saves
             // loads: two per thread.
             if ((double)n / (double)cells_w(g) < kPairMaxOccupancy)
-                sph::density_multi_kernel<4><<<grid_blocks((n + 3) / 4, kSphThreads), kSphThreads, 0, st>>>(
+                launch_pdl(sph::density_multi_kernel<4>, grid_blocks((n + 3) / 4, kSphThreads), kSphThreads, st,
                     g->pos4, g->cell_start, g->sorted_idx, n, G, c, g->vel4, g->aux, density);
             else
-                sph::density_pair_kernel<<<grid_blocks((n + 1) / 2, kSphThreads), kSphThreads, 0, st>>>(
+                launch_pdl(sph::density_pair_kernel, grid_blocks((n + 1) / 2, kSphThreads), kSphThreads, st,
                     g->pos4, g->cell_start, g->sorted_idx, n, G, c, g->vel4, g->aux, density);
     }
     FORGE_LAUNCHED();
@@ -734,23 +765,27 @@ void launch_force_k(forge_grid* g, const sph::SphConsts& c, const sph::StepEpi& 
     const uint32_t n = (uint32_t)g->n;
     switch (walk_of(g)) {
         case FORGE_WALK_GROUP4:
-            sph::force_group_kernel<TERMS, EPI, 4, LIST><<<group_blocks<4>(n), kSphThreads, 0, st>>>(
+            launch_pdl(sph::force_group_kernel<TERMS, EPI, 4, LIST>, group_blocks<4>(n), kSphThreads, st,
                 g->pos4, g->vel4, g->aux, g->cell_start, g->sorted_idx, n, G, c, ep, o, zl);
             break;
         case FORGE_WALK_GROUP8:
-            sph::force_group_kernel<TERMS, EPI, 8, LIST><<<group_blocks<8>(n), kSphThreads, 0, st>>>(
+            launch_pdl(sph::force_group_kernel<TERMS, EPI, 8, LIST>, group_blocks<8>(n), kSphThreads, st,
                 g->pos4, g->vel4, g->aux, g->cell_start, g->sorted_idx, n, G, c, ep, o, zl);
             break;
         case FORGE_WALK_GROUP16:
-            sph::force_group_kernel<TERMS, EPI, 16, LIST><<<group_blocks<16>(n), kSphThreads, 0, st>>>(
+            launch_pdl(sph::force_group_kernel<TERMS, EPI, 16, LIST>, group_blocks<16>(n), kSphThreads, st,
+                g->pos4, g->vel4, g->aux, g->cell_start, g->sorted_idx, n, G, c, ep, o, zl);
+            break;
+        case FORGE_WALK_ROWS:
+            launch_pdl(sph::force_rows_kernel<TERMS, EPI, LIST>, rows_blocks(n), sph::kRowsThreads, st,
                 g->pos4, g->vel4, g->aux, g->cell_start, g->sorted_idx, n, G, c, ep, o, zl);
             break;
         default:
             if ((double)n / (double)cells_w(g) < kPairMaxOccupancy)
-                sph::force_kernel<TERMS, EPI, LIST><<<grid_blocks((n + 1) / 2, kSphThreads), kSphThreads, 0, st>>>(
+                launch_pdl(sph::force_kernel<TERMS, EPI, LIST>, grid_blocks((n + 1) / 2, kSphThreads), kSphThreads, st,
                     g->pos4, g->vel4, g->aux, g->cell_start, g->sorted_idx, n, G, c, ep, o, zl);
             else
-                sph::force_single_kernel<TERMS, EPI, LIST><<<grid_blocks(n, kSphThreads), kSphThreads, 0, st>>>(
+                launch_pdl(sph::force_single_kernel<TERMS, EPI, LIST>, grid_blocks(n, kSphThreads), kSphThreads, st,
                     g->pos4, g->vel4, g->aux, g->cell_start, g->sorted_idx, n, G, c, ep, o, zl);
     }
 }
@@ -805,9 +840,9 @@ int zone_classify(forge_grid* g, float inner_lo, float inner_hi, cudaStream_t st
     const uint32_t k_hi = std::max(k_lo, edge(inner_hi, false));
     const sph::ZoneRows z{g->cell_start, (uint32_t)G.ny * (uint32_t)G.nz, row_len, k_lo, k_hi};
     const uint32_t tiles = grid_blocks(z.rows, sph::kZoneRows);
-    sph::zone_rows_count_kernel<<<tiles, sph::kZoneRows, 0, st>>>(z, g->zone_tiles);
+    launch_pdl(sph::zone_rows_count_kernel, tiles, sph::kZoneRows, st, z, g->zone_tiles);
     slab::classify_scan_kernel<<<1, 1024, 0, st>>>(g->zone_tiles, tiles, g->zone_counts);
-    sph::zone_rows_write_kernel<<<tiles, sph::kZoneRows, 0, st>>>(z, g->zone_tiles, g->zone_counts, g->zone_idx);
+    launch_pdl(sph::zone_rows_write_kernel, tiles, sph::kZoneRows, st, z, g->zone_tiles, g->zone_counts, g->zone_idx);
     FORGE_LAUNCHED();
     return FORGE_OK;
 }
@@ -919,7 +954,7 @@ extern "C" int forge_sph_force(forge_grid* g, const forge_sph_params* p, uint32_
     FORGE_DEVICE_SCOPE(g->device);
     cudaStream_t st = as_stream(stream);
     const sph::SphConsts c = make_consts(p);
-    sph::gather_vel_rho_kernel<<<grid_blocks(n, 256), 256, 0, st>>>(g->sorted_idx, (uint32_t)n, vx_in, vy_in,
+    launch_pdl(sph::gather_vel_rho_kernel, grid_blocks(n, 256), 256, st, g->sorted_idx, (uint32_t)n, vx_in, vy_in,
                                                                     vz_in, density, c, g->vel4, g->aux);
     FORGE_LAUNCHED();
     sph::StepEpi ep{};
@@ -977,7 +1012,7 @@ int force_step_impl(const char* fn, forge_grid* g, const forge_sph_params* p, co
     const sph::SphConsts c = make_consts(p);
     sph::ForceOut o{vx, vy, vz, nullptr, nullptr, nullptr, px, py, pz, (uint32_t)n_update};
     if (!mode) {
-        sph::gather_vel_rho_kernel<<<grid_blocks(n, 256), 256, 0, st>>>(g->sorted_idx, (uint32_t)n, vx, vy, vz,
+        launch_pdl(sph::gather_vel_rho_kernel, grid_blocks(n, 256), 256, st, g->sorted_idx, (uint32_t)n, vx, vy, vz,
                                                                         density, c, g->vel4, g->aux);
         g->force_gathered = false;
         launch_force_t<3, 1>(g, c, epi_of(sp), o, st);
@@ -990,7 +1025,7 @@ int force_step_impl(const char* fn, forge_grid* g, const forge_sph_params* p, co
         // cell-ordered velocities + density, both zone lists: what the two
         // zones' kernels read (the boundary particles' columns are updated
         // in place afterwards, so this is done once per build)
-        sph::gather_vel_rho_kernel<<<grid_blocks(n, 256), 256, 0, st>>>(g->sorted_idx, (uint32_t)n, vx, vy, vz,
+        launch_pdl(sph::gather_vel_rho_kernel, grid_blocks(n, 256), 256, st, g->sorted_idx, (uint32_t)n, vx, vy, vz,
                                                                         density, c, g->vel4, g->aux);
         FORGE_LAUNCHED();
         if ((rc = zone_setup(g)) != FORGE_OK) return rc;
@@ -1004,7 +1039,7 @@ int force_step_impl(const char* fn, forge_grid* g, const forge_sph_params* p, co
         FORGE_CUDA(cudaStreamWaitEvent(st, g->ev_zone, 0));
         if (mode == FORGE_ZONE_BOUNDARY && n_update < n) {
             // ghost densities may have arrived since the prepare pass
-            sph::ghost_rho_kernel<<<grid_blocks(n, 256), 256, 0, st>>>(g->sorted_idx, (uint32_t)n,
+            launch_pdl(sph::ghost_rho_kernel, grid_blocks(n, 256), 256, st, g->sorted_idx, (uint32_t)n,
                                                                        (uint32_t)n_update, density, c, g->vel4,
                                                                        g->aux);
             FORGE_LAUNCHED();
@@ -1044,7 +1079,7 @@ extern "C" int forge_apply_ops(const forge_step_params* sp, float* px, float* py
     if (!px || !py || !pz || !vx || !vy || !vz)
         return set_error(FORGE_ERR_INVALID_ARG, "forge_apply_ops: NULL position/velocity pointer");
     FORGE_DEVICE_SCOPE(device);
-    sph::apply_ops_kernel<<<grid_blocks(n, 256), 256, 0, as_stream(stream)>>>(epi_of(sp), px, py, pz, vx, vy, vz,
+    launch_pdl(sph::apply_ops_kernel, grid_blocks(n, 256), 256, as_stream(stream), epi_of(sp), px, py, pz, vx, vy, vz,
                                                                             (uint32_t)n);
     FORGE_LAUNCHED();
     return FORGE_OK;
@@ -1077,7 +1112,7 @@ extern "C" int forge_sph_step(forge_grid* g, const forge_sph_params* p, const fo
 
 extern "C" int forge_grid_set_walk(forge_grid* g, int walk) {
     if (!g) return set_error(FORGE_ERR_INVALID_ARG, "forge_grid_set_walk: grid is NULL");
-    if (walk < FORGE_WALK_AUTO || walk > FORGE_WALK_GROUP16)
+    if (walk < FORGE_WALK_AUTO || walk > FORGE_WALK_ROWS)
         return set_error(FORGE_ERR_INVALID_ARG, "forge_grid_set_walk: unknown walk %d", walk);
     g->walk = walk;
     return FORGE_OK;

@@ -148,6 +148,7 @@ __global__ void __launch_bounds__(256)
     cell_start_gather_kernel(const uint32_t* __restrict__ skeys, const uint32_t* __restrict__ svals,
                              uint32_t n, uint32_t C, uint32_t* __restrict__ cell_start, GatherSrc src,
                              float4* __restrict__ pos4, float4* __restrict__ vel4, uint32_t* __restrict__ chunk_val) {
+    pdl_enter();
     const uint32_t s = blockIdx.x * blockDim.x + threadIdx.x;
     int64_t a = 1, b = 0;  // empty
     uint32_t key = 0;
@@ -180,6 +181,7 @@ __global__ void __launch_bounds__(256)
 // stride), marks cleared for the next build.
 __global__ void __launch_bounds__(256)
     fill_chunks_kernel(uint32_t* __restrict__ cell_start, uint32_t* __restrict__ chunk_val, uint32_t chunks) {
+    pdl_enter();
     for (uint32_t k = blockIdx.x; k < chunks; k += gridDim.x) {
         const uint32_t v = chunk_val[k];
         if (v == kChunkFree) continue;  // uniform per block

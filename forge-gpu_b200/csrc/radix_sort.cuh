@@ -107,6 +107,7 @@ __global__ void __launch_bounds__(kHistThreads)
     digit_histogram_kernel(Src src, uint32_t n, uint32_t begin_bit, uint32_t end_bit,
                            uint32_t passes, uint32_t* __restrict__ hist,
                            uint4* __restrict__ status, uint32_t status_vec4) {
+    pdl_enter();
     static_assert(kHistItems == 8, "load8 runs");
     constexpr int kW = kHistThreads / 32;
     __shared__ uint32_t s_hist[kW][kMaxPasses * kRadix];
@@ -176,6 +177,7 @@ __global__ void __launch_bounds__(kThreads, FORGE_SORT_MIN_BLOCKS)
                          uint32_t* status,                        // [tiles][256]
                          uint32_t* tile_counter, uint32_t parity, uint32_t* err,
                          uint32_t tile_base, uint32_t spin_limit, uint32_t ntiles) {
+    pdl_enter();
     __shared__ uint32_t s_whist[kWarps][kRadix];  // per-warp digit counts, then offsets
     __shared__ uint32_t s_tile_off[kRadix];       // digit start inside the sorted tile
     __shared__ uint32_t s_base[kRadix];           // global dst = s_base[d] + tile position

@@ -217,6 +217,7 @@ __global__ void __launch_bounds__(128, FORGE_DENSITY_MIN_BLOCKS)
     density_pair_kernel(const float4* __restrict__ pos4, const uint32_t* __restrict__ cell_start,
                         const uint32_t* __restrict__ sorted_idx, uint32_t n, Geom g, SphConsts c,
                         float4* __restrict__ vel4, float2* __restrict__ aux, float* __restrict__ density_out) {
+    pdl_enter();
     const uint32_t s0 = 2u * (blockIdx.x * blockDim.x + threadIdx.x);
     if (s0 >= n) return;
     const bool has1 = s0 + 1 < n;
@@ -271,6 +272,7 @@ __global__ void __launch_bounds__(128)
     density_multi_kernel(const float4* __restrict__ pos4, const uint32_t* __restrict__ cell_start,
                          const uint32_t* __restrict__ sorted_idx, uint32_t n, Geom g, SphConsts c,
                          float4* __restrict__ vel4, float2* __restrict__ aux, float* __restrict__ density_out) {
+    pdl_enter();
     const uint32_t s0 = P * (blockIdx.x * blockDim.x + threadIdx.x);
     if (s0 >= n) return;
     const uint32_t np = min((uint32_t)P, n - s0);
@@ -340,6 +342,7 @@ __global__ void __launch_bounds__(256)
                           const float* __restrict__ vy, const float* __restrict__ vz,
                           const float* __restrict__ rho, SphConsts c, float4* __restrict__ vel4,
                           float2* __restrict__ aux) {
+    pdl_enter();
     const uint32_t s = blockIdx.x * blockDim.x + threadIdx.x;
     if (s >= n) return;
     const uint32_t i = svals[s];
@@ -355,6 +358,7 @@ __global__ void __launch_bounds__(256)
 __global__ void __launch_bounds__(256)
     ghost_rho_kernel(const uint32_t* __restrict__ svals, uint32_t n, uint32_t limit, const float* __restrict__ rho,
                      SphConsts c, float4* __restrict__ vel4, float2* __restrict__ aux) {
+    pdl_enter();
     const uint32_t s = blockIdx.x * blockDim.x + threadIdx.x;
     if (s >= n) return;
     const uint32_t i = svals[s];
@@ -439,6 +443,7 @@ struct ZoneRows {
 // Per-tile sums of the boundary and interior lengths (tile_counts[t*3 + 1],
 // [t*3 + 2]; [t*3] = 0), in the layout slab::classify_scan_kernel scans.
 __global__ void __launch_bounds__(kZoneRows) zone_rows_count_kernel(ZoneRows z, uint32_t* __restrict__ tile_counts) {
+    pdl_enter();
     __shared__ uint32_t s[2];
     if (threadIdx.x < 2) s[threadIdx.x] = 0;
     __syncthreads();
@@ -471,6 +476,7 @@ __global__ void __launch_bounds__(kZoneRows) zone_rows_count_kernel(ZoneRows z, 
 __global__ void __launch_bounds__(kZoneRows)
     zone_rows_write_kernel(ZoneRows z, const uint32_t* __restrict__ tile_offsets, const uint32_t* __restrict__ counts,
                            uint32_t* __restrict__ out) {
+    pdl_enter();
     __shared__ uint32_t s_scan[kZoneRows / 32 + 1];
     __shared__ uint32_t s_seg[kZoneRows][6];
     const uint32_t r = blockIdx.x * kZoneRows + threadIdx.x;
@@ -826,6 +832,7 @@ __global__ void __launch_bounds__(128)
                         const float2* __restrict__ aux, const uint32_t* __restrict__ cell_start,
                         const uint32_t* __restrict__ sorted_idx, uint32_t n, Geom g, SphConsts c, StepEpi ep,
                         ForceOut out, ZoneList zl) {
+    pdl_enter();
     if (!LIST) {
         const uint32_t s = blockIdx.x * blockDim.x + threadIdx.x;
         if (s < n) force_single_at<TERMS, EPI>(s, pos4, vel4, aux, cell_start, sorted_idx, g, c, ep, out);
@@ -846,6 +853,7 @@ __global__ void __launch_bounds__(128, FORGE_FORCE_MIN_BLOCKS)
     force_kernel(const float4* __restrict__ pos4, const float4* __restrict__ vel4, const float2* __restrict__ aux,
                  const uint32_t* __restrict__ cell_start, const uint32_t* __restrict__ sorted_idx, uint32_t n, Geom g,
                  SphConsts c, StepEpi ep, ForceOut out, ZoneList zl) {
+    pdl_enter();
     if (!LIST) {
         const uint32_t s0 = 2u * (blockIdx.x * blockDim.x + threadIdx.x);
         if (s0 < n)
@@ -868,6 +876,7 @@ __global__ void __launch_bounds__(128, FORGE_FORCE_MIN_BLOCKS)
 __global__ void __launch_bounds__(256)
     apply_ops_kernel(StepEpi ep, float* __restrict__ px, float* __restrict__ py, float* __restrict__ pz,
                      float* __restrict__ vx, float* __restrict__ vy, float* __restrict__ vz, uint32_t n) {
+    pdl_enter();
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     float x = px[i], y = py[i], z = pz[i], u = vx[i], v = vy[i], w = vz[i];

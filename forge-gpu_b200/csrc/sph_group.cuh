@@ -99,6 +99,7 @@ __global__ void __launch_bounds__(128)
     density_group_kernel(const float4* __restrict__ pos4, const uint32_t* __restrict__ cell_start,
                          const uint32_t* __restrict__ sorted_idx, uint32_t n, Geom g, SphConsts c,
                          float4* __restrict__ vel4, float2* __restrict__ aux, float* __restrict__ density_out) {
+    pdl_enter();
     constexpr int J = GroupLanes<G>::J;
     const uint32_t warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31, ii = lane / J, jj = lane % J;
@@ -182,6 +183,7 @@ __global__ void __launch_bounds__(128)
                        const float2* __restrict__ aux, const uint32_t* __restrict__ cell_start,
                        const uint32_t* __restrict__ sorted_idx, uint32_t n, Geom g, SphConsts c, StepEpi ep,
                        ForceOut out, ZoneList zl) {
+    pdl_enter();
     constexpr int J = GroupLanes<G>::J;
     const uint32_t warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31, ii = lane / J, jj = lane % J;

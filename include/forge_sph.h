@@ -488,20 +488,23 @@ FORGE_API int forge_io_download_vec3(forge_io* io, const float* x, const float* 
 
 /* Neighbour-pass kernel family of a grid's density and force passes (no
  * reference counterpart: the reference has one thread per particle). AUTO
- * (the default) takes per-thread walks for large particle counts and group
+ * (the default) takes per-thread walks for large particle counts and row
  * walks below 2^18 particles, where per-thread walks leave most of the GPU
  * idle; the others force one family, for tests and benchmarks. Every family
  * meets the parity tolerances and is deterministic run to run. Per-thread
  * walks sum each particle's pairs in the reference's order (bit-identical
- * whatever the other particles of the thread); group walks sum a particle's
- * four lanes in a fixed tree whose lane split depends on the particles that
- * share its warp, so the same particle can round differently in another
- * cell order (a zone list, a shard). */
+ * whatever the other particles of the thread); row walks sum each of the
+ * nine rows in that order and add the nine partial sums in row order (the
+ * same whatever the other particles, so bit-identical across cell orders,
+ * zone lists and shards too); group walks sum a particle's lanes in a fixed
+ * tree whose lane split depends on the particles that share its warp, so the
+ * same particle can round differently in another cell order. */
 #define FORGE_WALK_AUTO 0
 #define FORGE_WALK_THREAD 1  /* one, two or four particles per thread */
 #define FORGE_WALK_GROUP4 2  /* warp-cooperative: 4 particles per warp, 8 lanes each */
 #define FORGE_WALK_GROUP8 3  /* 8 particles per warp, 4 lanes each */
 #define FORGE_WALK_GROUP16 4 /* 16 particles per warp, 2 lanes each */
+#define FORGE_WALK_ROWS 5    /* nine threads per particle, one per neighbour row */
 FORGE_API int forge_grid_set_walk(forge_grid* g, int walk);
 
 /* x-window of a grid (no reference counterpart; for a shard of an x-slab

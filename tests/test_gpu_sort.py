@@ -52,7 +52,8 @@ def test_sort_argument_checks(cuda):
     assert e.value.code == forge_sph.FORGE_ERR_INVALID_ARG
 
 
-SIZES = [0, 1, 2, 31, 4095, 4096, 4097, 65537, 1_000_003]
+# tile edges of the small (1024-key) and large (4096-key) tiles
+SIZES = [0, 1, 2, 31, 4095, 4096, 4097, 8191, 8192, 8193, 65537, 131_072, 131_073, 1_000_003]
 RANGES = [(0, 32), (0, 16), (4, 20), (8, 30), (0, 1), (0, 8), (28, 32)]
 
 
@@ -72,8 +73,8 @@ def test_sort_pairs_uniform_vs_oracle(cuda, n):
 
 
 @pytest.mark.parametrize("kind", ["dups4", "allsame", "sorted", "reversed", "morton"])
-def test_sort_pairs_skewed_keys(cuda, kind):
-    n = 300_000
+@pytest.mark.parametrize("n", [100_000, 300_000])
+def test_sort_pairs_skewed_keys(cuda, kind, n):
     rng = np.random.default_rng(11)
     if kind == "dups4":
         keys_np = rng.integers(0, 4, n).astype(np.uint32)

@@ -347,12 +347,13 @@ def _force_step_run(torch, cfg, pos, vel, n_update, zones, walk=forge_sph.WALK_T
 
 
 @pytest.mark.parametrize("name,walk", [("ref65k", forge_sph.WALK_THREAD), ("dambreak65k", forge_sph.WALK_THREAD),
-                                       ("dambreak65k", forge_sph.WALK_GROUP8)])
+                                       ("dambreak65k", forge_sph.WALK_GROUP8), ("dambreak65k", forge_sph.WALK_ROWS)])
 def test_zoned_force_step_equals_whole_pass(cuda, name, walk):
     """Boundary zone then interior zone (the split a sharded step overlaps
     its exchange with) updates every particle exactly once, ghosts
     (i >= n_update) untouched. Per-thread walks (pair and single-particle
-    force kernels) equal the single forge_sph_force_step bit for bit; a group
+    force kernels) and row-parallel walks (a particle's sum involves no other
+    particle) equal the single forge_sph_force_step bit for bit; a group
     walk splits a particle's candidates over lanes by the particles that
     share its warp, which differ between a zone list and the whole cell
     order, so it agrees to fp32 rounding."""
@@ -364,7 +365,7 @@ def test_zoned_force_step_equals_whole_pass(cuda, name, walk):
     g1, got = _force_step_run(cuda, cfg, pos, vel, n_upd, [(1,) + zones, (2,) + zones], walk)
     g1.check()
     for a, b in zip(got, want):
-        if walk == forge_sph.WALK_THREAD:
+        if walk in (forge_sph.WALK_THREAD, forge_sph.WALK_ROWS):
             assert np.array_equal(a, b)
         else:
             np.testing.assert_allclose(a, b, rtol=1e-5, atol=1e-7)

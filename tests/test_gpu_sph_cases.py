@@ -1,6 +1,6 @@
 """GPU parity of every neighbour-pass kernel family (forge_grid_set_walk:
 per-thread walks; warp-cooperative group walks of 4, 8 and 16 particles per
-warp) against the oracle, on sparse, lattice, dense, skewed, ragged and
+warp; row-parallel walks, nine threads per particle) against the oracle, on sparse, lattice, dense, skewed, ragged and
 out-of-grid inputs and with cell size < h (no shared walk across cells).
 
 Tolerances as in test_gpu_sph.py: density 1e-5 relative; accelerations
@@ -50,7 +50,7 @@ def _case(name):
 
 CASES = ["sparse", "lattice", "dense", "blobs", "ragged", "small_cells"]
 WALKS = {"auto": forge_sph.WALK_AUTO, "thread": forge_sph.WALK_THREAD, "group4": forge_sph.WALK_GROUP4,
-         "group8": forge_sph.WALK_GROUP8, "group16": forge_sph.WALK_GROUP16}
+         "group8": forge_sph.WALK_GROUP8, "group16": forge_sph.WALK_GROUP16, "rows": forge_sph.WALK_ROWS}
 
 
 def _params(mod, cfg):
@@ -98,7 +98,7 @@ def test_density_and_force_vs_oracle(cuda, case, walk):
 
 @pytest.mark.parametrize("terms", [1, 2])
 @pytest.mark.parametrize("case", ["dense", "blobs"])
-@pytest.mark.parametrize("walk", ["thread", "group8"])
+@pytest.mark.parametrize("walk", ["thread", "group8", "rows"])
 def test_single_terms(cuda, terms, case, walk):
     cfg, pos, vel = _case(case)
     _, a, scale = _oracle(cfg, pos, vel, terms)
@@ -107,7 +107,7 @@ def test_single_terms(cuda, terms, case, walk):
 
 
 @pytest.mark.parametrize("case", ["lattice", "blobs"])
-@pytest.mark.parametrize("walk", ["thread", "group8"])
+@pytest.mark.parametrize("walk", ["thread", "group8", "rows"])
 def test_passes_are_deterministic(cuda, case, walk):
     cfg, pos, vel = _case(case)
     r1, a1 = _gpu(cuda, cfg, pos, vel, 3, WALKS[walk])
