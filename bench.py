@@ -110,7 +110,7 @@ class Clocks:
 
 
 PHASES = ("sort", "cells_gather", "density", "force")
-WALKS = {"auto": 0, "thread": 1, "group4": 2, "group8": 3, "group16": 4, "rows": 5}  # forge_grid_set_walk
+WALKS = {"auto": 0, "thread": 1, "group4": 2, "group8": 3, "group16": 4, "rows": 5, "tile": 6}  # forge_grid_set_walk
 WALK = 0
 
 

@@ -18,6 +18,7 @@
 #include "sph.cuh"
 #include "sph_group.cuh"
 #include "sph_rows.cuh"
+#include "sph_tile.cuh"
 #include "slab.cuh"
 
 using namespace forge;
@@ -85,11 +86,12 @@ uint32_t grid_blocks(uint64_t work, uint32_t threads) { return (uint32_t)((work 
 // pdl_enter() (common.cuh) until that kernel has completed. Errors
 // surface through cudaGetLastError like a <<<>>> launch.
 template <typename... KArgs, typename... Args>
-void launch_pdl(void (*kernel)(KArgs...), uint32_t grid, uint32_t block, cudaStream_t st, Args&&... args) {
+void launch_pdl_smem(void (*kernel)(KArgs...), uint32_t grid, uint32_t block, uint32_t smem, cudaStream_t st,
+                     Args&&... args) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(block);
-    cfg.dynamicSmemBytes = 0;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute at[1];
     at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -97,6 +99,11 @@ void launch_pdl(void (*kernel)(KArgs...), uint32_t grid, uint32_t block, cudaStr
     cfg.attrs = at;
     cfg.numAttrs = 1;
     cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+template <typename... KArgs, typename... Args>
+void launch_pdl(void (*kernel)(KArgs...), uint32_t grid, uint32_t block, cudaStream_t st, Args&&... args) {
+    launch_pdl_smem(kernel, grid, block, 0, st, std::forward<Args>(args)...);
 }
 
 int num_sms(int device) {
@@ -553,6 +560,10 @@ extern "C" int forge_grid_create(float cell_size, uint32_t nx, uint32_t ny, uint
     if (!ok) rc = set_error(FORGE_ERR_CUDA, "forge_grid_create: cudaMalloc failed (max_n=%llu, cells=%llu)",
                             (unsigned long long)max_n, (unsigned long long)C);
     if (rc == FORGE_OK) rc = scratch_alloc(g->scratch, max_n, device);
+    // the cell-block density pass stages up to kTileCap positions (64 KiB)
+    if (rc == FORGE_OK && cudaFuncSetAttribute(sph::density_tile_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int)(sph::kTileCap * sizeof(float4))) != cudaSuccess)
+        rc = set_error(FORGE_ERR_CUDA, "forge_grid_create: shared-memory attribute of the tile pass");
     if (rc != FORGE_OK) {
         forge_grid_destroy(g);
         return rc;
@@ -736,6 +747,15 @@ int launch_density(forge_grid* g, const forge_sph_params* p, float* density, cud
             launch_pdl(sph::density_group_kernel<16>, group_blocks<16>(n), kSphThreads, st,
                 g->pos4, g->cell_start, g->sorted_idx, n, G, c, g->vel4, g->aux, density);
             break;
+        case FORGE_WALK_TILE:
+            if (g->sub_bits <= (uint32_t)sph::kTileMaxSub) {
+                const uint32_t segs = (uint32_t)((G.nx + sph::kTileCells - 1) / sph::kTileCells);
+                launch_pdl_smem(sph::density_tile_kernel, (uint32_t)G.ny * (uint32_t)G.nz * segs, sph::kTileThreads,
+                                (uint32_t)(sph::kTileCap * sizeof(float4)), st, g->pos4, g->cell_start, g->sorted_idx,
+                                G, c, segs, g->vel4, g->aux, density, g->scratch.meta + kMetaErr);
+                break;
+            }
+            [[fallthrough]];
         case FORGE_WALK_ROWS:
             launch_pdl(sph::density_rows_kernel, rows_blocks(n), sph::kRowsThreads, st,
                 g->pos4, g->cell_start, g->sorted_idx, n, G, c, g->vel4, g->aux, density);
@@ -1112,7 +1132,7 @@ extern "C" int forge_sph_step(forge_grid* g, const forge_sph_params* p, const fo
 
 extern "C" int forge_grid_set_walk(forge_grid* g, int walk) {
     if (!g) return set_error(FORGE_ERR_INVALID_ARG, "forge_grid_set_walk: grid is NULL");
-    if (walk < FORGE_WALK_AUTO || walk > FORGE_WALK_ROWS)
+    if (walk < FORGE_WALK_AUTO || walk > FORGE_WALK_TILE)
         return set_error(FORGE_ERR_INVALID_ARG, "forge_grid_set_walk: unknown walk %d", walk);
     g->walk = walk;
     return FORGE_OK;

@@ -41,7 +41,7 @@ FORGE_ERR_DEVICE = -6
 
 OP_GRAVITY, OP_DRAG, OP_INTEGRATE, OP_GROUND, OP_SPHERE, OP_BOX = 1, 2, 3, 4, 5, 6
 # neighbour-pass kernel families (forge_grid_set_walk)
-WALK_AUTO, WALK_THREAD, WALK_GROUP4, WALK_GROUP8, WALK_GROUP16, WALK_ROWS = 0, 1, 2, 3, 4, 5
+WALK_AUTO, WALK_THREAD, WALK_GROUP4, WALK_GROUP8, WALK_GROUP16, WALK_ROWS, WALK_TILE = 0, 1, 2, 3, 4, 5, 6
 STEP_MAX_OPS = 8
 
 TERM_PRESSURE = 1

@@ -505,6 +505,8 @@ FORGE_API int forge_io_download_vec3(forge_io* io, const float* x, const float* 
 #define FORGE_WALK_GROUP8 3  /* 8 particles per warp, 4 lanes each */
 #define FORGE_WALK_GROUP16 4 /* 16 particles per warp, 2 lanes each */
 #define FORGE_WALK_ROWS 5    /* nine threads per particle, one per neighbour row */
+#define FORGE_WALK_TILE 6    /* density: cell-block CTAs, neighbour rows staged in shared memory by TMA
+                              * (slower than THREAD on every measured case; force passes as THREAD) */
 FORGE_API int forge_grid_set_walk(forge_grid* g, int walk);
 
 /* x-window of a grid (no reference counterpart; for a shard of an x-slab

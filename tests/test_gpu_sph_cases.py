@@ -1,6 +1,7 @@
 """GPU parity of every neighbour-pass kernel family (forge_grid_set_walk:
 per-thread walks; warp-cooperative group walks of 4, 8 and 16 particles per
-warp; row-parallel walks, nine threads per particle) against the oracle, on sparse, lattice, dense, skewed, ragged and
+warp; row-parallel walks, nine threads per particle; cell-block CTAs over
+rows staged in shared memory) against the oracle, on sparse, lattice, dense, skewed, ragged and
 out-of-grid inputs and with cell size < h (no shared walk across cells).
 
 Tolerances as in test_gpu_sph.py: density 1e-5 relative; accelerations
@@ -50,7 +51,8 @@ def _case(name):
 
 CASES = ["sparse", "lattice", "dense", "blobs", "ragged", "small_cells"]
 WALKS = {"auto": forge_sph.WALK_AUTO, "thread": forge_sph.WALK_THREAD, "group4": forge_sph.WALK_GROUP4,
-         "group8": forge_sph.WALK_GROUP8, "group16": forge_sph.WALK_GROUP16, "rows": forge_sph.WALK_ROWS}
+         "group8": forge_sph.WALK_GROUP8, "group16": forge_sph.WALK_GROUP16, "rows": forge_sph.WALK_ROWS,
+         "tile": forge_sph.WALK_TILE}
 
 
 def _params(mod, cfg):
@@ -115,6 +117,18 @@ def test_passes_are_deterministic(cuda, case, walk):
     assert np.array_equal(r1, r2)
     for x, y in zip(a1, a2):
         assert np.array_equal(x, y)
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_tile_density_equals_thread_walk(cuda, case):
+    """The cell-block density pass walks the same candidates in the same
+    order as the per-thread walk, from staged shared memory (or from global
+    memory where a segment's rows exceed the staging capacity: the dense and
+    blob cases): bit-identical densities."""
+    cfg, pos, vel = _case(case)
+    rt, _ = _gpu(cuda, cfg, pos, vel, 3, forge_sph.WALK_THREAD)
+    rs, _ = _gpu(cuda, cfg, pos, vel, 3, forge_sph.WALK_TILE)
+    assert np.array_equal(rt, rs)
 
 
 @pytest.mark.parametrize("case", ["dense", "blobs"])
