@@ -617,6 +617,30 @@ __device__ __forceinline__ uint32_t in_range_bit(const float4& p, const float4& 
     return (r2 < c.h2 && r2 > 1e-12f) ? (1u << k) : 0u;
 }
 
+// Pressure and viscosity terms of one pair (neighbour position q, velocity
+// and 1/rho vj, p_j/rho_j pjr) added to A.
+template <int TERMS>
+__device__ __forceinline__ void force_term(const float4& q, const float4& vj, float pjr, ForceAcc& A,
+                                           const SphConsts& c) {
+    const float djx = A.p.x - q.x, djy = A.p.y - q.y, djz = A.p.z - q.z;
+    const float r2 = __fadd_rn(__fadd_rn(__fmul_rn(djx, djx), __fmul_rn(djy, djy)), __fmul_rn(djz, djz));
+    const float diff = c.h - sqrtf(r2);
+    const float inv_rho_j = vj.w;
+    if (TERMS & 1) {
+        const float pp = fmaf(A.pres, inv_rho_j, pjr);
+        const float f = c.kp * pp * (diff * diff) * rsqrtf(r2);
+        A.pax = fmaf(f, djx, A.pax);
+        A.pay = fmaf(f, djy, A.pay);
+        A.paz = fmaf(f, djz, A.paz);
+    }
+    if (TERMS & 2) {
+        const float v = c.kv * inv_rho_j * diff;
+        A.vax = fmaf(v, vj.x - A.v.x, A.vax);
+        A.vay = fmaf(v, vj.y - A.v.y, A.vay);
+        A.vaz = fmaf(v, vj.z - A.v.z, A.vaz);
+    }
+}
+
 // Pair terms of the hits (bit k = candidate j0 + k), ascending j.
 template <int TERMS>
 __device__ __forceinline__ void force_hits(const float4* __restrict__ pos4, const float4* __restrict__ vel4,
@@ -629,23 +653,7 @@ __device__ __forceinline__ void force_hits(const float4* __restrict__ pos4, cons
         const float4 q = __ldg(pos4 + j);
         const float4 vj = __ldg(vel4 + j);
         const float pjr = (TERMS & 1) ? __ldg(pj_over_rho + 2 * j) : 0.f;
-        const float djx = A.p.x - q.x, djy = A.p.y - q.y, djz = A.p.z - q.z;
-        const float r2 = __fadd_rn(__fadd_rn(__fmul_rn(djx, djx), __fmul_rn(djy, djy)), __fmul_rn(djz, djz));
-        const float diff = c.h - sqrtf(r2);
-        const float inv_rho_j = vj.w;
-        if (TERMS & 1) {
-            const float pp = fmaf(A.pres, inv_rho_j, pjr);
-            const float f = c.kp * pp * (diff * diff) * rsqrtf(r2);
-            A.pax = fmaf(f, djx, A.pax);
-            A.pay = fmaf(f, djy, A.pay);
-            A.paz = fmaf(f, djz, A.paz);
-        }
-        if (TERMS & 2) {
-            const float v = c.kv * inv_rho_j * diff;
-            A.vax = fmaf(v, vj.x - A.v.x, A.vax);
-            A.vay = fmaf(v, vj.y - A.v.y, A.vay);
-            A.vaz = fmaf(v, vj.z - A.v.z, A.vaz);
-        }
+        force_term<TERMS>(q, vj, pjr, A, c);
     }
 }
 
