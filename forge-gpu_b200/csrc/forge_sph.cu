@@ -694,6 +694,7 @@ sph::Geom geom_of(const forge_grid* g, float h) {
     G.x_off = (int)((uint32_t)g->geom.cx0 << g->sub_bits);
     G.row_len = make_fastdiv((uint32_t)g->geom.nxw << g->sub_bits);
     G.ny_div = make_fastdiv((uint32_t)g->geom.ny);
+    G.keys = g->sorted_keys;
     return G;
 }
 
@@ -975,7 +976,7 @@ extern "C" int forge_sph_force(forge_grid* g, const forge_sph_params* p, uint32_
     cudaStream_t st = as_stream(stream);
     const sph::SphConsts c = make_consts(p);
     launch_pdl(sph::gather_vel_rho_kernel, grid_blocks(n, 256), 256, st, g->sorted_idx, (uint32_t)n, vx_in, vy_in,
-                                                                    vz_in, density, c, g->vel4, g->aux);
+                                                                    vz_in, density, c, g->vel4, g->aux, g->pos4);
     FORGE_LAUNCHED();
     sph::StepEpi ep{};
     ep.dt = dt;
@@ -1033,7 +1034,7 @@ int force_step_impl(const char* fn, forge_grid* g, const forge_sph_params* p, co
     sph::ForceOut o{vx, vy, vz, nullptr, nullptr, nullptr, px, py, pz, (uint32_t)n_update};
     if (!mode) {
         launch_pdl(sph::gather_vel_rho_kernel, grid_blocks(n, 256), 256, st, g->sorted_idx, (uint32_t)n, vx, vy, vz,
-                                                                        density, c, g->vel4, g->aux);
+                                                                        density, c, g->vel4, g->aux, g->pos4);
         g->force_gathered = false;
         launch_force_t<3, 1>(g, c, epi_of(sp), o, st);
         FORGE_LAUNCHED();
@@ -1046,7 +1047,7 @@ int force_step_impl(const char* fn, forge_grid* g, const forge_sph_params* p, co
         // zones' kernels read (the boundary particles' columns are updated
         // in place afterwards, so this is done once per build)
         launch_pdl(sph::gather_vel_rho_kernel, grid_blocks(n, 256), 256, st, g->sorted_idx, (uint32_t)n, vx, vy, vz,
-                                                                        density, c, g->vel4, g->aux);
+                                                                        density, c, g->vel4, g->aux, g->pos4);
         FORGE_LAUNCHED();
         if ((rc = zone_setup(g)) != FORGE_OK) return rc;
         if ((rc = zone_classify(g, zone->inner_lo, zone->inner_hi, st)) != FORGE_OK) return rc;
@@ -1061,7 +1062,7 @@ int force_step_impl(const char* fn, forge_grid* g, const forge_sph_params* p, co
             // ghost densities may have arrived since the prepare pass
             launch_pdl(sph::ghost_rho_kernel, grid_blocks(n, 256), 256, st, g->sorted_idx, (uint32_t)n,
                                                                        (uint32_t)n_update, density, c, g->vel4,
-                                                                       g->aux);
+                                                                       g->aux, g->pos4);
             FORGE_LAUNCHED();
         }
     }

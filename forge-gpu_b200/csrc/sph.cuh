@@ -5,7 +5,11 @@
 // order. The SPH grid build sorts them by key = cell << sub_bits | x-slice
 // (each cell cut into 2^sub_bits slabs along x; ties in ascending particle
 // index) and the library holds cell-ordered copies
-//   pos4[s] = (x, y, z, bits(key))
+//   pos4[s] = (x, y, z, bits(key))     after the build
+//           = (x, y, z, p/rho)         after the density pass (a force-pass
+//                                      neighbour's position and p_j/rho_j in
+//                                      one 16-byte load; own keys then come
+//                                      from the sorted keys)
 //   vel4[s] = (vx, vy, vz, 1/rho)       (1/rho := 0 when rho < 1e-6)
 //   aux[s]  = (p/rho, rho)              p = k (rho - rho0)
 // so for each row (dz, dy) of the 3x3x3 cell block the candidates are ONE
@@ -59,7 +63,20 @@ struct Geom {
     int x_off;         // first slice of the grid's x-window: cx0 << sub_bits (nx is the window's width)
     FastDiv row_len;   // nx << sub_bits: key -> (row, slice in row)
     FastDiv ny_div;    // ny: row -> (cy, cz)
+    const uint32_t* __restrict__ keys;  // cell keys in cell order (a particle's own key: its frame)
 };
+
+// Cell-ordered position of particle s with w = bits(its cell key), for the
+// force pass. pos4.w holds the key from the grid build (the density pass
+// reads its own particles' keys there) until the density pass replaces it
+// with p/rho (the force pass's neighbour data: one 16-byte load gives a
+// neighbour's position and p_j/rho_j), so the force pass takes a particle's
+// own key from the sorted keys. Every density pass follows a build.
+__device__ __forceinline__ float4 own_pos(const float4* __restrict__ pos4, const Geom& g, uint32_t s) {
+    float4 p = pos4[s];
+    p.w = __uint_as_float(__ldg(g.keys + s));
+    return p;
+}
 
 // Squared conservative gap: distance shrunk by a slack covering the rounding
 // of the cell assignment and of r^2, clamped at 0 (clamped out-of-grid
@@ -214,7 +231,7 @@ __device__ __forceinline__ void poly6_two(const float4* __restrict__ pos4, uint3
 #endif
 
 __global__ void __launch_bounds__(128, FORGE_DENSITY_MIN_BLOCKS)
-    density_pair_kernel(const float4* __restrict__ pos4, const uint32_t* __restrict__ cell_start,
+    density_pair_kernel(float4* __restrict__ pos4, const uint32_t* __restrict__ cell_start,
                         const uint32_t* __restrict__ sorted_idx, uint32_t n, Geom g, SphConsts c,
                         float4* __restrict__ vel4, float2* __restrict__ aux, float* __restrict__ density_out) {
     pdl_enter();
@@ -251,6 +268,7 @@ __global__ void __launch_bounds__(128, FORGE_DENSITY_MIN_BLOCKS)
     if (vel4 != nullptr) {
         vel4[s0].w = inv_rho;
         aux[s0] = a;
+        pos4[s0] = make_float4(p0.x, p0.y, p0.z, a.x);
     }
     if (density_out != nullptr) density_out[sorted_idx[s0]] = rho0;
     if (has1) {
@@ -258,6 +276,7 @@ __global__ void __launch_bounds__(128, FORGE_DENSITY_MIN_BLOCKS)
         if (vel4 != nullptr) {
             vel4[s0 + 1].w = inv_rho;
             aux[s0 + 1] = a;
+            pos4[s0 + 1] = make_float4(p1.x, p1.y, p1.z, a.x);
         }
         if (density_out != nullptr) density_out[sorted_idx[s0 + 1]] = rho1;
     }
@@ -267,9 +286,12 @@ __global__ void __launch_bounds__(128, FORGE_DENSITY_MIN_BLOCKS)
 // one grid row (and cell size >= h), one walk over the union of their
 // windows feeds P pair evaluations per neighbour load (extra candidates add
 // exactly +0, as in the two-particle kernel); otherwise P single walks.
+#ifndef FORGE_MULTI_MIN_BLOCKS
+#define FORGE_MULTI_MIN_BLOCKS 8  // at most 64 registers: 8 blocks per SM
+#endif
 template <int P>
-__global__ void __launch_bounds__(128)
-    density_multi_kernel(const float4* __restrict__ pos4, const uint32_t* __restrict__ cell_start,
+__global__ void __launch_bounds__(128, FORGE_MULTI_MIN_BLOCKS)
+    density_multi_kernel(float4* __restrict__ pos4, const uint32_t* __restrict__ cell_start,
                          const uint32_t* __restrict__ sorted_idx, uint32_t n, Geom g, SphConsts c,
                          float4* __restrict__ vel4, float2* __restrict__ aux, float* __restrict__ density_out) {
     pdl_enter();
@@ -330,6 +352,7 @@ __global__ void __launch_bounds__(128)
         if (vel4 != nullptr) {
             vel4[s0 + k].w = inv_rho;
             aux[s0 + k] = a;
+            pos4[s0 + k] = make_float4(p[k].x, p[k].y, p[k].z, a.x);
         }
         if (density_out != nullptr) density_out[sorted_idx[s0 + k]] = r;
     }
@@ -341,7 +364,7 @@ __global__ void __launch_bounds__(256)
     gather_vel_rho_kernel(const uint32_t* __restrict__ svals, uint32_t n, const float* __restrict__ vx,
                           const float* __restrict__ vy, const float* __restrict__ vz,
                           const float* __restrict__ rho, SphConsts c, float4* __restrict__ vel4,
-                          float2* __restrict__ aux) {
+                          float2* __restrict__ aux, float4* __restrict__ pos4) {
     pdl_enter();
     const uint32_t s = blockIdx.x * blockDim.x + threadIdx.x;
     if (s >= n) return;
@@ -351,13 +374,14 @@ __global__ void __launch_bounds__(256)
     density_derived(rho[i], c, inv_rho, a);
     vel4[s] = make_float4(vx[i], vy[i], vz[i], inv_rho);
     aux[s] = a;
+    pos4[s].w = a.x;
 }
 
 // Re-derives 1/rho, p/rho and rho of the ghosts (original index >= limit)
 // from density[] after their owners' values arrived.
 __global__ void __launch_bounds__(256)
     ghost_rho_kernel(const uint32_t* __restrict__ svals, uint32_t n, uint32_t limit, const float* __restrict__ rho,
-                     SphConsts c, float4* __restrict__ vel4, float2* __restrict__ aux) {
+                     SphConsts c, float4* __restrict__ vel4, float2* __restrict__ aux, float4* __restrict__ pos4) {
     pdl_enter();
     const uint32_t s = blockIdx.x * blockDim.x + threadIdx.x;
     if (s >= n) return;
@@ -368,6 +392,7 @@ __global__ void __launch_bounds__(256)
     density_derived(rho[i], c, inv_rho, a);
     vel4[s].w = inv_rho;
     aux[s] = a;
+    pos4[s].w = a.x;
 }
 
 // ---------------------------------------------------------------------------
@@ -602,9 +627,10 @@ struct ForceAcc {
 };
 
 __device__ __forceinline__ ForceAcc force_acc(const float4* __restrict__ pos4, const float4* __restrict__ vel4,
-                                              const float2* __restrict__ aux, uint32_t s, const SphConsts& c) {
+                                              const float2* __restrict__ aux, uint32_t s, const SphConsts& c,
+                                              const Geom& g) {
     ForceAcc A;
-    A.p = pos4[s];
+    A.p = own_pos(pos4, g, s);
     A.v = vel4[s];
     A.pres = c.k * (aux[s].y - c.rho0);
     A.pax = A.pay = A.paz = A.vax = A.vay = A.vaz = 0.f;
@@ -644,16 +670,15 @@ __device__ __forceinline__ void force_term(const float4& q, const float4& vj, fl
 // Pair terms of the hits (bit k = candidate j0 + k), ascending j.
 template <int TERMS>
 __device__ __forceinline__ void force_hits(const float4* __restrict__ pos4, const float4* __restrict__ vel4,
-                                           const float* __restrict__ pj_over_rho, uint32_t j0, uint32_t hit,
+                                           uint32_t j0, uint32_t hit,
                                            ForceAcc& A, const SphConsts& c) {
     while (hit) {
         const uint32_t j = j0 + (uint32_t)(__ffs(hit) - 1);
         hit &= hit - 1;
-        // all three loads issued together (one latency per hit)
+        // both loads issued together (one latency per hit)
         const float4 q = __ldg(pos4 + j);
         const float4 vj = __ldg(vel4 + j);
-        const float pjr = (TERMS & 1) ? __ldg(pj_over_rho + 2 * j) : 0.f;
-        force_term<TERMS>(q, vj, pjr, A, c);
+        force_term<TERMS>(q, vj, q.w, A, c);  // q.w = p_j / rho_j
     }
 }
 
@@ -661,21 +686,21 @@ __device__ __forceinline__ void force_hits(const float4* __restrict__ pos4, cons
 // evaluate only the hits.
 template <int TERMS>
 __device__ __forceinline__ void force_one(const float4* __restrict__ pos4, const float4* __restrict__ vel4,
-                                          const float* __restrict__ pj, uint32_t b, uint32_t e, ForceAcc& A,
+                                          uint32_t b, uint32_t e, ForceAcc& A,
                                           const SphConsts& c) {
     for (uint32_t j0 = b; j0 < e; j0 += 32) {
         const uint32_t cnt = min(32u, e - j0);
         uint32_t hit = 0;
 #pragma unroll 4
         for (uint32_t k = 0; k < cnt; ++k) hit |= in_range_bit(A.p, __ldg(pos4 + j0 + k), c, k);
-        force_hits<TERMS>(pos4, vel4, pj, j0, hit, A, c);
+        force_hits<TERMS>(pos4, vel4, j0, hit, A, c);
     }
 }
 
 // Candidates [b, e) for two particles: one load per candidate in the scan.
 template <int TERMS>
 __device__ __forceinline__ void force_two(const float4* __restrict__ pos4, const float4* __restrict__ vel4,
-                                          const float* __restrict__ pj, uint32_t b, uint32_t e, ForceAcc& A,
+                                          uint32_t b, uint32_t e, ForceAcc& A,
                                           ForceAcc& B, const SphConsts& c) {
     for (uint32_t j0 = b; j0 < e; j0 += 32) {
         const uint32_t cnt = min(32u, e - j0);
@@ -686,8 +711,8 @@ __device__ __forceinline__ void force_two(const float4* __restrict__ pos4, const
             ha |= in_range_bit(A.p, q, c, k);
             hb |= in_range_bit(B.p, q, c, k);
         }
-        force_hits<TERMS>(pos4, vel4, pj, j0, ha, A, c);
-        force_hits<TERMS>(pos4, vel4, pj, j0, hb, B, c);
+        force_hits<TERMS>(pos4, vel4, j0, ha, A, c);
+        force_hits<TERMS>(pos4, vel4, j0, hb, B, c);
     }
 }
 
@@ -759,8 +784,7 @@ __device__ __forceinline__ void force_single_at(uint32_t s, const float4* __rest
                                                 const SphConsts& c, const StepEpi& ep, const ForceOut& out) {
     const uint32_t i = sorted_idx[s];
     if (i >= out.limit) return;  // not updated (a ghost of a sharded run)
-    const float* __restrict__ pj = reinterpret_cast<const float*>(aux);
-    ForceAcc A = force_acc(pos4, vel4, aux, s, c);
+    ForceAcc A = force_acc(pos4, vel4, aux, s, c, g);
     if (A.v.w != 0.f) {
         const Frame f = make_frame(A.p, g);
 #pragma unroll 1
@@ -768,7 +792,7 @@ __device__ __forceinline__ void force_single_at(uint32_t s, const float4* __rest
             int lo, hi;
             if (!row_window(f, r, g, c.h2_skip, lo, hi)) continue;
             const uint32_t row = row_base(g, f, r);
-            force_one<TERMS>(pos4, vel4, pj, __ldg(cell_start + row + lo), __ldg(cell_start + row + hi + 1), A, c);
+            force_one<TERMS>(pos4, vel4, __ldg(cell_start + row + lo), __ldg(cell_start + row + hi + 1), A, c);
         }
     }
     force_finish<EPI>(A, i, ep, out);
@@ -786,9 +810,8 @@ __device__ __forceinline__ void force_pair_at(uint32_t s0, uint32_t s1, bool has
                                               const uint32_t* __restrict__ cell_start,
                                               const uint32_t* __restrict__ sorted_idx, const Geom& g,
                                               const SphConsts& c, const StepEpi& ep, const ForceOut& out) {
-    const float* __restrict__ pj = reinterpret_cast<const float*>(aux);
-    ForceAcc A = force_acc(pos4, vel4, aux, s0, c);
-    ForceAcc B = force_acc(pos4, vel4, aux, has1 ? s1 : s0, c);
+    ForceAcc A = force_acc(pos4, vel4, aux, s0, c, g);
+    ForceAcc B = force_acc(pos4, vel4, aux, has1 ? s1 : s0, c, g);
     const uint32_t i0 = sorted_idx[s0], i1 = has1 ? sorted_idx[s1] : 0xffffffffu;
     // rho < 1e-6 (1/rho stored as 0) or not updated (ghost): no walk
     const bool va = A.v.w != 0.f && i0 < out.limit, vb = has1 && B.v.w != 0.f && i1 < out.limit;
@@ -803,7 +826,7 @@ __device__ __forceinline__ void force_pair_at(uint32_t s0, uint32_t s1, bool has
             const bool b = row_window(f1, r, g, c.h2_skip, l1, h1);
             if (!union_window(a, l0, h0, b, l1, h1, lo, hi)) continue;
             const uint32_t row = row_base(g, f0, r);
-            force_two<TERMS>(pos4, vel4, pj, __ldg(cell_start + row + lo), __ldg(cell_start + row + hi + 1), A, B, c);
+            force_two<TERMS>(pos4, vel4, __ldg(cell_start + row + lo), __ldg(cell_start + row + hi + 1), A, B, c);
         }
     } else {
 #pragma unroll 1
@@ -811,7 +834,7 @@ __device__ __forceinline__ void force_pair_at(uint32_t s0, uint32_t s1, bool has
             int lo, hi;
             if (va && row_window(f0, r, g, c.h2_skip, lo, hi)) {
                 const uint32_t row = row_base(g, f0, r);
-                force_one<TERMS>(pos4, vel4, pj, __ldg(cell_start + row + lo), __ldg(cell_start + row + hi + 1), A,
+                force_one<TERMS>(pos4, vel4, __ldg(cell_start + row + lo), __ldg(cell_start + row + hi + 1), A,
                                  c);
             }
         }
@@ -820,7 +843,7 @@ __device__ __forceinline__ void force_pair_at(uint32_t s0, uint32_t s1, bool has
             int lo, hi;
             if (vb && row_window(f1, r, g, c.h2_skip, lo, hi)) {
                 const uint32_t row = row_base(g, f1, r);
-                force_one<TERMS>(pos4, vel4, pj, __ldg(cell_start + row + lo), __ldg(cell_start + row + hi + 1), B,
+                force_one<TERMS>(pos4, vel4, __ldg(cell_start + row + lo), __ldg(cell_start + row + hi + 1), B,
                                  c);
             }
         }

@@ -96,7 +96,7 @@ __device__ __forceinline__ bool group_row(const Frame& f, bool member, int r, co
 // ---------------------------------------------------------------------------
 template <int G>
 __global__ void __launch_bounds__(128)
-    density_group_kernel(const float4* __restrict__ pos4, const uint32_t* __restrict__ cell_start,
+    density_group_kernel(float4* __restrict__ pos4, const uint32_t* __restrict__ cell_start,
                          const uint32_t* __restrict__ sorted_idx, uint32_t n, Geom g, SphConsts c,
                          float4* __restrict__ vel4, float2* __restrict__ aux, float* __restrict__ density_out) {
     pdl_enter();
@@ -137,6 +137,7 @@ __global__ void __launch_bounds__(128)
         if (vel4 != nullptr) {
             vel4[s].w = inv_rho;
             aux[s] = a;
+            pos4[s] = make_float4(p.x, p.y, p.z, a.x);
         }
         if (density_out != nullptr) density_out[sorted_idx[s]] = rho;
     }
@@ -150,7 +151,7 @@ __global__ void __launch_bounds__(128)
 // ---------------------------------------------------------------------------
 template <int TERMS, int J>
 __device__ __forceinline__ void force_hits_strided(const float4* __restrict__ pos4, const float4* __restrict__ vel4,
-                                                   const float* __restrict__ pj_over_rho, uint32_t j0,
+                                                   uint32_t j0,
                                                    uint32_t hit, ForceAcc& A, const SphConsts& c) {
     while (hit) {
         const uint32_t j = j0 + (uint32_t)(__ffs(hit) - 1) * J;
@@ -162,7 +163,7 @@ __device__ __forceinline__ void force_hits_strided(const float4* __restrict__ po
         const float diff = c.h - sqrtf(r2);
         const float inv_rho_j = vj.w;
         if (TERMS & 1) {
-            const float pp = fmaf(A.pres, inv_rho_j, __ldg(pj_over_rho + 2 * j));
+            const float pp = fmaf(A.pres, inv_rho_j, q.w);  // q.w = p_j / rho_j
             const float fs = c.kp * pp * (diff * diff) * rsqrtf(r2);
             A.pax = fmaf(fs, djx, A.pax);
             A.pay = fmaf(fs, djy, A.pay);
@@ -195,8 +196,7 @@ __global__ void __launch_bounds__(128)
     const uint32_t t = t0 + ii;
     const bool in = t < cnt;
     const uint32_t s = LIST ? lst[in ? t : t0] : (in ? t : t0);
-    const float* __restrict__ pj = reinterpret_cast<const float*>(aux);
-    ForceAcc A = force_acc(pos4, vel4, aux, s, c);
+    ForceAcc A = force_acc(pos4, vel4, aux, s, c, g);
     const uint32_t i = sorted_idx[s];
     // rho < 1e-6 (1/rho stored as 0) or not updated (a ghost): no walk
     bool pending = in && A.v.w != 0.f && i < out.limit;
@@ -214,7 +214,7 @@ __global__ void __launch_bounds__(128)
 #pragma unroll 4
                 for (uint32_t k = 0; k < k_end; ++k) hit |= in_range_bit(A.p, __ldg(pos4 + j0 + k * J), c, k);
                 if (!member) hit = 0;
-                force_hits_strided<TERMS, J>(pos4, vel4, pj, j0, hit, A, c);
+                force_hits_strided<TERMS, J>(pos4, vel4, j0, hit, A, c);
             }
         }
         pending = pending && !member;

@@ -30,7 +30,7 @@ constexpr int kRowsThreads = kRowsParticles * 9;
 // Density (poly6, self included).
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kRowsThreads)
-    density_rows_kernel(const float4* __restrict__ pos4, const uint32_t* __restrict__ cell_start,
+    density_rows_kernel(float4* __restrict__ pos4, const uint32_t* __restrict__ cell_start,
                         const uint32_t* __restrict__ sorted_idx, uint32_t n, Geom g, SphConsts c,
                         float4* __restrict__ vel4, float2* __restrict__ aux, float* __restrict__ density_out) {
     pdl_enter();
@@ -63,6 +63,8 @@ __global__ void __launch_bounds__(kRowsThreads)
     if (vel4 != nullptr) {
         vel4[sp].w = inv_rho;
         aux[sp] = a;
+        const float4 q = pos4[sp];
+        pos4[sp] = make_float4(q.x, q.y, q.z, a.x);
     }
     if (density_out != nullptr) density_out[sorted_idx[sp]] = sum;
 }
@@ -87,20 +89,19 @@ __global__ void __launch_bounds__(kRowsThreads)
     const int t = threadIdx.x, pl = t / 9, r = t - pl * 9;
     const uint32_t t0 = blockIdx.x * kRowsParticles;
     if (t0 >= cnt) return;  // whole block
-    const float* __restrict__ pj = reinterpret_cast<const float*>(aux);
     const uint32_t slot = t0 + pl;
     ForceAcc A;
     A.pax = A.pay = A.paz = A.vax = A.vay = A.vaz = 0.f;
     if (slot < cnt) {
         const uint32_t s = LIST ? lst[slot] : slot;
-        A = force_acc(pos4, vel4, aux, s, c);
+        A = force_acc(pos4, vel4, aux, s, c, g);
         // rho < 1e-6 (1/rho stored as 0) or not updated (a ghost): no walk
         if (A.v.w != 0.f && sorted_idx[s] < out.limit) {
             const Frame f = make_frame(A.p, g);
             int lo, hi;
             if (row_window(f, r, g, c.h2_skip, lo, hi)) {
                 const uint32_t row = row_base(g, f, r);
-                force_one<TERMS>(pos4, vel4, pj, __ldg(cell_start + row + lo), __ldg(cell_start + row + hi + 1), A,
+                force_one<TERMS>(pos4, vel4, __ldg(cell_start + row + lo), __ldg(cell_start + row + hi + 1), A,
                                  c);
             }
         }
@@ -116,7 +117,7 @@ __global__ void __launch_bounds__(kRowsThreads)
     const uint32_t sp = t0 + t;
     if (sp >= cnt) return;
     const uint32_t s = LIST ? lst[sp] : sp;
-    ForceAcc B = force_acc(pos4, vel4, aux, s, c);
+    ForceAcc B = force_acc(pos4, vel4, aux, s, c, g);
     float acc[6];
 #pragma unroll
     for (int q = 0; q < 6; ++q) {

@@ -61,7 +61,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t phase) {
 }
 
 __global__ void __launch_bounds__(kTileThreads)
-    density_tile_kernel(const float4* __restrict__ pos4, const uint32_t* __restrict__ cell_start,
+    density_tile_kernel(float4* __restrict__ pos4, const uint32_t* __restrict__ cell_start,
                         const uint32_t* __restrict__ sorted_idx, Geom g, SphConsts c, uint32_t segs,
                         float4* __restrict__ vel4, float2* __restrict__ aux, float* __restrict__ density_out,
                         uint32_t* __restrict__ err) {
@@ -157,6 +157,7 @@ __global__ void __launch_bounds__(kTileThreads)
         if (vel4 != nullptr) {
             vel4[j].w = inv_rho;
             aux[j] = a;
+            pos4[j] = make_float4(p.x, p.y, p.z, a.x);
         }
         if (density_out != nullptr) density_out[sorted_idx[j]] = rho;
     }
