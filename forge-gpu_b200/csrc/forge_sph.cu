@@ -821,8 +821,8 @@ void launch_force_t(forge_grid* g, const sph::SphConsts& c, const sph::StepEpi& 
 // lived blocks leave room for concurrent work (the other zone, the exchange
 // kernels, NCCL).
 int launch_force_zone(forge_grid* g, const sph::SphConsts& c, const sph::StepEpi& ep, const sph::ForceOut& o,
-                      uint32_t list, uint32_t part, float split, cudaStream_t st) {
-    const sph::ZoneList zl{g->zone_idx, g->zone_counts, list, part, split};
+                      uint32_t list, cudaStream_t st) {
+    const sph::ZoneList zl{g->zone_idx, g->zone_counts, list};
     launch_force_k<3, 1, true>(g, c, ep, o, zl, st);
     FORGE_LAUNCHED();
     return FORGE_OK;
@@ -1022,16 +1022,8 @@ int force_step_impl(const char* fn, forge_grid* g, const forge_sph_params* p, co
                          fn, (unsigned long long)n, (unsigned long long)g->n);
     if (n_update > n) return set_error(FORGE_ERR_INVALID_ARG, "%s: n_update > n", fn);
     const uint32_t mode = zone ? zone->mode : 0u;
-    if (mode > FORGE_ZONE_INTERIOR_TAIL) return set_error(FORGE_ERR_INVALID_ARG, "%s: bad zone mode %u", fn, mode);
-    const bool interior = mode == FORGE_ZONE_INTERIOR || mode == FORGE_ZONE_INTERIOR_HEAD ||
-                          mode == FORGE_ZONE_INTERIOR_TAIL;
-    float split = 0.5f;
-    if (mode == FORGE_ZONE_INTERIOR_HEAD || mode == FORGE_ZONE_INTERIOR_TAIL) {
-        if (zone->split != 0.f) split = zone->split;
-        if (!(split > 0.f && split <= 1.f))
-            return set_error(FORGE_ERR_INVALID_ARG, "%s: zone split must lie in (0, 1]", fn);
-    }
-    if (interior && !g->force_gathered)
+    if (mode > FORGE_ZONE_PREPARE) return set_error(FORGE_ERR_INVALID_ARG, "%s: bad zone mode %u", fn, mode);
+    if (mode == FORGE_ZONE_INTERIOR && !g->force_gathered)
         return set_error(FORGE_ERR_INVALID_ARG,
                          "%s: an interior pass must follow a prepare or boundary pass of the same build", fn);
     if (n == 0) return FORGE_OK;
@@ -1074,12 +1066,11 @@ int force_step_impl(const char* fn, forge_grid* g, const forge_sph_params* p, co
             FORGE_LAUNCHED();
         }
     }
-    o.zone = interior ? FORGE_ZONE_INTERIOR : mode;
+    o.zone = mode;
     o.glo = zone->guard_lo;
     o.ghi = zone->guard_hi;
     o.status = g->scratch.meta + kMetaErr;
-    const uint32_t part = mode == FORGE_ZONE_INTERIOR_HEAD ? 1u : (mode == FORGE_ZONE_INTERIOR_TAIL ? 2u : 0u);
-    return launch_force_zone(g, c, epi_of(sp), o, interior ? FORGE_ZONE_INTERIOR : mode, part, split, st);
+    return launch_force_zone(g, c, epi_of(sp), o, mode, st);
 }
 
 }  // namespace

@@ -441,8 +441,6 @@ struct ZoneList {
     const uint32_t* idx = nullptr;
     const uint32_t* counts = nullptr;
     uint32_t list = 0;
-    uint32_t part = 0;   // 0: the whole list; 1: its first `split`; 2: the rest
-    float split = 0.5f;
 };
 
 // Zone lists from the cell-start table. With keys cell << sub_bits | slice
@@ -856,17 +854,7 @@ __device__ __forceinline__ void force_pair_at(uint32_t s0, uint32_t s1, bool has
 
 __device__ __forceinline__ const uint32_t* zone_begin(const ZoneList& z, uint32_t& cnt) {
     cnt = z.counts[z.list];
-    const uint32_t* p = z.idx + z.counts[0] + (z.list == 2 ? z.counts[1] : 0u);
-    if (z.part) {
-        const uint32_t k = min(cnt, (uint32_t)((float)cnt * z.split));
-        if (z.part == 1) {
-            cnt = k;
-        } else {
-            p += k;
-            cnt -= k;
-        }
-    }
-    return p;
+    return z.idx + z.counts[0] + (z.list == 2 ? z.counts[1] : 0u);
 }
 
 template <int TERMS, int EPI, bool LIST>

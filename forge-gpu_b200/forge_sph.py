@@ -107,7 +107,7 @@ class StepParams(ctypes.Structure):
 class ForceZone(ctypes.Structure):
     """forge_force_zone: the x-split of forge_sph_force_step_zone."""
     _fields_ = [("mode", ctypes.c_uint32), ("inner_lo", ctypes.c_float), ("inner_hi", ctypes.c_float),
-                ("guard_lo", ctypes.c_float), ("guard_hi", ctypes.c_float), ("split", ctypes.c_float)]
+                ("guard_lo", ctypes.c_float), ("guard_hi", ctypes.c_float)]
 
 
 _lib = None

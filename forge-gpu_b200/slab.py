@@ -241,9 +241,6 @@ class SlabRun:
         self.cols[:, :n_own] = own.to(device)
         self.n = n_own
         self.ng = 0
-        # fraction of the interior zone updated before the boundary zone (while
-        # the ghost densities travel); the rest runs beside round 1
-        self.interior_head = 0.5
         self.timing = None  # set to a list to record per-phase CUDA events
         self.timing_side = []
         self._hp = None  # high-priority stream of the split force pass
@@ -400,10 +397,9 @@ class SlabRun:
     def _step_overlapped(self) -> None:
         """The step with both exchange rounds off the critical path.
 
-        main stream:  density -> prepare (gather, zone lists) -> interior
-                      force, head -> [wait for the ghost densities] ->
-                      boundary force -> interior force, tail -> [wait
-                      payload] finish round 1
+        main stream:  density -> prepare (gather, zone lists) -> [wait for
+                      the ghost densities] -> boundary force -> interior
+                      force -> [wait payload] finish round 1
         side stream (high priority): density round (beside the prepare
                       step), then, once the boundary force is done, round 1
                       begin (selection, counts) and the payload (enqueued by
@@ -429,9 +425,6 @@ class SlabRun:
                 self.comm.exchange_rho(rho)
         self.backend.force_step(cols6, rho, n, n_own, zone=(3,) + zones)
         self._mark("prepare")
-        # the interior's head needs no ghost densities: it runs while they travel
-        self.backend.force_step(cols6, rho, n, n_own, zone=(4,) + zones + (self.interior_head,))
-        self._mark("interior_head")
         main.wait_stream(self._hp)  # the ghosts' exact densities
         self.backend.force_step(cols6, rho, n, n_own, zone=(1,) + zones)
         self._mark("boundary")
@@ -439,7 +432,7 @@ class SlabRun:
         with torch.cuda.stream(self._hp):
             self.comm.exchange_begin()
             self._mark_side("counts_done")
-        self.backend.force_step(cols6, rho, n, n_own, zone=(5,) + zones + (self.interior_head,))
+        self.backend.force_step(cols6, rho, n, n_own, zone=(2,) + zones)
         self._mark("force")
         self.comm.exchange_end()  # the main stream waits for the payload
         with torch.cuda.stream(self._hp):

@@ -327,14 +327,8 @@ FORGE_API int forge_sph_force_step(forge_grid* g, const forge_sph_params* p, con
  *                        the ghosts' densities, i >= n_update, which may
  *                        have arrived since);
  *   FORGE_ZONE_INTERIOR  update the interior particles (needs a prepare or
- *                        boundary call before it);
- *   FORGE_ZONE_INTERIOR_HEAD / _TAIL  the same for the first `split` of the
- *                        interior list (0: one half) / the rest, so one part
- *                        can run before the ghost densities arrive and the
- *                        other beside the exchange that follows the boundary
- *                        pass.
- * BOUNDARY + INTERIOR (or + INTERIOR_HEAD + INTERIOR_TAIL, same split)
- * equal one forge_sph_force_step bit for bit. Each zone
+ *                        boundary call before it).
+ * BOUNDARY + INTERIOR equal one forge_sph_force_step bit for bit. Each zone
  * call waits, on its own stream, only for the prepare step, so the two
  * zones' kernels may run concurrently on two streams; interior particles
  * have no ghost neighbours, so the interior pass may also run before the
@@ -348,13 +342,10 @@ FORGE_API int forge_sph_force_step(forge_grid* g, const forge_sph_params* p, con
 #define FORGE_ZONE_BOUNDARY 1u
 #define FORGE_ZONE_INTERIOR 2u
 #define FORGE_ZONE_PREPARE 3u
-#define FORGE_ZONE_INTERIOR_HEAD 4u
-#define FORGE_ZONE_INTERIOR_TAIL 5u
 typedef struct forge_force_zone {
     uint32_t mode;
     float inner_lo, inner_hi;
     float guard_lo, guard_hi;
-    float split; /* INTERIOR_HEAD/_TAIL: fraction of the interior list in the head (0: 0.5) */
 } forge_force_zone;
 
 FORGE_API int forge_sph_force_step_zone(forge_grid* g, const forge_sph_params* p, const forge_step_params* sp,
