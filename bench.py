@@ -39,7 +39,7 @@ import workloads  # noqa: E402
 # traffic grows with the particle count, so it is quoted per particle).
 # bench.py cannot read DRAM counters itself; the figure is refreshed with each
 # capture of a changed kernel.
-NCU_TRAFFIC_B_PER_PARTICLE = {("sharded16m", "force"): 1131.2e6 / 16384000}
+NCU_TRAFFIC_B_PER_PARTICLE = {("sharded16m", "force"): 1191.3e6 / 16384000}
 
 
 def peaks():
