@@ -159,11 +159,13 @@ void scratch_free(SortScratch& s) {
 template <class Src>
 int run_onesweep(const SortScratch& s, Src src, const uint32_t* keys0, const uint32_t* vals0, uint32_t* ka,
                  uint32_t* va, uint32_t* kb, uint32_t* vb, uint32_t n, uint32_t begin_bit, uint32_t end_bit,
-                 cudaStream_t st, int* where) {
+                 cudaStream_t st, int* where, bool meta_zeroed = false) {
     const uint32_t passes = (end_bit - begin_bit + radix::kRadixBits - 1) / radix::kRadixBits;
     const bool small = n <= radix::kSmallN && s.max_tiles >= radix::num_tiles(n, radix::kSmallTile);
     const uint32_t tiles = small ? radix::num_tiles(n, radix::kSmallTile) : radix::num_tiles(n);
-    FORGE_CUDA(cudaMemsetAsync(s.meta, 0, kMetaErr * sizeof(uint32_t), st));
+    // histograms and tile counters start at zero (meta_zeroed: the caller's
+    // previous use left them so)
+    if (!meta_zeroed) FORGE_CUDA(cudaMemsetAsync(s.meta, 0, kMetaErr * sizeof(uint32_t), st));
     const uint32_t status_vec4 = (uint32_t)(((size_t)tiles * radix::kRadix + 3) / 4);
     const uint32_t hblocks =
         std::max(1u, std::min(grid_blocks(n, radix::kHistThreads * radix::kHistItems), (uint32_t)s.sms * 8u));
@@ -627,7 +629,7 @@ int grid_build_impl(forge_grid* g, const float* px, const float* py, const float
         grid::HashKeys src{px, py, pz, stride, g->geom, keys, sub_bits};
         int where = 0;
         int rc = run_onesweep(g->scratch, src, keys, nullptr, g->kb, g->vb, g->kc, g->vc, nn, 0,
-                              key_bits_w(g) + sub_bits, st, &where);
+                              key_bits_w(g) + sub_bits, st, &where, true);
         if (rc != FORGE_OK) return rc;
         g->sorted_keys = where == 0 ? g->kb : g->kc;
         g->sorted_idx = where == 0 ? g->vb : g->vc;
@@ -640,7 +642,7 @@ int grid_build_impl(forge_grid* g, const float* px, const float* py, const float
     const uint32_t table = cells_w(g) << sub_bits;  // entries [0, table]
     launch_pdl(grid::cell_start_gather_kernel, grid_blocks(n + 1, 256), 256, st,
         g->sorted_keys, g->sorted_idx, nn, table, g->cell_start, gs, gather_pos ? g->pos4 : nullptr,
-        (gather_pos && vx) ? g->vel4 : nullptr, g->chunk_val);
+        (gather_pos && vx) ? g->vel4 : nullptr, g->chunk_val, g->scratch.meta, (uint32_t)kMetaErr);
     const uint32_t chunks = table / grid::kFillChunk;  // whole chunks below entry `table`
     if (chunks)
         launch_pdl(grid::fill_chunks_kernel, std::min(chunks, (uint32_t)g->scratch.sms * 8u), 256, st, g->cell_start,

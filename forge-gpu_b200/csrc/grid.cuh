@@ -129,6 +129,7 @@ __device__ __forceinline__ void warp_fill_runs(uint32_t* __restrict__ table, int
 // fill_chunks_kernel, which writes them one block per chunk. Entries are
 // written once, except that whole chunks of a run may be written twice with
 // the same value; the table needs no clearing.
+// Also zeroes the sort's histograms and tile counters for the next build.
 // Optionally gathers positions (and velocities) into cell order:
 //   pos4[s] = (x, y, z, bits(key)), vel4[s] = (vx, vy, vz, 0).
 struct GatherSrc {
@@ -147,8 +148,13 @@ constexpr uint32_t kChunkFree = 0xffffffffu;  // chunk_val: not marked
 __global__ void __launch_bounds__(256)
     cell_start_gather_kernel(const uint32_t* __restrict__ skeys, const uint32_t* __restrict__ svals,
                              uint32_t n, uint32_t C, uint32_t* __restrict__ cell_start, GatherSrc src,
-                             float4* __restrict__ pos4, float4* __restrict__ vel4, uint32_t* __restrict__ chunk_val) {
+                             float4* __restrict__ pos4, float4* __restrict__ vel4, uint32_t* __restrict__ chunk_val,
+                             uint32_t* __restrict__ sort_meta, uint32_t sort_meta_words) {
     pdl_enter();
+    // the build's sort is done with its digit histograms and tile counters:
+    // zero them for the next build's sort (no memset node between builds)
+    if (blockIdx.x == 0)
+        for (uint32_t j = threadIdx.x; j < sort_meta_words; j += blockDim.x) sort_meta[j] = 0u;
     const uint32_t s = blockIdx.x * blockDim.x + threadIdx.x;
     int64_t a = 1, b = 0;  // empty
     uint32_t key = 0;
