@@ -92,3 +92,22 @@ def test_sharded_entry_points_reject_bad_arguments_without_gpu():
     assert L.forge_slab_exchange_end(None, None, 0, ctypes.byref(n_own), ctypes.byref(ng), None) == bad
     assert L.forge_slab_exchange_rho(None, None, None) == bad
     assert L.forge_slab_comm_create(None, 0, 1, 0, 16, 0.0, 1.0, 0.1, None) == bad
+
+
+def header_defines(prefix):
+    txt = open(os.path.join(ROOT, "include", "forge_sph.h")).read()
+    return {m.group(1): int(m.group(2)) for m in re.finditer(r"^#define (" + prefix + r"\w+)\s+(\d+)u?\b", txt,
+                                                                 flags=re.M)}
+
+
+def test_walk_and_zone_constants_match_header():
+    """The neighbour-pass families and force-zone modes the Python mirror and
+    bench.py pass through the C ABI are the header's values."""
+    import bench
+    walks = header_defines("FORGE_WALK_")
+    assert walks, "no FORGE_WALK_* in the header"
+    for name, v in walks.items():
+        assert getattr(forge_sph, name[len("FORGE_"):]) == v, name
+    assert set(bench.WALKS.values()) == set(walks.values())
+    zones = header_defines("FORGE_ZONE_")
+    assert zones == {"FORGE_ZONE_BOUNDARY": 1, "FORGE_ZONE_INTERIOR": 2, "FORGE_ZONE_PREPARE": 3}
