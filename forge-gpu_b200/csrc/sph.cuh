@@ -397,7 +397,8 @@ __global__ void __launch_bounds__(256)
 
 // ---------------------------------------------------------------------------
 // Force pass. TERMS: 1 pressure, 2 viscosity, 3 both (fused). Jacobi: all
-// neighbour data come from the cell-ordered snapshot (pos4, vel4, aux), so
+// neighbour data come from the cell-ordered snapshot (pos4 with p/rho in w,
+// vel4 with 1/rho in w; aux holds each particle's own rho), so
 // the update never races with reads (fixes the in-place vx[i] += of
 // sph_fused.rs:635-637 / sph_viscosity.rs:103-105).
 //
